@@ -1,0 +1,576 @@
+"""CPU oracle for the screened density-fitted Coulomb (RI-J) path — TEST INFRASTRUCTURE ONLY.
+
+This module is the checker, never the product: only ``tests/``, ``__graft_entry__.smoke()`` and the
+``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it. The product path
+(``gs_dft_b200``) runs the CUDA kernels and fails loudly when they are missing.
+
+It is a NumPy FP64 restatement of the reference (andresguzco/gs-dft) algorithm. Each function cites
+the reference file:line it follows. Parity pin: the restatement is checked against golden vectors
+produced by executing the reference's own source files under a NumPy stand-in for the JAX API
+(``tests/golden/make_golden.py``); the gradient, which the reference obtains by JAX autodiff, is
+checked against central finite differences of that executed reference energy and, for the node
+reverse pass, against the reference's hand-written ``nodes_bwd`` (gs_dft/coulomb/ri.py:190-222).
+
+Third-party arithmetic: the reference takes Boys F0 from ``dftax.energy.boys`` (dftax 0.8.0, not
+in the reference tree; used only in the aux metric, gs_dft/coulomb/ri.py:35,72-74). Here
+F0(T) = 1/2 sqrt(pi/T) erf(sqrt(T)) with its Taylor series at small T, the closed form the
+reference's own tests use (tests/unit/test_coulomb_stream.py:115-134). The metric V is therefore
+pinned to that closed form, not to dftax's table.
+
+One deliberate, documented deviation: the pair overlap used for screening is evaluated once per
+unordered pair, in the orientation (min(i,j), max(i,j)), and shared by (i,j) and (j,i). The
+reference evaluates both orientations; they agree to the last bit or two. This keeps the ordered
+list exactly symmetric and makes the overflow ranking's tie order well defined.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+from scipy.special import erf
+
+PI = math.pi
+
+# ----------------------------------------------------------------------------------------------
+#  Laplace half-line node table  (gs_dft/integrals/dense.py:46-53, 77-82)
+# ----------------------------------------------------------------------------------------------
+
+
+def gauss_legendre_halfline(n_quad: int = 20):
+    """t = s/(1-s) map of Gauss-Legendre on [0,1) (gs_dft/integrals/dense.py:46-53)."""
+    x, w = np.polynomial.legendre.leggauss(n_quad)
+    s = (x + 1.0) / 2.0
+    w_s = w / 2.0
+    t = s / (1.0 - s)
+    jac = 1.0 / (1.0 - s) ** 2
+    return np.asarray(t, np.float64), np.asarray(w_s * jac, np.float64)
+
+
+QUAD_T, QUAD_W = gauss_legendre_halfline(20)
+
+# ----------------------------------------------------------------------------------------------
+#  Splat chart  (gs_dft/basis/spectral.py:33-40, 71-82)
+# ----------------------------------------------------------------------------------------------
+
+
+def quat_to_rotation(q):
+    """gs_dft/basis/spectral.py:33-40 — normalise with +1e-12, then the Hamilton matrix."""
+    n = np.sqrt(np.sum(q * q, axis=-1, keepdims=True))
+    q = q / (n + 1e-12)
+    w, x, y, z = q[..., 0], q[..., 1], q[..., 2], q[..., 3]
+    r0 = np.stack([1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y)], -1)
+    r1 = np.stack([2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x)], -1)
+    r2 = np.stack([2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)], -1)
+    return np.stack([r0, r1, r2], -2)
+
+
+def splat_A(quat, log_scale):
+    """A = R diag(exp l) R^T (gs_dft/basis/spectral.py:71-76); entry (i,k) summed j = 0,1,2."""
+    R = quat_to_rotation(quat)
+    a = np.exp(log_scale)
+    A = np.empty(R.shape)
+    for i in range(3):
+        for k in range(3):
+            A[:, i, k] = ((R[:, i, 0] * a[:, 0]) * R[:, k, 0] + (R[:, i, 1] * a[:, 1]) * R[:, k, 1]
+                          + (R[:, i, 2] * a[:, 2]) * R[:, k, 2])
+    return A
+
+
+def splat_norm(log_scale):
+    """N = (8 det A / pi^3)^(1/4), det A = exp(sum l) (gs_dft/basis/spectral.py:78-82)."""
+    detA = np.exp(np.sum(log_scale, axis=-1))
+    return (8.0 * detA / PI ** 3) ** 0.25
+
+
+def full_quantities(quat, log_scale, centers):
+    """(A, mu, N) once per call (gs_dft/coulomb/stream.py:79-81)."""
+    return splat_A(quat, log_scale), np.asarray(centers, np.float64), splat_norm(log_scale)
+
+# ----------------------------------------------------------------------------------------------
+#  Closed-form 3x3 algebra  (gs_dft/integrals/linalg3.py:17-51)
+# ----------------------------------------------------------------------------------------------
+
+
+def det3(A):
+    """Cofactor expansion along the first row (gs_dft/integrals/linalg3.py:17-23)."""
+    return (A[..., 0, 0] * (A[..., 1, 1] * A[..., 2, 2] - A[..., 1, 2] * A[..., 2, 1])
+            - A[..., 0, 1] * (A[..., 1, 0] * A[..., 2, 2] - A[..., 1, 2] * A[..., 2, 0])
+            + A[..., 0, 2] * (A[..., 1, 0] * A[..., 2, 1] - A[..., 1, 1] * A[..., 2, 0]))
+
+
+def adj3(A):
+    """Adjugate (gs_dft/integrals/linalg3.py:26-41)."""
+    c00 = A[..., 1, 1] * A[..., 2, 2] - A[..., 1, 2] * A[..., 2, 1]
+    c01 = A[..., 0, 2] * A[..., 2, 1] - A[..., 0, 1] * A[..., 2, 2]
+    c02 = A[..., 0, 1] * A[..., 1, 2] - A[..., 0, 2] * A[..., 1, 1]
+    c10 = A[..., 1, 2] * A[..., 2, 0] - A[..., 1, 0] * A[..., 2, 2]
+    c11 = A[..., 0, 0] * A[..., 2, 2] - A[..., 0, 2] * A[..., 2, 0]
+    c12 = A[..., 0, 2] * A[..., 1, 0] - A[..., 0, 0] * A[..., 1, 2]
+    c20 = A[..., 1, 0] * A[..., 2, 1] - A[..., 1, 1] * A[..., 2, 0]
+    c21 = A[..., 0, 1] * A[..., 2, 0] - A[..., 0, 0] * A[..., 2, 1]
+    c22 = A[..., 0, 0] * A[..., 1, 1] - A[..., 0, 1] * A[..., 1, 0]
+    return np.stack([np.stack([c00, c01, c02], -1), np.stack([c10, c11, c12], -1),
+                     np.stack([c20, c21, c22], -1)], -2)
+
+
+def matvec3(A, b):
+    """sum_l A[k,l] b[l], l summed left to right."""
+    return np.stack([A[..., k, 0] * b[..., 0] + A[..., k, 1] * b[..., 1] + A[..., k, 2] * b[..., 2]
+                     for k in range(3)], -1)
+
+
+def solve3(A, b):
+    """adj(A) b / det(A) (gs_dft/integrals/linalg3.py:49-51)."""
+    return matvec3(adj3(A), b) / det3(A)[..., None]
+
+# ----------------------------------------------------------------------------------------------
+#  Pair quantities and overlap  (gs_dft/coulomb/stream.py:203-215; gs_dft/screening/pairs.py:342-345)
+# ----------------------------------------------------------------------------------------------
+
+
+def full_pair_quantities(q, pi, pj):
+    """A_hat = A_i + A_j, P = A_hat^-1 (A_i mu_i + A_j mu_j), KN = N_i N_j exp(-d.A_i A_hat^-1 A_j d)
+    (gs_dft/coulomb/stream.py:203-215)."""
+    A, mu, N = q
+    Ai, Aj = A[pi], A[pj]
+    mui, muj = mu[pi], mu[pj]
+    Aij = Ai + Aj
+    rhs = matvec3(Ai, mui) + matvec3(Aj, muj)
+    Pa = solve3(Aij, rhs)
+    d = mui - muj
+    Ajd = matvec3(Aj, d)
+    AiAinvAjd = matvec3(Ai, solve3(Aij, Ajd))
+    K = np.exp(-(d[..., 0] * AiAinvAjd[..., 0] + d[..., 1] * AiAinvAjd[..., 1]
+                 + d[..., 2] * AiAinvAjd[..., 2]))
+    return Aij, Pa, N[pi] * N[pj] * K
+
+
+def overlap_pairs(q, pi, pj):
+    """S_ij = KN pi^1.5 / sqrt(det A_hat) (gs_dft/screening/pairs.py:342-345)."""
+    Aij, _, NK = full_pair_quantities(q, pi, pj)
+    return NK * PI ** 1.5 / np.sqrt(det3(Aij))
+
+
+def canonical_abs_overlap(q, pi, pj):
+    """|S| evaluated in the (min, max) orientation, shared by (i,j) and (j,i)."""
+    lo = np.minimum(pi, pj)
+    hi = np.maximum(pi, pj)
+    return np.abs(overlap_pairs(q, lo, hi))
+
+# ----------------------------------------------------------------------------------------------
+#  Significant-pair list  (gs_dft/screening/pairs.py:50-164, 225-322)
+# ----------------------------------------------------------------------------------------------
+
+
+def pair_weights(pi, pj, unique):
+    """bool mask, or (2 - delta_ij) weights when unique (gs_dft/screening/pairs.py:318-322)."""
+    if not unique:
+        return np.ones(pi.shape[0], bool)
+    return np.where(pi == pj, 1.0, 2.0)
+
+
+def _significant_flat(q, M, eps, unique, row_chunk=256):
+    """Ascending flat indices i*M+j with |S_ij| > eps, plus their |S| (pairs.py:50-87,103-118)."""
+    flats, vals = [], []
+    for a in range(0, M, row_chunk):
+        rows = np.arange(a, min(a + row_chunk, M))
+        pi = np.repeat(rows, M)
+        pj = np.tile(np.arange(M), rows.size)
+        s = canonical_abs_overlap(q, pi, pj)
+        sig = s > eps
+        if unique:
+            sig &= pj >= pi
+        flats.append(pi[sig].astype(np.int64) * M + pj[sig])
+        vals.append(s[sig])
+    return np.concatenate(flats), np.concatenate(vals)
+
+
+def count_significant(q, M, eps, unique):
+    """_count_significant (gs_dft/screening/pairs.py:103-118)."""
+    return int(_significant_flat(q, M, eps, unique)[0].size)
+
+
+def _decode(flat, M, pad_to, unique):
+    """_decode_flat (gs_dft/screening/pairs.py:90-100): tail-padded with (0,0), weight 0."""
+    pi = (flat // M).astype(np.int32)
+    pj = (flat % M).astype(np.int32)
+    valid = pair_weights(pi, pj, unique)
+    k = pi.size
+    if pad_to is not None and pad_to > k:
+        z = np.zeros(pad_to - k, np.int32)
+        pi = np.concatenate([pi, z])
+        pj = np.concatenate([pj, z])
+        valid = np.concatenate([valid, np.zeros(pad_to - k, valid.dtype)])
+    return pi, pj, valid
+
+
+def neighbor_pairs(q, eps=1e-5, pad_to=None, unique=False, headroom=2):
+    """Significant ordered pairs, lexsorted, tail-padded; overflow keeps the ``pad_to`` largest |S|
+    (ties by ascending flat index), re-lexsorted (gs_dft/screening/pairs.py:225-315, 155-164).
+    Returns (pi, pj, valid, n_sig)."""
+    M = int(q[1].shape[0])
+    n_all = M * (M + 1) // 2 if unique else M * M
+    if eps < 0.0 and (pad_to is None or pad_to >= n_all):
+        if unique:
+            pi, pj = np.triu_indices(M)
+        else:
+            pi = np.repeat(np.arange(M), M)
+            pj = np.tile(np.arange(M), M)
+        flat = pi.astype(np.int64) * M + pj
+        out = _decode(flat, M, pad_to, unique)
+        return (*out, n_all)
+    flat, vals = _significant_flat(q, M, eps, unique)
+    n_sig = int(flat.size)
+    if pad_to is None:
+        return (*_decode(flat, M, None, unique), n_sig)
+    if n_sig <= pad_to:
+        return (*_decode(flat, M, pad_to, unique), n_sig)
+    if n_sig > headroom * pad_to:
+        raise ValueError(f"neighbor_pairs: {n_sig} significant pairs exceed {headroom}x the pad")
+    order = np.argsort(-vals, kind="stable")[:pad_to]
+    keep = np.sort(flat[order])
+    return (*_decode(keep, M, pad_to, unique), n_sig)
+
+
+def pad_rule(n0, pad, G):
+    """pad_to = ceil(pad * n0 / G) * G  (gs_dft/ks/train.py:356-359)."""
+    return -(-int(pad * n0) // G) * G
+
+
+def stripe_pairs(pi, pj, valid, G):
+    """Round-robin deal so every device block has the same valid:dummy ratio
+    (gs_dft/ks/shard.py:146-166)."""
+    n = pi.shape[0]
+    if G <= 1 or n % G:
+        return pi, pj, valid
+    f = lambda a: a.reshape(-1, G).T.reshape(-1)
+    return f(pi), f(pj), f(valid)
+
+# ----------------------------------------------------------------------------------------------
+#  Product auxiliary basis  (gs_dft/basis/isotropic.py:22-39, 81-116; gs_dft/coulomb/ri.py:238-240)
+# ----------------------------------------------------------------------------------------------
+
+
+def init_product_aux(q, scales=(1.0,), diagonal_only=True, pi=None, pj=None, valid=None):
+    """Frozen product aux: per kept pair, alpha0 = det(A_hat)^(1/3), centre = product centre;
+    log_alpha = log(alpha0*s) per scale (gs_dft/basis/isotropic.py:81-116). Returns (log_alpha, R)."""
+    M = q[1].shape[0]
+    if diagonal_only or pi is None:
+        pi = pj = np.arange(M)
+        valid = None
+    Aij, Pa, _ = full_pair_quantities(q, pi, pj)
+    alpha0 = det3(Aij) ** (1.0 / 3.0)
+    if valid is not None:
+        alpha0 = np.where(valid, alpha0, 1.0)
+    log_alpha = np.concatenate([np.log(alpha0 * float(s)) for s in scales])
+    R = np.concatenate([Pa for _ in scales], axis=0)
+    return log_alpha, R
+
+
+def aux_quantities(log_alpha, R):
+    """(beta, R, norm): alpha = exp(log_alpha), norm = (2 alpha/pi)^(3/4)
+    (gs_dft/basis/isotropic.py:30-39; gs_dft/coulomb/ri.py:238-240)."""
+    alpha = np.exp(log_alpha)
+    return alpha, R, (2.0 * alpha / PI) ** 0.75
+
+# ----------------------------------------------------------------------------------------------
+#  Aux metric, factor, solve  (gs_dft/coulomb/ri.py:63-123, 243-275, 472-482)
+# ----------------------------------------------------------------------------------------------
+
+
+def boys0(T):
+    """F0(T) = 1/2 sqrt(pi/T) erf(sqrt T); Taylor 1 - T/3 + T^2/10 - T^3/42 below 1e-8."""
+    T = np.asarray(T, np.float64)
+    small = T < 1e-8
+    Ts = np.where(small, 1.0, T)
+    big = 0.5 * np.sqrt(PI / Ts) * erf(np.sqrt(Ts))
+    ser = 1.0 - T / 3.0 + T * T / 10.0 - T * T * T / 42.0
+    return np.where(small, ser, big)
+
+
+def coulomb_block(g1, P1, KN1, g2, P2, KN2):
+    """(1|2) = KN1 KN2 2 pi^2.5/(g1 g2 sqrt(g1+g2)) F0(g1g2/(g1+g2) |P1-P2|^2)
+    (gs_dft/coulomb/ri.py:63-76)."""
+    gab = g1[:, None] * g2[None, :]
+    gsum = g1[:, None] + g2[None, :]
+    dx = P1[:, None, :] - P2[None, :, :]
+    PQ2 = dx[..., 0] ** 2 + dx[..., 1] ** 2 + dx[..., 2] ** 2
+    rho = gab / gsum
+    T = rho * PQ2
+    coul = 2.0 * PI ** 2.5 / (gab * np.sqrt(gsum)) * boys0(T)
+    return (KN1[:, None] * KN2[None, :]) * coul
+
+
+def aux_metric(beta, R, KN):
+    """V_PQ = (P|Q) (gs_dft/coulomb/ri.py:267-275)."""
+    return coulomb_block(beta, R, KN, beta, R, KN)
+
+
+def aux_cholesky(V, lam):
+    """Lower Cholesky of V + lam I (gs_dft/coulomb/ri.py:243-264)."""
+    Vs = V.copy()
+    Vs[np.diag_indices_from(Vs)] += lam
+    return np.linalg.cholesky(Vs)
+
+
+def df_coulomb_solve(gamma, L):
+    """d = cho_solve((L, lower), gamma); E_J = 1/2 gamma.d (gs_dft/coulomb/ri.py:472-482)."""
+    from scipy.linalg import cho_solve
+    d = cho_solve((L, True), gamma)
+    return 0.5 * float(np.dot(gamma, d)), d
+
+# ----------------------------------------------------------------------------------------------
+#  3-centre (aux | pair) block  (gs_dft/coulomb/ri.py:126-185)
+# ----------------------------------------------------------------------------------------------
+
+PREF = 2.0 * PI ** 3 / math.sqrt(PI)
+
+
+def isobra_nodes(beta, dp2, Lam):
+    """sum_t w_t (G0G1G2)^-1/2 exp(-t^2 sum_k W_k/G_k) in the division-lean form
+    (gs_dft/coulomb/ri.py:167-185). beta (A,), dp2 (A,B,3), Lam (B,3) -> (A,B)."""
+    b = beta[:, None]
+    L0, L1, L2 = Lam[None, :, 0], Lam[None, :, 1], Lam[None, :, 2]
+    coul = np.zeros((beta.shape[0], Lam.shape[0]))
+    for t, w in zip(QUAD_T, QUAD_W):
+        t2 = t * t
+        G0 = b * L0 + t2 * (b + L0)
+        G1 = b * L1 + t2 * (b + L1)
+        G2 = b * L2 + t2 * (b + L2)
+        invp = 1.0 / (G0 * G1 * G2)
+        num = b * (L0 * dp2[..., 0] * G1 * G2 + L1 * dp2[..., 1] * G0 * G2
+                   + L2 * dp2[..., 2] * G0 * G1)
+        coul = coul + w * np.sqrt(invp) * np.exp(-t2 * num * invp)
+    return coul
+
+
+def isobra_nodes_bwd(beta, dp2, Lam, gI):
+    """The reference's analytic reverse of the node sum (gs_dft/coulomb/ri.py:190-222):
+    returns (d_beta, d_dp2 (A,B,3), d_Lam (B,3))."""
+    b = beta[:, None]
+    Ls = (Lam[None, :, 0], Lam[None, :, 1], Lam[None, :, 2])
+    d_beta = np.zeros_like(b)
+    d_Lam = [np.zeros((1, Lam.shape[0])) for _ in range(3)]
+    d_dp2 = [np.zeros((beta.shape[0], Lam.shape[0])) for _ in range(3)]
+    for t, w in zip(QUAD_T, QUAD_W):
+        t2 = t * t
+        G = [b * L + t2 * (b + L) for L in Ls]
+        invG = [1.0 / Gk for Gk in G]
+        W = [b * L * dp2[..., k] for k, L in enumerate(Ls)]
+        S = W[0] * invG[0] + W[1] * invG[1] + W[2] * invG[2]
+        I = w * np.sqrt(invG[0] * invG[1] * invG[2]) * np.exp(-t2 * S)
+        gIt = gI * I
+        db = np.zeros_like(gIt)
+        for k, L in enumerate(Ls):
+            dIdG = gIt * (t2 * W[k] * invG[k] - 0.5) * invG[k]
+            dIdW = -gIt * t2 * invG[k]
+            db = db + dIdG * (L + t2) + dIdW * L * dp2[..., k]
+            d_Lam[k] = d_Lam[k] + np.sum(dIdG * (b + t2) + dIdW * b * dp2[..., k], axis=0,
+                                         keepdims=True)
+            d_dp2[k] = d_dp2[k] + dIdW * b * L
+        d_beta = d_beta + np.sum(db, axis=1, keepdims=True)
+    return d_beta[:, 0], np.stack(d_dp2, -1), np.stack([dL[0] for dL in d_Lam], -1)
+
+
+def full_isobra_block(beta, R, KN_aux, A_pair, P_pair, KN_pair):
+    """(P|a): eigh of A_hat, dp2 = (U^T (R - P))^2, node sum, prefactor
+    (gs_dft/coulomb/ri.py:126-151). Returns (N_aux, n_pair)."""
+    Lam, U = np.linalg.eigh(A_pair)
+    d = R[:, None, :] - P_pair[None, :, :]
+    dp2 = np.einsum("bki,abk->abi", U, d) ** 2
+    coul = isobra_nodes(beta, dp2, Lam)
+    return (KN_aux[:, None] * KN_pair[None, :]) * PREF * coul
+
+# ----------------------------------------------------------------------------------------------
+#  Screened gamma stream and energy  (gs_dft/coulomb/ri.py:436-494)
+# ----------------------------------------------------------------------------------------------
+
+
+def pair_density(C_occ, occ, pi, pj, valid):
+    """q_a = valid_a * sum_o occ_o C_io C_jo (gs_dft/coulomb/ri.py:456)."""
+    return np.asarray(valid, np.float64) * np.sum(occ[None, :] * C_occ[pi] * C_occ[pj], axis=1)
+
+
+def df_coulomb_gamma_screened(q_splat, C_occ, occ, aux_q, pi, pj, valid, chunk=2048):
+    """gamma_P = sum_a (P|a) q_a over the pair list, chunked (gs_dft/coulomb/ri.py:436-469)."""
+    beta, R, KN = aux_q
+    gamma = np.zeros(beta.shape[0])
+    for a in range(0, pi.shape[0], chunk):
+        ci, cj, cv = pi[a:a + chunk], pj[a:a + chunk], valid[a:a + chunk]
+        qa = pair_density(C_occ, occ, ci, cj, cv)
+        blk = full_isobra_block(beta, R, KN, *full_pair_quantities(q_splat, ci, cj))
+        gamma = gamma + blk @ qa
+    return gamma
+
+
+def energy(sys_arrays, aux_q, L, pi, pj, valid, chunk=2048):
+    """E_J^DF = 1/2 gamma^T (V + lam I)^-1 gamma (gs_dft/coulomb/ri.py:485-494).
+    ``sys_arrays`` = (quat, log_scale, centers, C_occ, occ). Returns (E, gamma, d)."""
+    quat, log_scale, centers, C_occ, occ = sys_arrays
+    q = full_quantities(quat, log_scale, centers)
+    gamma = df_coulomb_gamma_screened(q, C_occ, occ, aux_q, pi, pj, valid, chunk)
+    E, d = df_coulomb_solve(gamma, L)
+    return E, gamma, d
+
+# ----------------------------------------------------------------------------------------------
+#  Analytic gradient (the reference obtains it by JAX autodiff through ri.py:126-185,
+#  stream.py:203-215 and spectral.py:33-82, with the node reverse of ri.py:190-222).
+# ----------------------------------------------------------------------------------------------
+
+
+def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa):
+    """For each pair: J_a = sum_P (P|a) d_P and the cotangents of (A_hat, P_a, KN_a) of
+    E = sum_P d_P sum_a (P|a) q_a, without the 1/(lambda_i - lambda_j) terms of an eigh VJP.
+
+    Per node, f = w det(G)^-1/2 exp(-t^2 beta d^T A_hat G^-1 d) with G = (beta+t^2) A_hat + t^2 beta I:
+      df/dA_hat = f (-1/2 (beta+t^2) G^-1 - t^4 beta^2 z z^T),  z = G^-1 d
+      df/dP     = f 2 t^2 beta A_hat z.
+    Evaluated in the eigenframe of A_hat (G and A_hat commute)."""
+    Lam, U = np.linalg.eigh(A_pair)                           # (B,3), (B,3,3)
+    dd = R[:, None, :] - P_pair[None, :, :]                   # (A,B,3)
+    y = np.einsum("bki,abk->abi", U, dd)                      # eigenframe displacement
+    b = beta[:, None]
+    coul = np.zeros(y.shape[:2])
+    Dk = np.zeros(y.shape)                                    # sum_t f s / G_k
+    Zkl = np.zeros(y.shape + (3,))                            # sum_t f t^4 beta^2 z_k z_l
+    Vk = np.zeros(y.shape)                                    # sum_t f t^2 beta lam_k z_k
+    for t, w in zip(QUAD_T, QUAD_W):
+        t2 = t * t
+        s = b + t2
+        G = b[..., None] * Lam[None] + t2 * (b[..., None] + Lam[None])   # (A,B,3)
+        invG = 1.0 / G
+        S = np.sum(b[..., None] * Lam[None] * y * y * invG, axis=-1)
+        f = w * np.sqrt(invG[..., 0] * invG[..., 1] * invG[..., 2]) * np.exp(-t2 * S)
+        coul += f
+        z = y * invG
+        Dk += (f * s)[..., None] * invG
+        Zkl += (f * t2 * t2 * b * b)[..., None, None] * z[..., :, None] * z[..., None, :]
+        Vk += (f * t2 * b)[..., None] * Lam[None] * z
+    c = dvec[:, None] * KN_aux[:, None] * (KN_pair * PREF)[None, :]   # d_P KN_P KN_a pref
+    J = np.sum(c * coul, axis=0)
+    cq = c * qa[None, :]
+    Mk = -0.5 * np.sum(cq[..., None] * Dk, axis=0)                     # (B,3) diagonal part
+    Mkl = -np.sum(cq[..., None, None] * Zkl, axis=0)                   # (B,3,3)
+    Mkl[:, [0, 1, 2], [0, 1, 2]] += Mk
+    Abar = np.einsum("bik,bkl,bjl->bij", U, Mkl, U)
+    Pbar_eig = 2.0 * np.sum(cq[..., None] * Vk, axis=0)                # (B,3) eigenframe
+    Pbar = np.einsum("bik,bk->bi", U, Pbar_eig)
+    KNbar = qa * np.sum(dvec[:, None] * KN_aux[:, None] * PREF * coul, axis=0)
+    return J, Abar, Pbar, KNbar
+
+
+def _pair_chain(q_splat, pi, pj, Abar_h, Pbar, KNbar):
+    """Cotangents of (A_hat, P, KN) -> (A_i, A_j, mu_i, mu_j, N_i, N_j)
+    (the reverse of gs_dft/coulomb/stream.py:203-215)."""
+    A, mu, N = q_splat
+    Ai, Aj, mui, muj = A[pi], A[pj], mu[pi], mu[pj]
+    Ah = Ai + Aj
+    Ahinv = np.linalg.inv(Ah)
+    b = np.einsum("pkl,pl->pk", Ai, mui) + np.einsum("pkl,pl->pk", Aj, muj)
+    P = np.einsum("pkl,pl->pk", Ahinv, b)
+    v = np.einsum("pkl,pl->pk", Ahinv, Pbar)
+    Ah_bar = Abar_h - v[:, :, None] * P[:, None, :]
+    gAi = Ah_bar + v[:, :, None] * mui[:, None, :]
+    gAj = Ah_bar + v[:, :, None] * muj[:, None, :]
+    gmui = np.einsum("plk,pl->pk", Ai, v)
+    gmuj = np.einsum("plk,pl->pk", Aj, v)
+    d = mui - muj
+    e = np.einsum("pkl,pl->pk", Ahinv, np.einsum("pkl,pl->pk", Aj, d))
+    f = d - e
+    Hd = np.einsum("pkl,pl->pk", Ai, e)                       # A_i A_hat^-1 A_j d
+    K = np.exp(-np.sum(d * Hd, axis=-1))
+    KN = N[pi] * N[pj] * K
+    gNi = KNbar * N[pj] * K
+    gNj = KNbar * N[pi] * K
+    Qbar = -KNbar * KN
+    gd = (2.0 * Qbar)[:, None] * Hd
+    gmui = gmui + gd
+    gmuj = gmuj - gd
+    gAi = gAi + Qbar[:, None, None] * e[:, :, None] * e[:, None, :]
+    gAj = gAj + Qbar[:, None, None] * f[:, :, None] * f[:, None, :]
+    return gAi, gAj, gmui, gmuj, gNi, gNj
+
+
+def chart_vjp(quat, log_scale, gA, gN):
+    """Reverse of the chart A = R(q) diag(e^l) R^T, N = (8 e^(sum l)/pi^3)^(1/4)
+    (gs_dft/basis/spectral.py:33-40, 71-82). gA may be non-symmetric; only its symmetric part acts."""
+    gS = 0.5 * (gA + np.swapaxes(gA, -1, -2))
+    R = quat_to_rotation(quat)
+    a = np.exp(log_scale)
+    N = splat_norm(log_scale)
+    RtgR = np.einsum("mik,mij,mjl->mkl", R, gS, R)
+    g_log = a * np.stack([RtgR[:, k, k] for k in range(3)], -1) + (gN * N / 4.0)[:, None]
+    gR = 2.0 * np.einsum("mij,mjk->mik", gS, R) * a[:, None, :]
+    n = np.sqrt(np.sum(quat * quat, axis=-1))
+    qh = quat / (n + 1e-12)[:, None]
+    w, x, y, z = qh[:, 0], qh[:, 1], qh[:, 2], qh[:, 3]
+    g = gR
+    gw = 2 * (-z * g[:, 0, 1] + y * g[:, 0, 2] + z * g[:, 1, 0] - x * g[:, 1, 2]
+              - y * g[:, 2, 0] + x * g[:, 2, 1])
+    gx = 2 * (y * g[:, 0, 1] + z * g[:, 0, 2] + y * g[:, 1, 0] - 2 * x * g[:, 1, 1]
+              - w * g[:, 1, 2] + z * g[:, 2, 0] + w * g[:, 2, 1] - 2 * x * g[:, 2, 2])
+    gy = 2 * (-2 * y * g[:, 0, 0] + x * g[:, 0, 1] + w * g[:, 0, 2] + x * g[:, 1, 0]
+              + z * g[:, 1, 2] - w * g[:, 2, 0] + z * g[:, 2, 1] - 2 * y * g[:, 2, 2])
+    gz = 2 * (-2 * z * g[:, 0, 0] - w * g[:, 0, 1] + x * g[:, 0, 2] + w * g[:, 1, 0]
+              - 2 * z * g[:, 1, 1] + y * g[:, 1, 2] + x * g[:, 2, 0] + y * g[:, 2, 1])
+    gqh = np.stack([gw, gx, gy, gz], -1)
+    dot = np.sum(quat * gqh, axis=-1)
+    g_quat = gqh / (n + 1e-12)[:, None] - quat * (dot / (np.maximum(n, 1e-300) * (n + 1e-12) ** 2))[:, None]
+    return g_quat, g_log
+
+
+def energy_and_grad(sys_arrays, aux_q, L, pi, pj, valid, chunk=1024):
+    """E_J, gamma, d, J (per listed pair; 0 on zero-weight entries) and the gradient of E_J with
+    respect to (quat, log_scale, centers, C_occ), aux and pair list frozen."""
+    quat, log_scale, centers, C_occ, occ = sys_arrays
+    qs = full_quantities(quat, log_scale, centers)
+    E, gamma, dvec = energy(sys_arrays, aux_q, L, pi, pj, valid, chunk)
+    beta, R, KN_aux = aux_q
+    M = centers.shape[0]
+    n = pi.shape[0]
+    J = np.zeros(n)
+    gA = np.zeros((M, 3, 3))
+    gmu = np.zeros((M, 3))
+    gN = np.zeros(M)
+    gC = np.zeros_like(C_occ)
+    w = np.asarray(valid, np.float64)
+    for a in range(0, n, chunk):
+        sl = slice(a, a + chunk)
+        ci, cj, cw = pi[sl], pj[sl], w[sl]
+        live = cw != 0
+        if not np.any(live):
+            continue
+        ci, cj, cw = ci[live], cj[live], cw[live]
+        qa = pair_density(C_occ, occ, ci, cj, cw)
+        Ah, Pa, KNa = full_pair_quantities(qs, ci, cj)
+        Jc, Abar, Pbar, KNbar = _pair_vjp_integral(beta, R, KN_aux, dvec, Ah, Pa, KNa, qa)
+        J[np.arange(a, min(a + chunk, n))[live]] = Jc
+        gAi, gAj, gmui, gmuj, gNi, gNj = _pair_chain(qs, ci, cj, Abar, Pbar, KNbar)
+        np.add.at(gA, ci, gAi)
+        np.add.at(gA, cj, gAj)
+        np.add.at(gmu, ci, gmui)
+        np.add.at(gmu, cj, gmuj)
+        np.add.at(gN, ci, gNi)
+        np.add.at(gN, cj, gNj)
+        s = (Jc * cw)[:, None] * occ[None, :]
+        np.add.at(gC, ci, s * C_occ[cj])
+        np.add.at(gC, cj, s * C_occ[ci])
+    g_quat, g_log = chart_vjp(quat, log_scale, gA, gN)
+    return dict(E=E, gamma=gamma, d=dvec, J=J, g_quat=g_quat, g_log_scale=g_log,
+                g_centers=gmu, g_C=gC, gA=gA, gmu=gmu, gN=gN)
+
+# ----------------------------------------------------------------------------------------------
+#  Convenience: a full refresh + step for one system
+# ----------------------------------------------------------------------------------------------
+
+
+def refresh(quat, log_scale, centers, eps, lam, pad_to=None, unique=False, scales=(1.0,)):
+    """Pair list, product aux (diagonal), metric and its factor (gs_dft/ks/energy.py:454-473)."""
+    q = full_quantities(quat, log_scale, centers)
+    pi, pj, valid, n_sig = neighbor_pairs(q, eps=eps, pad_to=pad_to, unique=unique)
+    log_alpha, R = init_product_aux(q, scales=scales)
+    aux_q = aux_quantities(log_alpha, R)
+    V = aux_metric(*aux_q)
+    L = aux_cholesky(V, lam)
+    return dict(pi=pi, pj=pj, valid=valid, n_sig=n_sig, log_alpha=log_alpha, R=R,
+                aux_q=aux_q, V=V, L=L)

@@ -1,0 +1,145 @@
+"""Generate the golden vectors in this directory by EXECUTING THE REFERENCE'S OWN SOURCE.
+
+JAX is not installable here, so the reference modules (gs_dft/basis/spectral.py, isotropic.py,
+gs_dft/screening/pairs.py, gs_dft/coulomb/ri.py, stream.py, gs_dft/integrals/*.py) are imported
+unmodified from a checkout of andresguzco/gs-dft and run under ``jaxshim`` (a NumPy stand-in for the
+JAX API subset they use). Inputs are the seeded synthetic systems of ``gs_dft_b200.systems``.
+
+Run from the repository root, with the reference checkout at ``jaxshim.REFERENCE_ROOT``:
+
+    python tests/golden/make_golden.py
+
+Outputs (compressed .npz, a few hundred KB in all):
+  * ``ref_<case>.npz``  — chart (A, N), pair lists in every mode, product aux, metric, factor,
+    gamma, E_J and d for three systems;
+  * ``ref_grad.npz``    — the gradient of E_J w.r.t. (quat, log_scale, centers, C_occ) by
+    Richardson-extrapolated central differences of the executed reference energy (pair list,
+    aux and factor frozen, as in training);
+  * ``ref_nodes_bwd.npz`` — the reference's hand-written node reverse pass on one block.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, HERE)
+sys.path.insert(0, os.path.join(ROOT, "gs-dft_b200"))
+
+import jaxshim  # noqa: E402
+from gs_dft_b200.systems import make_config, small_random_system  # noqa: E402
+
+J = jaxshim.as_jarr
+
+
+def _modules():
+    return (jaxshim.load("gs_dft.basis.spectral"), jaxshim.load("gs_dft.basis.isotropic"),
+            jaxshim.load("gs_dft.screening.pairs"), jaxshim.load("gs_dft.coulomb.ri"))
+
+
+def _cases():
+    return {
+        "rand24": small_random_system(24, 4, seed=0),
+        "rand48": small_random_system(48, 5, seed=1, spread=4.0, n_atoms=6),
+        "co2": make_config(0),
+    }
+
+
+def make_case(name, s, eps=1e-7, lam=1e-8):
+    spec, iso, pairs, ri = _modules()
+    sp = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+    out = dict(quat=s.quat, log_scale=s.log_scale, centers=s.centers, C_occ=s.C_occ, occ=s.occ,
+               eps=eps, lam=lam)
+    out["A"] = np.asarray(sp.A)
+    out["N"] = np.asarray(sp.norm)
+    M = s.M
+    pi, pj, v = pairs.neighbor_pairs(sp, eps=eps)
+    n = int(pi.shape[0])
+    out.update(ord_pi=np.asarray(pi), ord_pj=np.asarray(pj), ord_v=np.asarray(v))
+    pi2, pj2, v2 = pairs.neighbor_pairs(sp, eps=eps, pad_to=n + 37)
+    out.update(pad_pi=np.asarray(pi2), pad_pj=np.asarray(pj2), pad_v=np.asarray(v2))
+    pi3, pj3, v3 = pairs.neighbor_pairs(sp, eps=eps, pad_to=n // 2 + 1)
+    out.update(over_pi=np.asarray(pi3), over_pj=np.asarray(pj3), over_v=np.asarray(v3))
+    ui, uj, uw = pairs.neighbor_pairs(sp, eps=eps, unique=True)
+    nu = int(ui.shape[0])
+    out.update(uni_pi=np.asarray(ui), uni_pj=np.asarray(uj), uni_w=np.asarray(uw))
+    ui2, uj2, uw2 = pairs.neighbor_pairs(sp, eps=eps, unique=True, pad_to=nu // 2 + 3)
+    out.update(uover_pi=np.asarray(ui2), uover_pj=np.asarray(uj2), uover_w=np.asarray(uw2))
+    fi, fj, fv = pairs.neighbor_pairs(sp, eps=-1.0, pad_to=M * M + 11)
+    out.update(all_pi=np.asarray(fi), all_pj=np.asarray(fj), all_v=np.asarray(fv))
+    aux = iso.init_product_aux(sp)
+    out.update(aux_log_alpha=np.asarray(aux.log_alpha), aux_R=np.asarray(aux.centers))
+    out["V"] = np.asarray(ri.aux_metric(aux))
+    L = ri.aux_cholesky(aux, lam)
+    out["L"] = np.asarray(L)
+    C, occ = J(s.C_occ), J(s.occ)
+    g = ri.df_coulomb_gamma_screened(sp, C, occ, aux, pi2, pj2, chunk=512, valid=v2)
+    out["gamma"] = np.asarray(g)
+    out["E"] = float(ri.df_coulomb_solve(g, aux, cholV=L))
+    from scipy.linalg import cho_solve
+    out["d"] = cho_solve((np.asarray(L), True), np.asarray(g))
+    gu = ri.df_coulomb_gamma_screened(sp, C, occ, aux, ui, uj, chunk=512, valid=uw)
+    out["gamma_unique"] = np.asarray(gu)
+    np.savez_compressed(os.path.join(HERE, f"ref_{name}.npz"), **out)
+    print(f"{name}: M={M} n_sig={n} unique={nu} E={out['E']:.15g}")
+
+
+def make_grad(eps=1e-7, lam=1e-8):
+    spec, iso, pairs, ri = _modules()
+    s = small_random_system(10, 3, seed=3, spread=1.0, n_atoms=3)
+    sp0 = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+    pi, pj, v = pairs.neighbor_pairs(sp0, eps=eps)
+    aux = iso.init_product_aux(sp0)
+    L = ri.aux_cholesky(aux, lam)
+
+    def energy(quat, ls, cen, C):
+        sp = spec.Splat(quat=J(quat), log_scale=J(ls), centers=J(cen))
+        return float(ri.df_coulomb_energy_screened(sp, J(C), J(s.occ), aux, pi, pj, chunk=64,
+                                                   valid=v, cholV=L))
+
+    x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy()]
+
+    def fd(k, h):
+        g = np.zeros_like(x0[k])
+        for idx in np.ndindex(x0[k].shape):
+            xp = [a.copy() for a in x0]
+            xm = [a.copy() for a in x0]
+            xp[k][idx] += h
+            xm[k][idx] -= h
+            g[idx] = (energy(*xp) - energy(*xm)) / (2 * h)
+        return g
+
+    out = dict(quat=s.quat, log_scale=s.log_scale, centers=s.centers, C_occ=s.C_occ, occ=s.occ,
+               eps=eps, lam=lam, E=energy(*x0))
+    for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
+        h = 1e-3
+        out[name] = (4 * fd(k, h / 2) - fd(k, h)) / 3          # Richardson, O(h^4)
+    np.savez_compressed(os.path.join(HERE, "ref_grad.npz"), **out)
+    print("grad: M=10 E=", out["E"])
+
+
+def make_nodes_bwd():
+    _, _, _, ri = _modules()
+    rng = np.random.default_rng(7)
+    A, B = 9, 13
+    beta = np.exp(rng.normal(0.0, 1.0, A))
+    Lam = np.exp(rng.normal(0.0, 1.0, (B, 3)))
+    dp2 = rng.uniform(0.0, 6.0, (A, B, 3))
+    gI = rng.normal(0.0, 1.0, (A, B))
+    nodes = ri._isobra_nodes
+    coul = np.asarray(nodes(J(beta), J(dp2), J(Lam)))
+    d_beta, d_dp2, d_Lam = nodes.bwd((J(beta), J(dp2), J(Lam)), J(gI))
+    np.savez_compressed(os.path.join(HERE, "ref_nodes_bwd.npz"), beta=beta, Lam=Lam, dp2=dp2,
+                        gI=gI, coul=coul, d_beta=np.asarray(d_beta), d_dp2=np.asarray(d_dp2),
+                        d_Lam=np.asarray(d_Lam))
+    print("nodes_bwd: done")
+
+
+if __name__ == "__main__":
+    for name, s in _cases().items():
+        make_case(name, s)
+    make_grad()
+    make_nodes_bwd()

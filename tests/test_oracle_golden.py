@@ -1,0 +1,141 @@
+"""The CPU oracle against golden vectors produced by executing the reference's own source
+(``tests/golden/make_golden.py``). These pin the oracle before it is trusted as the checker."""
+import numpy as np
+import pytest
+
+import gsdft_oracle as O
+from conftest import load_golden
+
+CASES = ["ref_rand24.npz", "ref_rand48.npz", "ref_co2.npz"]
+
+
+def _q(g):
+    return O.full_quantities(g["quat"], g["log_scale"], g["centers"])
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_chart_matches_reference(case):
+    g = load_golden(case)
+    A, _, N = _q(g)
+    np.testing.assert_allclose(A, g["A"], rtol=0, atol=1e-13 * np.abs(g["A"]).max())
+    np.testing.assert_allclose(N, g["N"], rtol=1e-14)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_pair_lists_bit_exact(case):
+    g = load_golden(case)
+    q = _q(g)
+    eps = float(g["eps"])
+    n = g["ord_pi"].size
+    pi, pj, v, n_sig = O.neighbor_pairs(q, eps=eps)
+    assert n_sig == n
+    np.testing.assert_array_equal(pi, g["ord_pi"])
+    np.testing.assert_array_equal(pj, g["ord_pj"])
+    assert v.dtype == bool and v.all()
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=eps, pad_to=n + 37)
+    np.testing.assert_array_equal(pi, g["pad_pi"])
+    np.testing.assert_array_equal(pj, g["pad_pj"])
+    np.testing.assert_array_equal(v, g["pad_v"])
+    pi, pj, w, _ = O.neighbor_pairs(q, eps=eps, unique=True)
+    np.testing.assert_array_equal(pi, g["uni_pi"])
+    np.testing.assert_array_equal(pj, g["uni_pj"])
+    np.testing.assert_array_equal(w, g["uni_w"])
+    M = q[1].shape[0]
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=-1.0, pad_to=M * M + 11)
+    np.testing.assert_array_equal(pi, g["all_pi"])
+    np.testing.assert_array_equal(pj, g["all_pj"])
+    np.testing.assert_array_equal(v, g["all_v"])
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_overflow_keeps_the_reference_set(case):
+    """Overflow ranks by |S|. The oracle shares one overlap per unordered pair; the reference
+    evaluates both orientations. The kept sets agree except where an (i,j)/(j,i) twin straddles
+    the cut, which this asserts is at most one twin swap."""
+    g = load_golden(case)
+    q = _q(g)
+    eps = float(g["eps"])
+    M = q[1].shape[0]
+    for key, unique in (("over", False), ("uover", True)):
+        ref_pi, ref_pj = g[f"{key}_pi"], g[f"{key}_pj"]
+        pad = ref_pi.size
+        pi, pj, _, _ = O.neighbor_pairs(q, eps=eps, pad_to=pad, unique=unique)
+        got = set(zip(pi.tolist(), pj.tolist()))
+        want = set(zip(ref_pi.tolist(), ref_pj.tolist()))
+        diff = got ^ want
+        if unique:
+            assert not diff
+        else:
+            assert len(diff) <= 2
+            if diff:
+                (a, b), (c, d) = sorted(diff)
+                assert (a, b) == (d, c), "only a transposed twin may differ"
+        flat = pi.astype(np.int64) * M + pj
+        assert np.all(np.diff(flat) > 0)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_aux_metric_factor_gamma_energy(case):
+    g = load_golden(case)
+    q = _q(g)
+    la, R = O.init_product_aux(q)
+    np.testing.assert_allclose(la, g["aux_log_alpha"], rtol=0, atol=1e-14)
+    np.testing.assert_allclose(R, g["aux_R"], rtol=0, atol=1e-13)
+    aq = O.aux_quantities(g["aux_log_alpha"], g["aux_R"])
+    V = O.aux_metric(*aq)
+    np.testing.assert_allclose(V, g["V"], rtol=1e-13, atol=1e-13 * np.abs(g["V"]).max())
+    L = O.aux_cholesky(V, float(g["lam"]))
+    gamma = O.df_coulomb_gamma_screened(q, g["C_occ"], g["occ"], aq, g["pad_pi"], g["pad_pj"],
+                                        g["pad_v"], chunk=512)
+    np.testing.assert_allclose(gamma, g["gamma"], rtol=1e-12, atol=1e-12 * np.abs(g["gamma"]).max())
+    E, d = O.df_coulomb_solve(gamma, L)
+    np.testing.assert_allclose(E, float(g["E"]), rtol=1e-12)
+    gu = O.df_coulomb_gamma_screened(q, g["C_occ"], g["occ"], aq, g["uni_pi"], g["uni_pj"],
+                                     g["uni_w"], chunk=512)
+    np.testing.assert_allclose(gu, g["gamma_unique"], rtol=1e-12,
+                               atol=1e-12 * np.abs(g["gamma"]).max())
+    # unique-weight gamma equals the ordered gamma (gs-dft tests/unit/test_pair_tricks.py:81-100)
+    np.testing.assert_allclose(gu, gamma, rtol=1e-10, atol=1e-12)
+
+
+def test_gradient_matches_reference_finite_differences():
+    g = load_golden("ref_grad.npz")
+    q = _q(g)
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=float(g["eps"]))
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    L = O.aux_cholesky(O.aux_metric(*aq), float(g["lam"]))
+    res = O.energy_and_grad((g["quat"], g["log_scale"], g["centers"], g["C_occ"], g["occ"]),
+                            aq, L, pi, pj, v)
+    np.testing.assert_allclose(res["E"], float(g["E"]), rtol=1e-13)
+    for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
+        ref = g[k]
+        # Richardson central differences are good to ~1e-10 of the largest component here.
+        np.testing.assert_allclose(res[k], ref, rtol=0, atol=2e-9 * np.abs(ref).max())
+
+
+def test_node_reverse_matches_reference_nodes_bwd():
+    g = load_golden("ref_nodes_bwd.npz")
+    coul = O.isobra_nodes(g["beta"], g["dp2"], g["Lam"])
+    np.testing.assert_allclose(coul, g["coul"], rtol=1e-14)
+    d_beta, d_dp2, d_Lam = O.isobra_nodes_bwd(g["beta"], g["dp2"], g["Lam"], g["gI"])
+    np.testing.assert_allclose(d_beta, g["d_beta"], rtol=1e-13, atol=1e-15)
+    np.testing.assert_allclose(d_dp2, g["d_dp2"], rtol=1e-13, atol=1e-15)
+    np.testing.assert_allclose(d_Lam, g["d_Lam"], rtol=1e-13, atol=1e-15)
+
+
+def test_pad_rule_and_stripe():
+    """pad_to = ceil(pad n0 / G) G (gs_dft/ks/train.py:356-359); striping deals pairs round-robin
+    so each device block has the same valid:dummy ratio (gs_dft/ks/shard.py:146-166)."""
+    assert O.pad_rule(1000, 2.0, 8) == 2000
+    assert O.pad_rule(1001, 2.0, 8) == 2008
+    pi = np.arange(24, dtype=np.int32)
+    v = np.arange(24) < 10
+    spi, spj, sv = O.stripe_pairs(pi, pi, v, 4)
+    blocks = sv.reshape(4, 6)
+    counts = blocks.sum(1)
+    assert counts.max() - counts.min() <= 1
+    for b in blocks:                       # valid entries at each block's front
+        k = b.sum()
+        assert b[:k].all() and not b[k:].any()
+    assert O.stripe_pairs(pi, pi, v, 5)[0] is pi      # n % G != 0 leaves the list alone
