@@ -1,0 +1,401 @@
+#!/usr/bin/env python
+"""Benchmark: screened RI-J J-build + gradient (FP64) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config C]
+
+Metric: "J-build+grad s/step and Gpair-aux integrals/s (FP64) at 1/2/4/8 B200".
+A step = splat quantities -> pair prep -> gamma -> [allreduce gamma] -> metric solve -> reverse
+pass -> chain -> per-splat reductions -> chart reverse -> [allreduce gradients]; the pair list,
+aux, metric and factor are refresh products, built before the timed region and reported apart.
+``value`` = N_aux x live pairs (all ranks) / step seconds, in G pair-aux integrals/s.
+
+Workload: configuration 1 of BASELINE.json (ethanol, M=600, n_occ=13, eps=1e-7), synthetic seeded
+splats (gs_dft_b200.systems). For N > 1 launch with torchrun (one rank per GPU, NCCL); the list is
+partitioned across ranks (strong scaling: total work fixed).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gs-dft_b200"))
+
+METRIC = "J-build+grad s/step and Gpair-aux integrals/s (FP64) at 1/2/4/8 B200"
+UNIT = "G pair-aux integrals/s"
+# Algorithmic FP64 work per (aux, pair) integral, fixed from the reference's expression count
+# (gs_dft/coulomb/ri.py:146-151,175-185 forward; :204-220 plus the dp2 chain reverse).
+FLOP_FWD, FLOP_VJP = 706, 2050
+FP64_DATASHEET = 37e12
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, default=1)
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ------------------------------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def start(self):
+        try:
+            self.p = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.index), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.flush()
+        rows = [r.split(",") for r in open(self.f.name).read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for k, n in enumerate(names):
+                    if "Active" in r[5 + k] or r[5 + k].strip() == "1":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------
+# the CPU oracle (checker / baseline)
+# ------------------------------------------------------------------------------------------------
+def oracle_problem(sy):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import gsdft_oracle as O
+    q = O.full_quantities(sy.quat, sy.log_scale, sy.centers)
+    pi, pj, v, n_sig = O.neighbor_pairs(q, eps=sy.eps)
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    L = O.aux_cholesky(O.aux_metric(*aq), sy.lam)
+    return O, (sy.quat, sy.log_scale, sy.centers, sy.C_occ, sy.occ), aq, L, pi, pj, v
+
+
+def cpu_sample_rate(sy, target_s=10.0, prob=None):
+    """Time the C/OpenMP oracle step on a slice of the live pairs; integrals/s, pairs, threads."""
+    O, sa, aq, L, pi, pj, v = prob or oracle_problem(sy)
+    n_aux = aq[0].shape[0]
+    k = min(2000, pi.shape[0])
+    t0 = time.perf_counter()
+    O.energy_and_grad_c(sa, aq, L, pi[:k], pj[:k], v[:k])
+    dt = time.perf_counter() - t0
+    k2 = int(min(pi.shape[0], max(k, k * target_s / max(dt, 1e-3))))
+    t0 = time.perf_counter()
+    O.energy_and_grad_c(sa, aq, L, pi[:k2], pj[:k2], v[:k2])
+    dt = time.perf_counter() - t0
+    return n_aux * k2 / dt, k2, dt, len(os.sched_getaffinity(0))
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from gs_dft_b200.systems import make_config
+    sy = make_config(args.config)
+    prob = oracle_problem(sy)
+    O, sa, aq, L, pi, pj, v = prob
+    n_aux = aq[0].shape[0]
+    k = min(4000, pi.shape[0])
+    for _ in range(args.warmup):
+        O.energy_and_grad_c(sa, aq, L, pi[:k], pj[:k], v[:k])
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        O.energy_and_grad_c(sa, aq, L, pi[:k], pj[:k], v[:k])
+        ts.append(time.perf_counter() - t0)
+    t = sum(ts) / len(ts)
+    val = n_aux * k / t / 1e9
+    cores = len(os.sched_getaffinity(0))
+    sample = (f"C/OpenMP restatement of the reference's RI-J step (oracle port; the JAX reference "
+              f"cannot be installed offline): first {k} of {int((v != 0).sum())} live pairs x all "
+              f"{n_aux} aux per step, energy + full gradient")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": sy.name, "M": sy.M, "n_occ": sy.n_occ, "eps": sy.eps,
+                   "n_aux": n_aux, "pairs_per_step": k},
+        "cpu_baseline": {"value": val, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+def dfma_peak(torch, lib, ptr, stream_handle):
+    """Measured FP64 FMA throughput (FLOP/s) of this device at the current clocks."""
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    blocks, threads, iters = props.multi_processor_count * 8, 256, 20000
+    out = torch.empty(blocks * threads, dtype=torch.float64, device="cuda")
+    s = stream_handle()
+    lib.call("gsdft_dfma_probe", ptr(out), 200, blocks, threads, s)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = 0.0
+    for _ in range(3):
+        a.record()
+        lib.call("gsdft_dfma_probe", ptr(out), iters, blocks, threads, s)
+        b.record()
+        torch.cuda.synchronize()
+        best = max(best, 2.0 * 16 * iters * blocks * threads / (a.elapsed_time(b) * 1e-3))
+    return best
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import gs_dft_b200 as g
+    from gs_dft_b200._lib import lib, ptr, stream_handle
+    from gs_dft_b200.coulomb.engine import check_device_status
+    from gs_dft_b200.ks.shard import ShardedRIJ
+    from gs_dft_b200.systems import make_config
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    sy = make_config(args.config)
+    t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64, device=dev)
+    quat, log_scale, centers, C, occ = (t(sy.quat), t(sy.log_scale), t(sy.centers), t(sy.C_occ),
+                                        t(sy.occ))
+    splats = g.Splat(quat, log_scale, centers)
+
+    # ---- refresh (timed apart; amortised at refresh = 10 steps in the report) -------------------
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    n0 = g.screening.count_significant(splats, sy.eps)
+    pad_to = g.pad_rule(n0, 2.0, world)
+    pi, pj, valid = g.neighbor_pairs(splats, eps=sy.eps, pad_to=pad_to)
+    aux = g.init_product_aux(splats)
+    L = g.aux_cholesky(aux, sy.lam)
+    beta, R, KN = aux.quantities()
+    R = R.contiguous()
+    sh = ShardedRIJ(pi, pj, valid, sy.M, sy.n_occ, beta, R, KN, L, rank, world)
+    torch.cuda.synchronize()
+    refresh_s = time.perf_counter() - t0
+    eng = sh.engine
+    n_live_local = eng.plan.n_live
+    n_live = n0
+    n_aux = int(beta.shape[0])
+
+    flush = torch.empty(L2_FLUSH_BYTES // 8, dtype=torch.float64, device=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def step():
+        return sh.step(quat, log_scale, centers, C, occ)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    check_device_status()
+
+    # ---- device-timed steps (inputs resident; L2 flushed between steps, outside the events) -----
+    eng.timing = True
+    eng.events = {"forward": [], "vjp": []}
+    clocks = Clocks(local)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = lib.gsdft_kernel_launches()
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for k in range(args.steps):
+        flush.fill_(float(k))
+        starts[k].record()
+        step()
+        ends[k].record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    launches = lib.gsdft_kernel_launches() - launches0
+    eng.timing = False
+    step_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    t_fwd = eng.kernel_ms("forward")
+    t_vjp = eng.kernel_ms("vjp")
+    check_device_status()
+    tt = torch.tensor([step_ms, t_fwd, t_vjp], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    step_ms, t_fwd, t_vjp = (float(x) for x in tt.tolist())
+    ms_per_step = step_ms / args.steps
+    value = n_aux * n_live / (ms_per_step * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers ------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        ks = g.CoulombKS(coulomb=g.df(), screen=g.pairlist(eps=sy.eps), n_devices=1)
+        e2e = measure_e2e(torch, g, ks, sy, dev, pi, pj, valid, aux, L, args, world, rank, sh,
+                          barrier)
+
+    peak = dfma_peak(torch, lib, ptr, stream_handle)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    cpu = None
+    if not args.no_cpu and world == 1:
+        rate, k2, dt, cores = cpu_sample_rate(sy)
+        cpu = {"value": rate / 1e9, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": (f"C/OpenMP oracle (restatement of the reference step, energy + full "
+                          f"gradient) on the first {k2} of {n_live} live pairs x all {n_aux} aux, "
+                          f"{dt:.1f} s on {cores} threads")}
+
+    dom = "j_vjp_kernel" if t_vjp >= t_fwd else "j_forward_kernel"
+    t_dom = max(t_vjp, t_fwd)
+    flop = (FLOP_VJP if t_vjp >= t_fwd else FLOP_FWD) * n_aux * n_live_local
+    achieved = flop / (t_dom * 1e-3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "s_per_step": ms_per_step * 1e-3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic",
+        "config": {"workload": f"{sy.name} (BASELINE configs[1])", "M": sy.M, "n_occ": sy.n_occ,
+                   "eps": sy.eps, "n_aux": n_aux, "live_pairs": n_live, "pad_to": int(pad_to),
+                   "parallelism": f"pair-partition x{world}", "l2": "flushed between steps"},
+        "refresh_s": refresh_s,
+        "kernel_ms": {"j_forward": t_fwd, "j_vjp": t_vjp},
+        "roofline": {"bound": "fp64", "kernel": dom, "achieved": achieved / 1e12,
+                     "peak": peak / 1e12, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": "measured DFMA probe on this GPU in this run (MEASURED_PEAKS.json has no FP64 figure); datasheet 37 TFLOP/s",
+                     "frac_of_datasheet": achieved / FP64_DATASHEET,
+                     "flop_per_integral": FLOP_VJP if t_vjp >= t_fwd else FLOP_FWD,
+                     "traffic": None},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+    }
+    if e2e is not None:
+        line["e2e"] = e2e
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def measure_e2e(torch, g, ks, sy, dev, pi, pj, valid, aux, L, args, world, rank, sh, barrier):
+    """Same metric through the public API (CoulombKS + autograd) with pinned host buffers: every
+    step copies the parameters in and reads E and the gradients back."""
+    import numpy as np
+    hp = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64).pin_memory()
+    h_quat, h_ls, h_cen, h_C, h_occ = hp(sy.quat), hp(sy.log_scale), hp(sy.centers), hp(sy.C_occ), hp(sy.occ)
+    d = lambda h: torch.empty(h.shape, dtype=torch.float64, device=dev)
+    quat, ls, cen, C, occ = d(h_quat), d(h_ls), d(h_cen), d(h_C), d(h_occ)
+    for x in (quat, ls, cen, C):
+        x.requires_grad_(True)
+    model = g.SplatModel(basis=g.Splat(quat, ls, cen), C=C, occupations=occ)
+    if world > 1:
+        s, e = sh.ranges[rank]
+        state = g.SplatState(pairs=(pi[s:e], pj[s:e], valid[s:e]), aux=aux, cholV=L)
+    else:
+        state = g.SplatState(pairs=(pi, pj, valid), aux=aux, cholV=L)
+    outs = [hp(np.zeros(1)), hp(sy.quat), hp(sy.log_scale), hp(sy.centers), hp(sy.C_occ)]
+    h2d = sum(x.numel() * 8 for x in (h_quat, h_ls, h_cen, h_C, h_occ))
+    d2h = sum(x.numel() * 8 for x in outs)
+
+    def one():
+        with torch.no_grad():
+            for dst, src in ((quat, h_quat), (ls, h_ls), (cen, h_cen), (C, h_C), (occ, h_occ)):
+                dst.copy_(src, non_blocking=True)
+        for x in (quat, ls, cen, C):
+            x.grad = None
+        E = ks(model, state)
+        E.backward()
+        outs[0].copy_(E.detach().reshape(1), non_blocking=True)
+        outs[1].copy_(quat.grad, non_blocking=True)
+        outs[2].copy_(ls.grad, non_blocking=True)
+        outs[3].copy_(cen.grad, non_blocking=True)
+        outs[4].copy_(C.grad, non_blocking=True)
+
+    def one_sharded():
+        with torch.no_grad():
+            for dst, src in ((quat, h_quat), (ls, h_ls), (cen, h_cen), (C, h_C), (occ, h_occ)):
+                dst.copy_(src, non_blocking=True)
+        o = sh.step(quat.detach(), ls.detach(), cen.detach(), C.detach(), occ)
+        outs[0].copy_(o["E"].reshape(1), non_blocking=True)
+        outs[1].copy_(o["g_quat"], non_blocking=True)
+        outs[2].copy_(o["g_log_scale"], non_blocking=True)
+        outs[3].copy_(o["g_centers"], non_blocking=True)
+        outs[4].copy_(o["g_C"], non_blocking=True)
+
+    fn = one if world == 1 else one_sharded
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms = a.elapsed_time(b) / args.steps
+    tt = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    n_aux = int(aux.n_basis)
+    n_live = int((valid != 0).sum().item())
+    return {"value": n_aux * n_live / (ms * 1e-3) / 1e9, "unit": UNIT, "ms_per_step": ms,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "api": "CoulombKS(model, state) + torch autograd" if world == 1 else "ShardedRIJ.step"}
+
+
+if __name__ == "__main__":
+    main()

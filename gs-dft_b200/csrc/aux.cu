@@ -1,0 +1,256 @@
+// Product auxiliary basis, its Coulomb metric, the metric's Cholesky factor and the per-step solve.
+// Reference: gs_dft/basis/isotropic.py:22-39,81-116 (aux); gs_dft/coulomb/ri.py:63-123,267-275
+// (metric), :243-264 (factor), :472-482 (solve).
+#include <cublas_v2.h>
+#include <cusolverDn.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+
+namespace gsdft {
+
+struct Scales {
+  double v[64];
+};
+
+__global__ void product_aux_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
+                                   const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                                   const double* __restrict__ w, int64_t n, Scales scales,
+                                   int n_scales, double* __restrict__ log_alpha,
+                                   double* __restrict__ R) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n) return;
+  int i = pi ? pi[a] : (int)a;
+  int j = pj ? pj[a] : (int)a;
+  double Ai[9], Aj[9], mui[3], muj[3];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    Ai[k] = A9[9 * (int64_t)i + k];
+    Aj[k] = A9[9 * (int64_t)j + k];
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    mui[k] = mu[3 * (int64_t)i + k];
+    muj[k] = mu[3 * (int64_t)j + k];
+  }
+  double Ah[9], P[3], KN, det;
+  pair_quantities_rn(Ai, Aj, mui, muj, 1.0, 1.0, Ah, P, &KN, &det);
+  double alpha0 = pow(det, 1.0 / 3.0);
+  if (w && w[a] == 0.0) alpha0 = 1.0;
+  for (int s = 0; s < n_scales; ++s) {
+    int64_t o = (int64_t)s * n + a;
+    log_alpha[o] = log(alpha0 * scales.v[s]);
+    R[3 * o + 0] = P[0];
+    R[3 * o + 1] = P[1];
+    R[3 * o + 2] = P[2];
+  }
+}
+
+__global__ void aux_quantities_kernel(const double* __restrict__ log_alpha, int64_t n,
+                                      double* __restrict__ beta, double* __restrict__ KN) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n) return;
+  double b = exp(log_alpha[a]);
+  beta[a] = b;
+  KN[a] = pow(2.0 * b / kPi, 0.75);
+}
+
+// F0(T) = 1/2 sqrt(pi/T) erf(sqrt T), Taylor series below 1e-8.
+__device__ __forceinline__ double boys0(double T) {
+  if (T < 1e-8) return 1.0 - T / 3.0 + T * T / 10.0 - T * T * T / 42.0;
+  return 0.5 * sqrt(kPi / T) * erf(sqrt(T));
+}
+
+// One metric entry in the canonical orientation (lo, hi) so V is exactly symmetric.
+__global__ void aux_metric_kernel(const double* __restrict__ beta, const double* __restrict__ R,
+                                  const double* __restrict__ KN, int64_t n, double* __restrict__ V) {
+  int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (q >= n) return;
+  for (int64_t p = blockIdx.y; p < n; p += gridDim.y) {
+    int64_t lo = p < q ? p : q, hi = p < q ? q : p;
+    double g1 = beta[lo], g2 = beta[hi];
+    double gab = g1 * g2;
+    double gsum = g1 + g2;
+    double dx = R[3 * lo] - R[3 * hi], dy = R[3 * lo + 1] - R[3 * hi + 1];
+    double dz = R[3 * lo + 2] - R[3 * hi + 2];
+    double PQ2 = dx * dx + dy * dy + dz * dz;
+    double rho = gab / gsum;
+    double T = rho * PQ2;
+    double coul = 34.986836655249725 / (gab * sqrt(gsum)) * boys0(T);   // 2 pi^2.5
+    V[p * n + q] = (KN[lo] * KN[hi]) * coul;
+  }
+}
+
+__global__ void shift_diag_kernel(double* V, int64_t n, double lam) {
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i < n) V[i * n + i] += lam;
+}
+
+// Zero the strict upper triangle of a row-major matrix.
+__global__ void zero_upper_kernel(double* V, int64_t n) {
+  int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (q >= n) return;
+  for (int64_t p = blockIdx.y; p < q; p += gridDim.y) V[p * n + q] = 0.0;
+}
+
+// E = 1/2 gamma . d, one block, fixed-order tree: deterministic.
+__global__ void half_dot_kernel(const double* __restrict__ g, const double* __restrict__ d,
+                                int64_t n, double* E) {
+  __shared__ double s[1024];
+  double acc = 0.0;
+  for (int64_t k = threadIdx.x; k < n; k += blockDim.x) acc = fma(g[k], d[k], acc);
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) s[threadIdx.x] += s[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *E = 0.5 * s[0];
+}
+
+// Library handles, one per device, created on first use.
+struct Handles {
+  cusolverDnHandle_t solver = nullptr;
+  cublasHandle_t blas = nullptr;
+};
+
+static std::mutex g_mu;
+static std::unordered_map<int, Handles> g_handles;
+
+static int get_handles(Handles** out) {
+  int dev = 0;
+  GSDFT_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_mu);
+  Handles& h = g_handles[dev];
+  if (!h.solver) {
+    if (cusolverDnCreate(&h.solver) != CUSOLVER_STATUS_SUCCESS)
+      return fail(GSDFT_ERR_LINALG, "cusolverDnCreate failed");
+  }
+  if (!h.blas) {
+    if (cublasCreate(&h.blas) != CUBLAS_STATUS_SUCCESS)
+      return fail(GSDFT_ERR_LINALG, "cublasCreate failed");
+  }
+  *out = &h;
+  return GSDFT_OK;
+}
+
+}  // namespace gsdft
+
+using namespace gsdft;
+
+extern "C" int gsdft_product_aux(const double* A9, const double* mu, const double* N, int64_t M,
+                                 const int32_t* pi, const int32_t* pj, const double* w,
+                                 int64_t n_pairs, const double* scales_host, int n_scales,
+                                 double* log_alpha, double* R, gsdft_stream_t stream) {
+  (void)N;
+  GSDFT_REQUIRE(M > 0 && n_scales >= 1 && n_scales <= 64, "bad M or n_scales (1..64)");
+  GSDFT_REQUIRE(A9 && mu && scales_host && log_alpha && R, "null pointer");
+  GSDFT_REQUIRE((pi == nullptr) == (pj == nullptr), "pi and pj must both be given or both NULL");
+  int64_t n = pi ? n_pairs : M;
+  if (n == 0) return GSDFT_OK;
+  Scales sc;
+  for (int s = 0; s < n_scales; ++s) sc.v[s] = scales_host[s];
+  product_aux_kernel<<<grid_1d(n, 128), 128, 0, (cudaStream_t)stream>>>(A9, mu, pi, pj, w, n, sc,
+                                                                       n_scales, log_alpha, R);
+  GSDFT_LAUNCHED("product_aux");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_aux_quantities(const double* log_alpha, int64_t n_aux, double* beta,
+                                    double* KN, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_aux >= 0, "n_aux < 0");
+  if (n_aux == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(log_alpha && beta && KN, "null pointer");
+  aux_quantities_kernel<<<grid_1d(n_aux, 128), 128, 0, (cudaStream_t)stream>>>(log_alpha, n_aux,
+                                                                              beta, KN);
+  GSDFT_LAUNCHED("aux_quantities");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_aux_metric(const double* beta, const double* R, const double* KN,
+                                int64_t n_aux, double* V, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_aux > 0 && n_aux < (int64_t(1) << 31), "n_aux out of range");
+  GSDFT_REQUIRE(beta && R && KN && V, "null pointer");
+  dim3 grid(grid_1d(n_aux, 128), (unsigned)imin64(n_aux, 65535));
+  aux_metric_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(beta, R, KN, n_aux, V);
+  GSDFT_LAUNCHED("aux_metric");
+  return GSDFT_OK;
+}
+
+extern "C" size_t gsdft_aux_cholesky_workspace_size(int64_t n_aux) {
+  Handles* h = nullptr;
+  if (get_handles(&h)) return 0;
+  int lwork = 0;
+  if (cusolverDnDpotrf_bufferSize(h->solver, CUBLAS_FILL_MODE_UPPER, (int)n_aux, nullptr,
+                                  (int)n_aux, &lwork) != CUSOLVER_STATUS_SUCCESS)
+    return 0;
+  return align_up((size_t)lwork * sizeof(double), 256) + 256 + 256;
+}
+
+extern "C" int gsdft_aux_cholesky(double* V, int64_t n_aux, double lam, void* ws, size_t ws_bytes,
+                                  gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_aux > 0 && n_aux < (int64_t(1) << 31), "n_aux out of range");
+  GSDFT_REQUIRE(V, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  Handles* h = nullptr;
+  int rc = get_handles(&h);
+  if (rc) return rc;
+  int lwork = 0;
+  if (cusolverDnDpotrf_bufferSize(h->solver, CUBLAS_FILL_MODE_UPPER, (int)n_aux, V, (int)n_aux,
+                                  &lwork) != CUSOLVER_STATUS_SUCCESS)
+    return fail(GSDFT_ERR_LINALG, "potrf_bufferSize failed");
+  Carver c(ws, ws_bytes);
+  double* work = c.take<double>((size_t)lwork);
+  int* info = c.take<int>(1);
+  if (!c.ok) return fail(GSDFT_ERR_ARG, "cholesky workspace too small (%zu < %zu)", ws_bytes, c.off);
+  shift_diag_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(V, n_aux, lam);
+  GSDFT_LAUNCHED("shift_diag");
+  cusolverDnSetStream(h->solver, st);
+  // Row-major V is symmetric, so it is its own column-major view; the column-major UPPER factor U
+  // (V = U^T U) read back row-major is the lower factor L = U^T.
+  if (cusolverDnDpotrf(h->solver, CUBLAS_FILL_MODE_UPPER, (int)n_aux, V, (int)n_aux, work, lwork,
+                       info) != CUSOLVER_STATUS_SUCCESS)
+    return fail(GSDFT_ERR_LINALG, "cusolverDnDpotrf failed to launch");
+  int info_h = 0;
+  GSDFT_CUDA(cudaMemcpyAsync(&info_h, info, sizeof(int), cudaMemcpyDeviceToHost, st));
+  GSDFT_CUDA(cudaStreamSynchronize(st));
+  if (info_h != 0)
+    return fail(GSDFT_ERR_LINALG, "aux metric + lam I is not positive definite (potrf info %d)",
+                info_h);
+  dim3 grid(grid_1d(n_aux, 256), (unsigned)imin64(n_aux, 65535));
+  zero_upper_kernel<<<grid, 256, 0, st>>>(V, n_aux);
+  GSDFT_LAUNCHED("zero_upper");
+  return GSDFT_OK;
+}
+
+extern "C" size_t gsdft_j_solve_workspace_size(int64_t n_aux) {
+  (void)n_aux;
+  return 0;
+}
+
+extern "C" int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d,
+                             double* E, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
+  (void)ws;
+  (void)ws_bytes;
+  GSDFT_REQUIRE(n_aux > 0 && n_aux < (int64_t(1) << 31), "n_aux out of range");
+  GSDFT_REQUIRE(L && gamma && d && E, "null pointer");
+  GSDFT_REQUIRE(d != gamma, "d must not alias gamma");
+  cudaStream_t st = (cudaStream_t)stream;
+  Handles* h = nullptr;
+  int rc = get_handles(&h);
+  if (rc) return rc;
+  GSDFT_CUDA(cudaMemcpyAsync(d, gamma, n_aux * sizeof(double), cudaMemcpyDeviceToDevice, st));
+  cublasSetStream(h->blas, st);
+  // Row-major lower L is the column-major upper U = L^T: L y = g  <=>  U^T y = g; L^T d = y <=> U d = y.
+  if (cublasDtrsv(h->blas, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_T, CUBLAS_DIAG_NON_UNIT, (int)n_aux, L,
+                  (int)n_aux, d, 1) != CUBLAS_STATUS_SUCCESS)
+    return fail(GSDFT_ERR_LINALG, "cublasDtrsv (forward) failed");
+  if (cublasDtrsv(h->blas, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N, CUBLAS_DIAG_NON_UNIT, (int)n_aux, L,
+                  (int)n_aux, d, 1) != CUBLAS_STATUS_SUCCESS)
+    return fail(GSDFT_ERR_LINALG, "cublasDtrsv (backward) failed");
+  half_dot_kernel<<<1, 1024, 0, st>>>(gamma, d, n_aux, E);
+  GSDFT_LAUNCHED("half_dot");
+  return GSDFT_OK;
+}

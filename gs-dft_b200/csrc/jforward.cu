@@ -1,0 +1,332 @@
+// Per-step pair preparation and the fused forward fit-vector contraction
+//   gamma_P = sum_a (P|a) q_a,   (P|a) = KN_P KN_a pref sum_t w_t (G0 G1 G2)^(-1/2) exp(-t^2 S),
+// the 3-centre integral never stored. Reference: gs_dft/coulomb/ri.py:126-185 (block + nodes),
+// :436-469 (gamma stream), gs_dft/coulomb/stream.py:203-215 (pair quantities), ri.py:456 (q).
+#include "common.cuh"
+
+namespace gsdft {
+
+// ------------------------------------------------------------------------------------------------
+// Pair prep: geometry + symmetric eigen-decomposition of A_hat (cyclic Jacobi).
+// ------------------------------------------------------------------------------------------------
+
+// Cyclic Jacobi on a symmetric 3x3 (Golub & Van Loan, symmetric Schur decomposition). a is
+// overwritten; lam gets the eigenvalues ascending and V (row-major) the matching eigenvectors as
+// columns.
+__device__ void jacobi_eig3(double a[3][3], double lam[3], double V[9]) {
+  double v[3][3] = {{1, 0, 0}, {0, 1, 0}, {0, 0, 1}};
+  for (int sweep = 0; sweep < 12; ++sweep) {
+    double off = a[0][1] * a[0][1] + a[0][2] * a[0][2] + a[1][2] * a[1][2];
+    double dia = a[0][0] * a[0][0] + a[1][1] * a[1][1] + a[2][2] * a[2][2];
+    if (off <= 1e-36 * dia) break;
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const int p = r == 2 ? 1 : 0;
+      const int q = r == 0 ? 1 : 2;
+      double apq = a[p][q];
+      if (apq == 0.0) continue;
+      double theta = (a[q][q] - a[p][p]) / (2.0 * apq);
+      double t = (theta >= 0.0 ? 1.0 : -1.0) / (fabs(theta) + sqrt(theta * theta + 1.0));
+      double c = 1.0 / sqrt(t * t + 1.0);
+      double s = t * c;
+      a[p][p] -= t * apq;
+      a[q][q] += t * apq;
+      a[p][q] = a[q][p] = 0.0;
+      const int o = 3 - p - q;
+      double aop = a[o][p], aoq = a[o][q];
+      a[o][p] = a[p][o] = c * aop - s * aoq;
+      a[o][q] = a[q][o] = s * aop + c * aoq;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        double vkp = v[k][p], vkq = v[k][q];
+        v[k][p] = c * vkp - s * vkq;
+        v[k][q] = s * vkp + c * vkq;
+      }
+    }
+  }
+  int idx[3] = {0, 1, 2};
+  double d[3] = {a[0][0], a[1][1], a[2][2]};
+  if (d[idx[1]] < d[idx[0]]) { int t = idx[0]; idx[0] = idx[1]; idx[1] = t; }
+  if (d[idx[2]] < d[idx[1]]) { int t = idx[1]; idx[1] = idx[2]; idx[2] = t; }
+  if (d[idx[1]] < d[idx[0]]) { int t = idx[0]; idx[0] = idx[1]; idx[1] = t; }
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    lam[c] = d[idx[c]];
+#pragma unroll
+    for (int r = 0; r < 3; ++r) V[3 * r + c] = v[r][idx[c]];
+  }
+}
+
+__global__ void pair_prep_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
+                                 const double* __restrict__ N, const int32_t* __restrict__ pi,
+                                 const int32_t* __restrict__ pj,
+                                 const int32_t* __restrict__ live_idx, int64_t n_live,
+                                 double* __restrict__ rec) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_live) return;
+  int64_t e = live_idx[a];
+  int i = pi[e], j = pj[e];
+  double Ai[9], Aj[9], mui[3], muj[3];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    Ai[k] = A9[9 * (int64_t)i + k];
+    Aj[k] = A9[9 * (int64_t)j + k];
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    mui[k] = mu[3 * (int64_t)i + k];
+    muj[k] = mu[3 * (int64_t)j + k];
+  }
+  double Ah[9], P[3], KN, det;
+  pair_quantities_rn(Ai, Aj, mui, muj, N[i], N[j], Ah, P, &KN, &det);
+  double s[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) s[r][c] = 0.5 * (Ah[3 * r + c] + Ah[3 * c + r]);
+  double lam[3], U[9];
+  jacobi_eig3(s, lam, U);
+  double* o = rec + a * GSDFT_REC_FIELDS;
+  o[GSDFT_REC_L0] = lam[0];
+  o[GSDFT_REC_L1] = lam[1];
+  o[GSDFT_REC_L2] = lam[2];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) o[GSDFT_REC_U00 + k] = U[k];
+  o[GSDFT_REC_P0] = P[0];
+  o[GSDFT_REC_P1] = P[1];
+  o[GSDFT_REC_P2] = P[2];
+  o[GSDFT_REC_KN] = KN * kPref;
+}
+
+// q_a = w_a sum_o occ_o C_io C_jo, one warp per live pair (lanes stride o; fixed-order reduce).
+__global__ void pair_density_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                                    const double* __restrict__ w,
+                                    const int32_t* __restrict__ live_idx, int64_t n_live,
+                                    const double* __restrict__ C, const double* __restrict__ occ,
+                                    int64_t n_occ, double* __restrict__ rec) {
+  int64_t a = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (a >= n_live) return;
+  int64_t e = live_idx[a];
+  const double* ci = C + (int64_t)pi[e] * n_occ;
+  const double* cj = C + (int64_t)pj[e] * n_occ;
+  double acc = 0.0;
+  for (int64_t o = lane; o < n_occ; o += 32) acc = fma(occ[o] * ci[o], cj[o], acc);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    double q = w[e] * acc;
+    double* r = rec + a * GSDFT_REC_FIELDS;
+    r[GSDFT_REC_Q] = q;
+    r[GSDFT_REC_QK] = q * r[GSDFT_REC_KN];
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Forward: one aux per thread (registers), pair-record tiles staged in shared memory by bulk copy.
+// ------------------------------------------------------------------------------------------------
+constexpr int kFwThreads = 128;  // aux per CTA
+constexpr int kFwTile = 32;      // pair records per staged tile (32 x 144 B)
+constexpr int kFwNP = 2;         // pairs evaluated together per thread (independent chains)
+
+__global__ void __launch_bounds__(kFwThreads)
+    j_forward_kernel(const double* __restrict__ rec, int64_t n_live,
+                     const double* __restrict__ beta, const double* __restrict__ R,
+                     const double* __restrict__ KN, int64_t n_aux, int64_t per_split,
+                     double* __restrict__ partial) {
+  __shared__ __align__(128) double tile[2][kFwTile * GSDFT_REC_FIELDS];
+  __shared__ __align__(8) uint64_t bar[2];
+  const int64_t P = blockIdx.x * (int64_t)kFwThreads + threadIdx.x;
+  const bool has_aux = P < n_aux;
+  const double b = has_aux ? beta[P] : 1.0;
+  const double r0 = has_aux ? R[3 * P] : 0.0;
+  const double r1 = has_aux ? R[3 * P + 1] : 0.0;
+  const double r2 = has_aux ? R[3 * P + 2] : 0.0;
+  const double cP = -kLog2e * b;
+  const int64_t a0 = blockIdx.y * per_split;
+  const int64_t a1 = imin64(a0 + per_split, n_live);
+  const int64_t npairs = a1 > a0 ? a1 - a0 : 0;
+  const int ntiles = (int)((npairs + kFwTile - 1) / kFwTile);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+  }
+  __syncthreads();
+  auto issue = [&](int t) {
+    int64_t s = a0 + (int64_t)t * kFwTile;
+    int cnt = (int)imin64(kFwTile, a1 - s);
+    uint32_t bytes = (uint32_t)cnt * GSDFT_REC_FIELDS * sizeof(double);
+    fence_proxy_async();
+    mbar_expect_tx(&bar[t & 1], bytes);
+    bulk_g2s(tile[t & 1], rec + s * GSDFT_REC_FIELDS, bytes, &bar[t & 1]);
+  };
+  if (threadIdx.x == 0) {
+    if (ntiles > 0) issue(0);
+    if (ntiles > 1) issue(1);
+  }
+
+  double acc = 0.0;
+  bool ok = true;
+  for (int t = 0; t < ntiles && ok; ++t) {
+    // block-uniform: a thread whose bounded wait ran out takes the whole block out of the loop
+    ok = __syncthreads_and(mbar_wait(&bar[t & 1], (t >> 1) & 1));
+    if (!ok) break;
+    const double* tl = tile[t & 1];
+    const int cnt = (int)imin64(kFwTile, a1 - (a0 + (int64_t)t * kFwTile));
+    for (int k = 0; k < cnt; k += kFwNP) {
+      double m[kFwNP][3], g[kFwNP][3], h[kFwNP][3], qk[kFwNP], coul[kFwNP];
+#pragma unroll
+      for (int p = 0; p < kFwNP; ++p) {
+        const int kk = k + p < cnt ? k + p : k;  // a duplicate of pair k stands in, weight 0
+        const double* rr = tl + kk * GSDFT_REC_FIELDS;
+        const double d0 = r0 - rr[GSDFT_REC_P0];
+        const double d1 = r1 - rr[GSDFT_REC_P1];
+        const double d2 = r2 - rr[GSDFT_REC_P2];
+#pragma unroll
+        for (int c = 0; c < 3; ++c) {
+          const double y = rr[GSDFT_REC_U00 + c] * d0 + rr[GSDFT_REC_U10 + c] * d1 +
+                           rr[GSDFT_REC_U20 + c] * d2;
+          const double L = rr[GSDFT_REC_L0 + c];
+          m[p][c] = (cP * L) * (y * y);
+          g[p][c] = L * b;
+          h[p][c] = L + b;
+        }
+        qk[p] = k + p < cnt ? rr[GSDFT_REC_QK] : 0.0;
+        coul[p] = 0.0;
+      }
+#pragma unroll
+      for (int n = 0; n < GSDFT_NQUAD; ++n) {
+        const double t2 = kQuadT2[n];
+#pragma unroll
+        for (int p = 0; p < kFwNP; ++p) {
+          const double G0 = fma(t2, h[p][0], g[p][0]);
+          const double G1 = fma(t2, h[p][1], g[p][1]);
+          const double G2 = fma(t2, h[p][2], g[p][2]);
+          const double p12 = G1 * G2;
+          const double prod = G0 * p12;
+          const double num = fma(m[p][0], p12, G0 * fma(m[p][1], G2, m[p][2] * G1));
+          const double y = rsqrt_pos(prod);
+          const double inv = y * y;
+          const double e = exp2_nonpos((num * inv) * t2);
+          coul[p] = fma(kQuadW[n] * y, e, coul[p]);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < kFwNP; ++p) acc = fma(qk[p], coul[p], acc);
+    }
+    __syncthreads();  // every thread is done with this buffer
+    if (threadIdx.x == 0 && t + 2 < ntiles) issue(t + 2);
+  }
+  if (has_aux) partial[blockIdx.y * n_aux + P] = ok ? acc * KN[P] : __longlong_as_double(-1LL);
+}
+
+// gamma_P = sum_s partial[s][P], fixed order.
+__global__ void sum_splits_kernel(const double* __restrict__ partial, int S, int64_t n,
+                                  double* __restrict__ out) {
+  int64_t P = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (P >= n) return;
+  double acc = 0.0;
+  for (int s = 0; s < S; ++s) acc += partial[s * n + P];
+  out[P] = acc;
+}
+
+static int num_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// Pair splits for the forward grid: about 4 resident CTAs per SM over the aux tiles.
+static int forward_splits(int64_t n_live, int64_t n_aux) {
+  int64_t aux_tiles = (n_aux + kFwThreads - 1) / kFwThreads;
+  int64_t want = (int64_t)num_sms() * 4;
+  int64_t S = (want + aux_tiles - 1) / aux_tiles;
+  int64_t max_s = (n_live + kFwTile - 1) / kFwTile;
+  if (S > max_s) S = max_s;
+  if (S < 1) S = 1;
+  if (S > 4096) S = 4096;
+  return (int)S;
+}
+
+}  // namespace gsdft
+
+using namespace gsdft;
+
+namespace gsdft {
+int device_status_forward(int* out, int clear) {
+  GSDFT_CUDA(cudaMemcpyFromSymbol(out, g_device_status, sizeof(int)));
+  if (clear) {
+    int z = 0;
+    GSDFT_CUDA(cudaMemcpyToSymbol(g_device_status, &z, sizeof(int)));
+  }
+  return GSDFT_OK;
+}
+int device_status_vjp(int* out, int clear);
+}  // namespace gsdft
+
+extern "C" int gsdft_device_status(int* status_host, int clear) {
+  GSDFT_REQUIRE(status_host, "null pointer");
+  GSDFT_CUDA(cudaDeviceSynchronize());
+  int a = 0, b = 0;
+  int rc = device_status_forward(&a, clear);
+  if (rc) return rc;
+  rc = device_status_vjp(&b, clear);
+  if (rc) return rc;
+  *status_host = a | b;
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_pair_prep(const double* A9, const double* mu, const double* N, int64_t M,
+                               const int32_t* pi, const int32_t* pj, const double* w,
+                               const int32_t* live_idx, int64_t n_live, const double* C_occ,
+                               const double* occ, int64_t n_occ, double* rec,
+                               gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_live >= 0 && n_occ >= 0, "bad sizes");
+  if (n_live == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(A9 && mu && N && pi && pj && w && live_idx && rec, "null pointer");
+  GSDFT_REQUIRE(n_occ == 0 || (C_occ && occ), "null C_occ/occ");
+  GSDFT_REQUIRE((reinterpret_cast<uintptr_t>(rec) & 15) == 0, "rec must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  pair_prep_kernel<<<grid_1d(n_live, 128), 128, 0, st>>>(A9, mu, N, pi, pj, live_idx, n_live, rec);
+  GSDFT_LAUNCHED("pair_prep");
+  pair_density_kernel<<<grid_1d(n_live * 32, 256), 256, 0, st>>>(pi, pj, w, live_idx, n_live,
+                                                                 C_occ, occ, n_occ, rec);
+  GSDFT_LAUNCHED("pair_density");
+  return GSDFT_OK;
+}
+
+extern "C" size_t gsdft_j_forward_workspace_size(int64_t n_live, int64_t n_aux) {
+  int S = forward_splits(n_live, n_aux);
+  return align_up((size_t)S * n_aux * sizeof(double), 256) + 256;
+}
+
+extern "C" int gsdft_j_forward(const double* rec, int64_t n_live, const double* beta,
+                               const double* R, const double* KN, int64_t n_aux, double* gamma,
+                               void* ws, size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31), "bad sizes");
+  GSDFT_REQUIRE(beta && R && KN && gamma, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n_live == 0) {
+    GSDFT_CUDA(cudaMemsetAsync(gamma, 0, n_aux * sizeof(double), st));
+    return GSDFT_OK;
+  }
+  GSDFT_REQUIRE(rec && (reinterpret_cast<uintptr_t>(rec) & 15) == 0, "rec must be 16-byte aligned");
+  int S = forward_splits(n_live, n_aux);
+  Carver c(ws, ws_bytes);
+  double* partial = c.take<double>((size_t)S * n_aux);
+  if (!c.ok) return fail(GSDFT_ERR_ARG, "forward workspace too small (%zu < %zu)", ws_bytes, c.off);
+  int64_t per_split = (n_live + S - 1) / S;
+  per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
+  dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
+  j_forward_kernel<<<grid, kFwThreads, 0, st>>>(rec, n_live, beta, R, KN, n_aux, per_split, partial);
+  GSDFT_LAUNCHED("j_forward");
+  sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(partial, S, n_aux, gamma);
+  GSDFT_LAUNCHED("sum_splits");
+  return GSDFT_OK;
+}

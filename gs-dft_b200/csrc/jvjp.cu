@@ -1,0 +1,466 @@
+// Reverse pass of the RI-J energy E = 1/2 gamma^T (V + lam I)^-1 gamma with respect to the splat
+// quantities, aux frozen. With dbar_P = g_E d_P and per node
+//   f = w det(G)^(-1/2) exp(-t^2 beta d^T A_hat G^-1 d),  G = (beta+t^2) A_hat + t^2 beta I,
+//   df/dA_hat = f (-1/2 (beta+t^2) G^-1 - t^4 beta^2 z z^T),   df/dP = 2 t^2 beta f A_hat z,  z = G^-1 d,
+// evaluated in the eigenframe of A_hat (where G is diagonal). This avoids the 1/(lam_i - lam_j)
+// terms of an eigh VJP. Reference for the quantities being differentiated: gs_dft/coulomb/ri.py
+// :126-222 (block, nodes, nodes_bwd), :436-494 (gamma, solve); gs_dft/coulomb/stream.py:203-215
+// (pair quantities); gs_dft/coulomb/ri.py:456 (q).
+#include "common.cuh"
+
+namespace gsdft {
+
+constexpr int kAuxRec = 8;        // [beta, -log2e beta, R0, R1, R2, dbar KN, beta^2, 0]
+constexpr int kVjpThreads = 128;  // pairs per CTA (one per thread)
+constexpr int kVjpTile = 64;      // aux records per staged tile (64 x 64 B)
+
+__global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const double* __restrict__ R,
+                                    const double* __restrict__ KN, const double* __restrict__ d,
+                                    const double* __restrict__ gE, int64_t n,
+                                    double* __restrict__ out) {
+  int64_t P = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (P >= n) return;
+  double b = beta[P];
+  double g = gE ? gE[0] : 1.0;
+  double* o = out + P * kAuxRec;
+  o[0] = b;
+  o[1] = -kLog2e * b;
+  o[2] = R[3 * P];
+  o[3] = R[3 * P + 1];
+  o[4] = R[3 * P + 2];
+  o[5] = (g * d[P]) * KN[P];
+  o[6] = b * b;
+  o[7] = 0.0;
+}
+
+__global__ void __launch_bounds__(kVjpThreads)
+    j_vjp_kernel(const double* __restrict__ rec, int64_t n_live, const double* __restrict__ auxr,
+                 int64_t n_aux, int64_t per_split, double* __restrict__ out) {
+  __shared__ __align__(128) double tile[2][kVjpTile * kAuxRec];
+  __shared__ __align__(8) uint64_t bar[2];
+  const int64_t a = blockIdx.x * (int64_t)kVjpThreads + threadIdx.x;
+  const bool live = a < n_live;
+  const int64_t aa = live ? a : 0;
+  const double* rr = rec + aa * GSDFT_REC_FIELDS;
+  double L[3], U[9], Pc[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) L[k] = live ? rr[GSDFT_REC_L0 + k] : 1.0;
+#pragma unroll
+  for (int k = 0; k < 9; ++k) U[k] = live ? rr[GSDFT_REC_U00 + k] : (k % 4 == 0 ? 1.0 : 0.0);
+#pragma unroll
+  for (int k = 0; k < 3; ++k) Pc[k] = live ? rr[GSDFT_REC_P0 + k] : 0.0;
+
+  const int64_t P0 = blockIdx.y * per_split;
+  const int64_t P1 = imin64(P0 + per_split, n_aux);
+  const int64_t naux = P1 > P0 ? P1 - P0 : 0;
+  const int ntiles = (int)((naux + kVjpTile - 1) / kVjpTile);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+  }
+  __syncthreads();
+  auto issue = [&](int t) {
+    int64_t s = P0 + (int64_t)t * kVjpTile;
+    int cnt = (int)imin64(kVjpTile, P1 - s);
+    uint32_t bytes = (uint32_t)cnt * kAuxRec * sizeof(double);
+    fence_proxy_async();
+    mbar_expect_tx(&bar[t & 1], bytes);
+    bulk_g2s(tile[t & 1], auxr + s * kAuxRec, bytes, &bar[t & 1]);
+  };
+  if (threadIdx.x == 0) {
+    if (ntiles > 0) issue(0);
+    if (ntiles > 1) issue(1);
+  }
+
+  double SJ = 0.0, SD[3] = {0, 0, 0}, SV[3] = {0, 0, 0}, SZ[6] = {0, 0, 0, 0, 0, 0};
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    ok = __syncthreads_and(mbar_wait(&bar[t & 1], (t >> 1) & 1));
+    if (!ok) break;
+    const double* tl = tile[t & 1];
+    const int cnt = (int)imin64(kVjpTile, P1 - (P0 + (int64_t)t * kVjpTile));
+    for (int k = 0; k < cnt; ++k) {
+      const double* ar = tl + k * kAuxRec;
+      const double b = ar[0], cP = ar[1], dk = ar[5], b2 = ar[6];
+      const double d0 = ar[2] - Pc[0], d1 = ar[3] - Pc[1], d2 = ar[4] - Pc[2];
+      double y[3], m[3], g[3], h[3];
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        y[c] = U[c] * d0 + U[3 + c] * d1 + U[6 + c] * d2;
+        m[c] = (cP * L[c]) * (y[c] * y[c]);
+        g[c] = L[c] * b;
+        h[c] = L[c] + b;
+      }
+      double cf = 0.0, B[3] = {0, 0, 0}, C[3] = {0, 0, 0}, Z[6] = {0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int n = 0; n < GSDFT_NQUAD; ++n) {
+        const double t2 = kQuadT2[n], t4 = kQuadT4[n];
+        const double G0 = fma(t2, h[0], g[0]);
+        const double G1 = fma(t2, h[1], g[1]);
+        const double G2 = fma(t2, h[2], g[2]);
+        const double p12 = G1 * G2, p02 = G0 * G2, p01 = G0 * G1;
+        const double prod = G0 * p12;
+        const double num = fma(m[0], p12, fma(m[1], p02, m[2] * p01));
+        const double yy = rsqrt_pos(prod);
+        const double inv = yy * yy;
+        const double e = exp2_nonpos((num * inv) * t2);
+        const double f = (kQuadW[n] * yy) * e;
+        cf += f;
+        const double iG0 = p12 * inv, iG1 = p02 * inv, iG2 = p01 * inv;
+        const double g0 = f * iG0, g1 = f * iG1, g2 = f * iG2;
+        B[0] += g0;
+        B[1] += g1;
+        B[2] += g2;
+        C[0] = fma(t2, g0, C[0]);
+        C[1] = fma(t2, g1, C[1]);
+        C[2] = fma(t2, g2, C[2]);
+        const double h0 = t4 * g0, h1 = t4 * g1, h2 = t4 * g2;
+        Z[0] = fma(h0, iG0, Z[0]);
+        Z[1] = fma(h1, iG1, Z[1]);
+        Z[2] = fma(h2, iG2, Z[2]);
+        Z[3] = fma(h0, iG1, Z[3]);
+        Z[4] = fma(h0, iG2, Z[4]);
+        Z[5] = fma(h1, iG2, Z[5]);
+      }
+      SJ = fma(dk, cf, SJ);
+      const double dkb = dk * b, dkb2 = dk * b2;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        SD[c] = fma(dk, fma(b, B[c], C[c]), SD[c]);
+        SV[c] = fma(dkb, y[c] * C[c], SV[c]);
+      }
+      SZ[0] = fma(dkb2, (y[0] * y[0]) * Z[0], SZ[0]);
+      SZ[1] = fma(dkb2, (y[1] * y[1]) * Z[1], SZ[1]);
+      SZ[2] = fma(dkb2, (y[2] * y[2]) * Z[2], SZ[2]);
+      SZ[3] = fma(dkb2, (y[0] * y[1]) * Z[3], SZ[3]);
+      SZ[4] = fma(dkb2, (y[0] * y[2]) * Z[4], SZ[4]);
+      SZ[5] = fma(dkb2, (y[1] * y[2]) * Z[5], SZ[5]);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && t + 2 < ntiles) issue(t + 2);
+  }
+  if (live) {
+    double* o = out + ((int64_t)blockIdx.y * n_live + a) * GSDFT_VJP_FIELDS;
+    const double bad = __longlong_as_double(-1LL);
+    o[GSDFT_VJP_SJ] = ok ? SJ : bad;
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      o[GSDFT_VJP_SD0 + c] = ok ? SD[c] : bad;
+      o[GSDFT_VJP_SV0 + c] = ok ? SV[c] : bad;
+    }
+#pragma unroll
+    for (int c = 0; c < 6; ++c) o[GSDFT_VJP_SZ00 + c] = ok ? SZ[c] : bad;
+  }
+}
+
+__global__ void sum_vjp_splits_kernel(const double* __restrict__ part, int S, int64_t n,
+                                      double* __restrict__ out) {
+  int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  int64_t tot = n * GSDFT_VJP_FIELDS;
+  if (k >= tot) return;
+  double acc = 0.0;
+  for (int s = 0; s < S; ++s) acc += part[s * tot + k];
+  out[k] = acc;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Chain: per-pair sums -> cotangents of (A_hat, P, KN) -> per-side (A, mu, N) contributions.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void sym6_add_outer(double* s6, double c, const double* u,
+                                               const double* v) {
+  // s6 += c * sym(u v^T), [xx,yy,zz,xy,xz,yz]
+  s6[0] += c * u[0] * v[0];
+  s6[1] += c * u[1] * v[1];
+  s6[2] += c * u[2] * v[2];
+  s6[3] += c * 0.5 * (u[0] * v[1] + u[1] * v[0]);
+  s6[4] += c * 0.5 * (u[0] * v[2] + u[2] * v[0]);
+  s6[5] += c * 0.5 * (u[1] * v[2] + u[2] * v[1]);
+}
+
+__global__ void pair_chain_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
+                                  const double* __restrict__ N, const int32_t* __restrict__ pi,
+                                  const int32_t* __restrict__ pj,
+                                  const int32_t* __restrict__ live_idx, int64_t n_live,
+                                  const double* __restrict__ rec, const double* __restrict__ sums,
+                                  double* __restrict__ side, double* __restrict__ J) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_live) return;
+  const double* r = rec + a * GSDFT_REC_FIELDS;
+  const double* sm = sums + a * GSDFT_VJP_FIELDS;
+  const int64_t e = live_idx[a];
+  const int i = pi[e], j = pj[e];
+  const double q = r[GSDFT_REC_Q], kn = r[GSDFT_REC_KN], qk = r[GSDFT_REC_QK];
+  const double SJ = sm[GSDFT_VJP_SJ];
+  J[e] = kn * SJ;
+  const double KNbar = q * kPref * SJ;
+  // eigenframe cotangent of A_hat: M_kl = -qk SZ_kl - 1/2 qk SD_k delta_kl
+  double Mm[3][3];
+  Mm[0][0] = -qk * sm[GSDFT_VJP_SZ00] - 0.5 * qk * sm[GSDFT_VJP_SD0];
+  Mm[1][1] = -qk * sm[GSDFT_VJP_SZ11] - 0.5 * qk * sm[GSDFT_VJP_SD1];
+  Mm[2][2] = -qk * sm[GSDFT_VJP_SZ22] - 0.5 * qk * sm[GSDFT_VJP_SD2];
+  Mm[0][1] = Mm[1][0] = -qk * sm[GSDFT_VJP_SZ01];
+  Mm[0][2] = Mm[2][0] = -qk * sm[GSDFT_VJP_SZ02];
+  Mm[1][2] = Mm[2][1] = -qk * sm[GSDFT_VJP_SZ12];
+  double U[3][3], L[3], Pe[3];
+  for (int rr = 0; rr < 3; ++rr)
+    for (int c = 0; c < 3; ++c) U[rr][c] = r[GSDFT_REC_U00 + 3 * rr + c];
+  for (int k = 0; k < 3; ++k) {
+    L[k] = r[GSDFT_REC_L0 + k];
+    Pe[k] = 2.0 * qk * L[k] * sm[GSDFT_VJP_SV0 + k];
+  }
+  // Abar = U M U^T (symmetric), Pbar = U Pe
+  double UM[3][3];
+  for (int rr = 0; rr < 3; ++rr)
+    for (int c = 0; c < 3; ++c) UM[rr][c] = U[rr][0] * Mm[0][c] + U[rr][1] * Mm[1][c] + U[rr][2] * Mm[2][c];
+  double Ab[3][3];
+  for (int rr = 0; rr < 3; ++rr)
+    for (int c = 0; c < 3; ++c) Ab[rr][c] = UM[rr][0] * U[c][0] + UM[rr][1] * U[c][1] + UM[rr][2] * U[c][2];
+  double Pb[3];
+  for (int rr = 0; rr < 3; ++rr) Pb[rr] = U[rr][0] * Pe[0] + U[rr][1] * Pe[1] + U[rr][2] * Pe[2];
+
+  double Ai[9], Aj[9], mui[3], muj[3];
+  for (int k = 0; k < 9; ++k) {
+    Ai[k] = A9[9 * (int64_t)i + k];
+    Aj[k] = A9[9 * (int64_t)j + k];
+  }
+  for (int k = 0; k < 3; ++k) {
+    mui[k] = mu[3 * (int64_t)i + k];
+    muj[k] = mu[3 * (int64_t)j + k];
+  }
+  double Ah[9], adj[9];
+  for (int k = 0; k < 9; ++k) Ah[k] = Ai[k] + Aj[k];
+  adj3_rn(Ah, adj);
+  const double idet = 1.0 / det3_rn(Ah);
+  auto ahinv = [&](const double* x, double* out3) {
+    for (int k = 0; k < 3; ++k)
+      out3[k] = (adj[3 * k] * x[0] + adj[3 * k + 1] * x[1] + adj[3 * k + 2] * x[2]) * idet;
+  };
+  const double P[3] = {r[GSDFT_REC_P0], r[GSDFT_REC_P1], r[GSDFT_REC_P2]};
+  double v[3];
+  ahinv(Pb, v);
+  // sym(A_hat bar) = Abar - sym(v P^T)
+  double gAi[6] = {Ab[0][0], Ab[1][1], Ab[2][2], Ab[0][1], Ab[0][2], Ab[1][2]};
+  sym6_add_outer(gAi, -1.0, v, P);
+  double gAj[6];
+  for (int k = 0; k < 6; ++k) gAj[k] = gAi[k];
+  sym6_add_outer(gAi, 1.0, v, mui);
+  sym6_add_outer(gAj, 1.0, v, muj);
+  double gmui[3], gmuj[3];
+  for (int k = 0; k < 3; ++k) {
+    gmui[k] = Ai[k] * v[0] + Ai[3 + k] * v[1] + Ai[6 + k] * v[2];
+    gmuj[k] = Aj[k] * v[0] + Aj[3 + k] * v[1] + Aj[6 + k] * v[2];
+  }
+  // KN = N_i N_j exp(-d^T A_i A_hat^-1 A_j d)
+  const double dd[3] = {mui[0] - muj[0], mui[1] - muj[1], mui[2] - muj[2]};
+  double Ajd[3], ev[3], fv[3], Hd[3];
+  for (int k = 0; k < 3; ++k) Ajd[k] = Aj[3 * k] * dd[0] + Aj[3 * k + 1] * dd[1] + Aj[3 * k + 2] * dd[2];
+  ahinv(Ajd, ev);
+  for (int k = 0; k < 3; ++k) fv[k] = dd[k] - ev[k];
+  for (int k = 0; k < 3; ++k) Hd[k] = Ai[3 * k] * ev[0] + Ai[3 * k + 1] * ev[1] + Ai[3 * k + 2] * ev[2];
+  const double K = exp(-(dd[0] * Hd[0] + dd[1] * Hd[1] + dd[2] * Hd[2]));
+  const double Ni = N[i], Nj = N[j];
+  const double KNv = Ni * Nj * K;
+  const double gNi = KNbar * Nj * K, gNj = KNbar * Ni * K;
+  const double Qbar = -KNbar * KNv;
+  for (int k = 0; k < 3; ++k) {
+    gmui[k] += 2.0 * Qbar * Hd[k];
+    gmuj[k] -= 2.0 * Qbar * Hd[k];
+  }
+  sym6_add_outer(gAi, Qbar, ev, ev);
+  sym6_add_outer(gAj, Qbar, fv, fv);
+  double* o = side + a * GSDFT_SIDE_FIELDS;
+  for (int k = 0; k < 6; ++k) {
+    o[k] = gAi[k];
+    o[10 + k] = gAj[k];
+  }
+  for (int k = 0; k < 3; ++k) {
+    o[6 + k] = gmui[k];
+    o[16 + k] = gmuj[k];
+  }
+  o[9] = gNi;
+  o[19] = gNj;
+}
+
+// One warp per splat: the i-side contributions of its pi-segment plus the j-side contributions of
+// its pj-segment, lanes striding the segments, then a fixed-order warp reduction.
+__global__ void splat_reduce_kernel(const double* __restrict__ side,
+                                    const int32_t* __restrict__ order_i,
+                                    const int64_t* __restrict__ seg_i,
+                                    const int32_t* __restrict__ order_j,
+                                    const int64_t* __restrict__ seg_j, int64_t M,
+                                    double* __restrict__ gA6, double* __restrict__ gmu,
+                                    double* __restrict__ gN) {
+  int64_t s = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  int lane = threadIdx.x & 31;
+  if (s >= M) return;
+  double acc[10];
+#pragma unroll
+  for (int k = 0; k < 10; ++k) acc[k] = 0.0;
+  for (int64_t e = seg_i[s] + lane; e < seg_i[s + 1]; e += 32) {
+    const double* o = side + (int64_t)order_i[e] * GSDFT_SIDE_FIELDS;
+#pragma unroll
+    for (int k = 0; k < 10; ++k) acc[k] += o[k];
+  }
+  for (int64_t e = seg_j[s] + lane; e < seg_j[s + 1]; e += 32) {
+    const double* o = side + (int64_t)order_j[e] * GSDFT_SIDE_FIELDS + 10;
+#pragma unroll
+    for (int k = 0; k < 10; ++k) acc[k] += o[k];
+  }
+#pragma unroll
+  for (int k = 0; k < 10; ++k)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], off);
+  if (lane == 0) {
+#pragma unroll
+    for (int k = 0; k < 6; ++k) gA6[6 * s + k] = acc[k];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) gmu[3 * s + k] = acc[6 + k];
+    gN[s] = acc[9];
+  }
+}
+
+// g_C[s, o] = occ_o (sum_{pi=s} J w C[pj, o] + sum_{pj=s} J w C[pi, o]); one block per splat row,
+// threads over o, segments walked in order.
+__global__ void density_grad_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                                    const double* __restrict__ w,
+                                    const int32_t* __restrict__ live_idx,
+                                    const double* __restrict__ J,
+                                    const int32_t* __restrict__ order_i,
+                                    const int64_t* __restrict__ seg_i,
+                                    const int32_t* __restrict__ order_j,
+                                    const int64_t* __restrict__ seg_j, const double* __restrict__ C,
+                                    const double* __restrict__ occ, int64_t n_occ,
+                                    double* __restrict__ gC) {
+  const int64_t s = blockIdx.x;
+  for (int64_t o = threadIdx.x; o < n_occ; o += blockDim.x) {
+    double acc = 0.0;
+    for (int64_t e = seg_i[s]; e < seg_i[s + 1]; ++e) {
+      int64_t l = live_idx[order_i[e]];
+      acc = fma(J[l] * w[l], C[(int64_t)pj[l] * n_occ + o], acc);
+    }
+    for (int64_t e = seg_j[s]; e < seg_j[s + 1]; ++e) {
+      int64_t l = live_idx[order_j[e]];
+      acc = fma(J[l] * w[l], C[(int64_t)pi[l] * n_occ + o], acc);
+    }
+    gC[s * n_occ + o] = occ[o] * acc;
+  }
+}
+
+static int vjp_num_sms() {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+// Aux splits so that the grid has about 4 CTAs per SM even when the pair tiles alone are few.
+static int vjp_splits(int64_t n_live, int64_t n_aux) {
+  int64_t tiles = (n_live + kVjpThreads - 1) / kVjpThreads;
+  int64_t want = (int64_t)vjp_num_sms() * 4;
+  int64_t S = (want + tiles - 1) / tiles;
+  int64_t max_s = (n_aux + kVjpTile - 1) / kVjpTile;
+  if (S > max_s) S = max_s;
+  if (S < 1) S = 1;
+  if (S > 64) S = 64;
+  return (int)S;
+}
+
+int device_status_vjp(int* out, int clear) {
+  GSDFT_CUDA(cudaMemcpyFromSymbol(out, g_device_status, sizeof(int)));
+  if (clear) {
+    int z = 0;
+    GSDFT_CUDA(cudaMemcpyToSymbol(g_device_status, &z, sizeof(int)));
+  }
+  return GSDFT_OK;
+}
+
+}  // namespace gsdft
+
+using namespace gsdft;
+
+extern "C" size_t gsdft_j_vjp_workspace_size(int64_t n_live, int64_t n_aux) {
+  int S = vjp_splits(n_live, n_aux);
+  Sizer z;
+  z.take<double>((size_t)n_aux * kAuxRec);
+  if (S > 1) z.take<double>((size_t)S * n_live * GSDFT_VJP_FIELDS);
+  return z.off + 256;
+}
+
+extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta, const double* R,
+                           const double* KN, const double* d, const double* g_E, int64_t n_aux,
+                           double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31), "bad sizes");
+  if (n_live == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(rec && beta && R && KN && d && sums, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  int S = vjp_splits(n_live, n_aux);
+  Carver c(ws, ws_bytes);
+  double* auxr = c.take<double>((size_t)n_aux * kAuxRec);
+  double* part = S > 1 ? c.take<double>((size_t)S * n_live * GSDFT_VJP_FIELDS) : sums;
+  if (!c.ok) return fail(GSDFT_ERR_ARG, "vjp workspace too small (%zu < %zu)", ws_bytes, c.off);
+  aux_vjp_pack_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(beta, R, KN, d, g_E, n_aux, auxr);
+  GSDFT_LAUNCHED("aux_vjp_pack");
+  int64_t per_split = (n_aux + S - 1) / S;
+  dim3 grid((unsigned)((n_live + kVjpThreads - 1) / kVjpThreads), (unsigned)S);
+  j_vjp_kernel<<<grid, kVjpThreads, 0, st>>>(rec, n_live, auxr, n_aux, per_split, part);
+  GSDFT_LAUNCHED("j_vjp");
+  if (S > 1) {
+    sum_vjp_splits_kernel<<<grid_1d(n_live * GSDFT_VJP_FIELDS, 256), 256, 0, st>>>(part, S, n_live,
+                                                                                   sums);
+    GSDFT_LAUNCHED("sum_vjp_splits");
+  }
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
+                                const int32_t* pi, const int32_t* pj, const int32_t* live_idx,
+                                int64_t n_live, int64_t n, const double* rec, const double* sums,
+                                double* side, double* J, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_live >= 0 && n >= n_live, "bad sizes");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n > 0) {
+    GSDFT_REQUIRE(J, "null J");
+    GSDFT_CUDA(cudaMemsetAsync(J, 0, n * sizeof(double), st));
+  }
+  if (n_live == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(A9 && mu && N && pi && pj && live_idx && rec && sums && side, "null pointer");
+  pair_chain_kernel<<<grid_1d(n_live, 128), 128, 0, st>>>(A9, mu, N, pi, pj, live_idx, n_live, rec,
+                                                          sums, side, J);
+  GSDFT_LAUNCHED("pair_chain");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_splat_reduce(const double* side, const int32_t* order_i, const int64_t* seg_i,
+                                  const int32_t* order_j, const int64_t* seg_j, int64_t n_live,
+                                  int64_t M, double* gA6, double* gmu, double* gN,
+                                  gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_live >= 0, "bad sizes");
+  GSDFT_REQUIRE(seg_i && seg_j && gA6 && gmu && gN, "null pointer");
+  GSDFT_REQUIRE(n_live == 0 || (side && order_i && order_j), "null pointer");
+  splat_reduce_kernel<<<grid_1d(M * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+      side, order_i, seg_i, order_j, seg_j, M, gA6, gmu, gN);
+  GSDFT_LAUNCHED("splat_reduce");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const double* w,
+                                  const int32_t* live_idx, const double* J, const int32_t* order_i,
+                                  const int64_t* seg_i, const int32_t* order_j,
+                                  const int64_t* seg_j, int64_t n_live, int64_t M,
+                                  const double* C_occ, const double* occ, int64_t n_occ,
+                                  double* g_C, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_live >= 0 && n_occ >= 0, "bad sizes");
+  if (n_occ == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(seg_i && seg_j && C_occ && occ && g_C, "null pointer");
+  GSDFT_REQUIRE(n_live == 0 || (pi && pj && w && live_idx && J && order_i && order_j),
+                "null pointer");
+  int threads = n_occ >= 256 ? 256 : (int)((n_occ + 31) / 32 * 32);
+  density_grad_kernel<<<(unsigned)M, threads, 0, (cudaStream_t)stream>>>(
+      pi, pj, w, live_idx, J, order_i, seg_i, order_j, seg_j, C_occ, occ, n_occ, g_C);
+  GSDFT_LAUNCHED("density_grad");
+  return GSDFT_OK;
+}

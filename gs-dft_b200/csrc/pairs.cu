@@ -1,0 +1,434 @@
+// Significant-pair list on the GPU: |S_ij| > eps over all M^2 ordered candidates, compacted in
+// lexsorted (flat i*M+j ascending) order, padded to pad_to; overflow keeps the pad_to largest |S|.
+// Reference: gs_dft/screening/pairs.py:50-164 (builders), :225-315 (neighbor_pairs), :318-322
+// (weights), :342-345 (overlap); gs_dft/ks/shard.py:146-166 (stripe_pairs).
+//
+// The overlap of a pair is evaluated once per unordered pair, in the (min, max) orientation, with
+// FMA contraction disabled and the reference's operation order, and shared by (i,j) and (j,i).
+#include <cub/cub.cuh>
+#include <thrust/iterator/counting_iterator.h>
+
+#include "common.cuh"
+
+namespace gsdft {
+
+constexpr int kRowThreads = 256;
+constexpr double kPi15 = 5.568327996831708;  // pi ** 1.5 as the reference's float computes it
+
+__device__ __forceinline__ double abs_overlap(const double* __restrict__ A9,
+                                              const double* __restrict__ mu,
+                                              const double* __restrict__ N, int i, int j) {
+  int lo = min(i, j), hi = max(i, j);
+  double Ai[9], Aj[9], mui[3], muj[3];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    Ai[k] = A9[9 * (int64_t)lo + k];
+    Aj[k] = A9[9 * (int64_t)hi + k];
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    mui[k] = mu[3 * (int64_t)lo + k];
+    muj[k] = mu[3 * (int64_t)hi + k];
+  }
+  double Ah[9], P[3], KN, det;
+  pair_quantities_rn(Ai, Aj, mui, muj, N[lo], N[hi], Ah, P, &KN, &det);
+  return fabs(__ddiv_rn(DM(KN, kPi15), __dsqrt_rn(det)));
+}
+
+// Per-row count of significant columns (j >= i when unique).
+__global__ void pairs_count_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
+                                   const double* __restrict__ N, int M, double eps, int unique,
+                                   int64_t* __restrict__ row_count) {
+  int i = blockIdx.x;
+  int j0 = unique ? i : 0;
+  int cnt = 0;
+  for (int j = j0 + threadIdx.x; j < M; j += blockDim.x)
+    cnt += abs_overlap(A9, mu, N, i, j) > eps ? 1 : 0;
+  typedef cub::BlockReduce<int, kRowThreads> BR;
+  __shared__ typename BR::TempStorage tmp;
+  int tot = BR(tmp).Sum(cnt);
+  if (threadIdx.x == 0) row_count[i] = tot;
+}
+
+// Ordered write of row i's significant columns at row_off[i]. Direct mode writes (pi,pj,w);
+// ranking mode writes (flat index, |S|) for the overflow selection.
+__global__ void pairs_build_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
+                                   const double* __restrict__ N, int M, double eps, int unique,
+                                   const int64_t* __restrict__ row_off, int ranking,
+                                   int32_t* __restrict__ pi, int32_t* __restrict__ pj,
+                                   double* __restrict__ w, int64_t* __restrict__ flat,
+                                   double* __restrict__ val) {
+  int i = blockIdx.x;
+  int j0 = unique ? i : 0;
+  typedef cub::BlockScan<int, kRowThreads> BS;
+  __shared__ typename BS::TempStorage tmp;
+  __shared__ int s_total;
+  int64_t base = row_off[i];
+  for (int jb = j0; jb < M; jb += kRowThreads) {
+    int j = jb + threadIdx.x;
+    double s = 0.0;
+    int sig = 0;
+    if (j < M) {
+      s = abs_overlap(A9, mu, N, i, j);
+      sig = s > eps ? 1 : 0;
+    }
+    int rank, total;
+    BS(tmp).ExclusiveSum(sig, rank, total);
+    if (sig) {
+      int64_t pos = base + rank;
+      if (ranking) {
+        flat[pos] = (int64_t)i * M + j;
+        val[pos] = s;
+      } else {
+        pi[pos] = i;
+        pj[pos] = j;
+        w[pos] = unique ? (i == j ? 1.0 : 2.0) : 1.0;
+      }
+    }
+    if (threadIdx.x == 0) s_total = total;
+    __syncthreads();
+    base += s_total;
+    __syncthreads();
+  }
+}
+
+__global__ void fill_pad_kernel(int64_t start, int64_t n, int32_t* pi, int32_t* pj, double* w) {
+  int64_t k = start + blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  pi[k] = 0;
+  pj[k] = 0;
+  w[k] = 0.0;
+}
+
+__global__ void decode_flat_kernel(const int64_t* __restrict__ flat, int64_t n, int M, int unique,
+                                   int32_t* pi, int32_t* pj, double* w) {
+  int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  int64_t f = flat[k];
+  int i = (int)(f / M), j = (int)(f % M);
+  pi[k] = i;
+  pj[k] = j;
+  w[k] = unique ? (i == j ? 1.0 : 2.0) : 1.0;
+}
+
+// |S| > 0 doubles order like their bit patterns as unsigned integers.
+__global__ void val_bits_kernel(const double* __restrict__ val, int64_t n, uint64_t* bits) {
+  int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (k < n) bits[k] = (uint64_t)__double_as_longlong(val[k]);
+}
+
+__global__ void stripe_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                              const double* __restrict__ w, int64_t n, int G, int32_t* pio,
+                              int32_t* pjo, double* wo) {
+  int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (k >= n) return;
+  int64_t d = n / G;
+  int64_t g = k / d, j = k % d;       // new[g*d + j] = old[j*G + g]
+  int64_t src = j * G + g;
+  pio[k] = pi[src];
+  pjo[k] = pj[src];
+  wo[k] = w[src];
+}
+
+// ------------------------------------------------------------------------------------------------
+// Pair plan helpers
+// ------------------------------------------------------------------------------------------------
+__global__ void live_flags_kernel(const double* __restrict__ w, int64_t n, char* flags) {
+  int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (k < n) flags[k] = w[k] != 0.0;
+}
+
+__global__ void gather_keys_kernel(const int32_t* __restrict__ key, const int32_t* __restrict__ live,
+                                   int64_t n_live, int32_t* __restrict__ out,
+                                   int32_t* __restrict__ iota) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_live) return;
+  out[a] = key[live[a]];
+  iota[a] = (int32_t)a;
+}
+
+// seg[s] = first position in the sorted keys with key >= s, s in [0, M].
+__global__ void segment_bounds_kernel(const int32_t* __restrict__ sorted, int64_t n, int64_t M,
+                                      int64_t* __restrict__ seg) {
+  int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (s > M) return;
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    int64_t mid = (lo + hi) >> 1;
+    if (sorted[mid] < s) lo = mid + 1; else hi = mid;
+  }
+  seg[s] = lo;
+}
+
+static int end_bit_for(int64_t M) {
+  int b = 1;
+  while (b < 31 && (int64_t(1) << b) <= M) ++b;
+  return b;
+}
+
+struct PairsWs {
+  int64_t* row_count;
+  int64_t* row_off;
+  void* scan_tmp;
+  size_t scan_bytes;
+  int64_t* flat;
+  double* val;
+  uint64_t* bits;
+  uint64_t* bits_sorted;
+  int64_t* flat_sorted;
+  int64_t* keep;
+  int64_t* keep_sorted;
+  void* sort_tmp;
+  size_t sort_bytes;
+};
+
+template <class C>
+static void layout_pairs_ws(C& c, int64_t M, int64_t pad_to, PairsWs* p, size_t scan_bytes,
+                            size_t sort_bytes) {
+  int64_t cap = 2 * (pad_to > 0 ? pad_to : 0);
+  auto rc = c.template take<int64_t>(M + 1);
+  auto ro = c.template take<int64_t>(M + 1);
+  auto st = c.template take<char>(scan_bytes);
+  auto fl = c.template take<int64_t>(cap + 1);
+  auto va = c.template take<double>(cap + 1);
+  auto bi = c.template take<uint64_t>(cap + 1);
+  auto bs = c.template take<uint64_t>(cap + 1);
+  auto fs = c.template take<int64_t>(cap + 1);
+  auto ke = c.template take<int64_t>(cap + 1);
+  auto ks = c.template take<int64_t>(cap + 1);
+  auto so = c.template take<char>(sort_bytes);
+  if (p) {
+    *p = PairsWs{(int64_t*)rc, (int64_t*)ro, st, scan_bytes, (int64_t*)fl, (double*)va,
+                 (uint64_t*)bi, (uint64_t*)bs, (int64_t*)fs, (int64_t*)ke, (int64_t*)ks, so,
+                 sort_bytes};
+  }
+}
+
+// Sizer::take returns void; wrap so both carve paths share one layout routine.
+struct SizerP {
+  Sizer s;
+  template <class T>
+  T* take(size_t n) {
+    s.take<T>(n);
+    return nullptr;
+  }
+};
+
+static void cub_sizes(int64_t M, int64_t pad_to, size_t* scan_bytes, size_t* sort_bytes) {
+  size_t sb = 0;
+  cub::DeviceScan::ExclusiveSum(nullptr, sb, (int64_t*)nullptr, (int64_t*)nullptr, (int)(M + 1));
+  int64_t cap = 2 * (pad_to > 0 ? pad_to : 0);
+  size_t s1 = 0, s2 = 0;
+  if (cap > 0) {
+    cub::DeviceRadixSort::SortPairsDescending(nullptr, s1, (uint64_t*)nullptr, (uint64_t*)nullptr,
+                                              (int64_t*)nullptr, (int64_t*)nullptr, (int)cap);
+    cub::DeviceRadixSort::SortKeys(nullptr, s2, (int64_t*)nullptr, (int64_t*)nullptr, (int)cap);
+  }
+  *scan_bytes = sb;
+  *sort_bytes = s1 > s2 ? s1 : s2;
+}
+
+}  // namespace gsdft
+
+using namespace gsdft;
+
+extern "C" size_t gsdft_pairs_workspace_size(int64_t M, int64_t pad_to) {
+  size_t sb, so;
+  cub_sizes(M, pad_to, &sb, &so);
+  SizerP z;
+  layout_pairs_ws(z, M, pad_to, nullptr, sb, so);
+  return z.s.off + 256;
+}
+
+static int pairs_counts(const double* A9, const double* mu, const double* N, int64_t M,
+                        double eps, int unique, const PairsWs& ws, int64_t* n_sig_host,
+                        cudaStream_t st) {
+  pairs_count_kernel<<<(int)M, kRowThreads, 0, st>>>(A9, mu, N, (int)M, eps, unique,
+                                                       ws.row_count);
+  GSDFT_LAUNCHED("pairs_count");
+  GSDFT_CUDA(cudaMemsetAsync(ws.row_count + M, 0, sizeof(int64_t), st));
+  size_t sb = ws.scan_bytes;
+  GSDFT_CUDA(cub::DeviceScan::ExclusiveSum(ws.scan_tmp, sb, ws.row_count, ws.row_off,
+                                           (int)(M + 1), st));
+  GSDFT_CUDA(cudaMemcpyAsync(n_sig_host, ws.row_off + M, sizeof(int64_t), cudaMemcpyDeviceToHost,
+                             st));
+  GSDFT_CUDA(cudaStreamSynchronize(st));
+  return GSDFT_OK;
+}
+
+static int carve_pairs_ws(void* ws, size_t ws_bytes, int64_t M, int64_t pad_to, PairsWs* p) {
+  size_t sb, so;
+  cub_sizes(M, pad_to, &sb, &so);
+  Carver c(ws, ws_bytes);
+  layout_pairs_ws(c, M, pad_to, p, sb, so);
+  if (!c.ok)
+    return fail(GSDFT_ERR_ARG, "pairs workspace too small: need %zu bytes, got %zu", c.off,
+                ws_bytes);
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_pairs_count(const double* A9, const double* mu, const double* N, int64_t M,
+                                 double eps, int unique, int64_t* n_sig_host, void* ws,
+                                 size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && M < (int64_t(1) << 31), "M out of range");
+  GSDFT_REQUIRE(A9 && mu && N && n_sig_host, "null pointer");
+  PairsWs p;
+  int rc = carve_pairs_ws(ws, ws_bytes, M, 0, &p);
+  if (rc) return rc;
+  return pairs_counts(A9, mu, N, M, eps, unique, p, n_sig_host, (cudaStream_t)stream);
+}
+
+extern "C" int gsdft_pairs_build(const double* A9, const double* mu, const double* N, int64_t M,
+                                 double eps, int unique, int64_t pad_to, int32_t* pi, int32_t* pj,
+                                 double* w, int64_t* n_sig_host, void* ws, size_t ws_bytes,
+                                 gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && M < (int64_t(1) << 31), "M out of range");
+  GSDFT_REQUIRE(pad_to >= 0 && pad_to < (int64_t(1) << 31), "pad_to out of range");
+  GSDFT_REQUIRE(A9 && mu && N && n_sig_host, "null pointer");
+  GSDFT_REQUIRE(pad_to == 0 || (pi && pj && w), "null output pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  PairsWs p;
+  int rc = carve_pairs_ws(ws, ws_bytes, M, pad_to, &p);
+  if (rc) return rc;
+  rc = pairs_counts(A9, mu, N, M, eps, unique, p, n_sig_host, st);
+  if (rc) return rc;
+  int64_t n_sig = *n_sig_host;
+  if (n_sig <= pad_to) {
+    pairs_build_kernel<<<(int)M, kRowThreads, 0, st>>>(A9, mu, N, (int)M, eps, unique, p.row_off,
+                                                         0, pi, pj, w, nullptr, nullptr);
+    GSDFT_LAUNCHED("pairs_build");
+    if (pad_to > n_sig) {
+      fill_pad_kernel<<<grid_1d(pad_to - n_sig, 256), 256, 0, st>>>(n_sig, pad_to, pi, pj, w);
+      GSDFT_LAUNCHED("fill_pad");
+    }
+    return GSDFT_OK;
+  }
+  if (n_sig > 2 * pad_to)
+    return fail(GSDFT_ERR_OVERFLOW,
+                "neighbor_pairs: %lld significant pairs exceed 2x the pad (%lld); raise the pad",
+                (long long)n_sig, (long long)(2 * pad_to));
+  // Overflow: all significant (flat, |S|), then a stable descending sort by |S| (ties keep the
+  // ascending flat order), the first pad_to, and an ascending sort of their flat indices.
+  pairs_build_kernel<<<(int)M, kRowThreads, 0, st>>>(A9, mu, N, (int)M, eps, unique, p.row_off, 1,
+                                                       nullptr, nullptr, nullptr, p.flat, p.val);
+  GSDFT_LAUNCHED("pairs_build_rank");
+  val_bits_kernel<<<grid_1d(n_sig, 256), 256, 0, st>>>(p.val, n_sig, p.bits);
+  GSDFT_LAUNCHED("val_bits");
+  size_t sb = p.sort_bytes;
+  GSDFT_CUDA(cub::DeviceRadixSort::SortPairsDescending(p.sort_tmp, sb, p.bits, p.bits_sorted,
+                                                       p.flat, p.flat_sorted, (int)n_sig, 0, 64,
+                                                       st));
+  sb = p.sort_bytes;
+  GSDFT_CUDA(cub::DeviceRadixSort::SortKeys(p.sort_tmp, sb, p.flat_sorted, p.keep_sorted,
+                                            (int)pad_to, 0, 64, st));
+  decode_flat_kernel<<<grid_1d(pad_to, 256), 256, 0, st>>>(p.keep_sorted, pad_to, (int)M, unique,
+                                                           pi, pj, w);
+  GSDFT_LAUNCHED("decode_flat");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_stripe_pairs(const int32_t* pi, const int32_t* pj, const double* w, int64_t n,
+                                  int G, int32_t* pi_out, int32_t* pj_out, double* w_out,
+                                  gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n >= 0 && G >= 1, "bad n or G");
+  if (n == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(pi && pj && w && pi_out && pj_out && w_out, "null pointer");
+  GSDFT_REQUIRE(pi_out != pi && pj_out != pj && w_out != w, "stripe_pairs is out of place");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (G <= 1 || n % G) {
+    GSDFT_CUDA(cudaMemcpyAsync(pi_out, pi, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    GSDFT_CUDA(cudaMemcpyAsync(pj_out, pj, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    GSDFT_CUDA(cudaMemcpyAsync(w_out, w, n * sizeof(double), cudaMemcpyDeviceToDevice, st));
+    return GSDFT_OK;
+  }
+  stripe_kernel<<<grid_1d(n, 256), 256, 0, st>>>(pi, pj, w, n, G, pi_out, pj_out, w_out);
+  GSDFT_LAUNCHED("stripe");
+  return GSDFT_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Pair plan
+// ------------------------------------------------------------------------------------------------
+namespace {
+struct PlanWs {
+  char* flags;
+  int64_t* n_sel;
+  int32_t* keys;
+  int32_t* keys_sorted;
+  int32_t* iota;
+  void* tmp;
+  size_t tmp_bytes;
+};
+
+size_t plan_tmp_bytes(int64_t n) {
+  size_t a = 0, b = 0;
+  cub::DeviceSelect::Flagged(nullptr, a, thrust::counting_iterator<int32_t>(0), (char*)nullptr,
+                             (int32_t*)nullptr, (int64_t*)nullptr, (int)n);
+  cub::DeviceRadixSort::SortPairs(nullptr, b, (int32_t*)nullptr, (int32_t*)nullptr,
+                                  (int32_t*)nullptr, (int32_t*)nullptr, (int)n);
+  return a > b ? a : b;
+}
+
+template <class C>
+void layout_plan(C& c, int64_t n, PlanWs* p, size_t tmp) {
+  auto f = c.template take<char>(n + 1);
+  auto ns = c.template take<int64_t>(1);
+  auto k = c.template take<int32_t>(n + 1);
+  auto ks = c.template take<int32_t>(n + 1);
+  auto io = c.template take<int32_t>(n + 1);
+  auto t = c.template take<char>(tmp);
+  if (p) *p = PlanWs{(char*)f, (int64_t*)ns, (int32_t*)k, (int32_t*)ks, (int32_t*)io, t, tmp};
+}
+}  // namespace
+
+extern "C" size_t gsdft_pair_plan_workspace_size(int64_t n, int64_t M) {
+  (void)M;
+  SizerP z;
+  layout_plan(z, n, nullptr, plan_tmp_bytes(n));
+  return z.s.off + 256;
+}
+
+extern "C" int gsdft_pair_plan(const int32_t* pi, const int32_t* pj, const double* w, int64_t n,
+                               int64_t M, int32_t* live_idx, int64_t* n_live_host, int32_t* order_i,
+                               int64_t* seg_i, int32_t* order_j, int64_t* seg_j, void* ws,
+                               size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n >= 0 && n < (int64_t(1) << 31) && M > 0, "bad n or M");
+  GSDFT_REQUIRE(n_live_host && seg_i && seg_j, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  PlanWs p;
+  size_t tmp = plan_tmp_bytes(n);
+  Carver c(ws, ws_bytes);
+  layout_plan(c, n, &p, tmp);
+  if (!c.ok) return fail(GSDFT_ERR_ARG, "pair plan workspace too small (%zu < %zu)", ws_bytes, c.off);
+  if (n == 0) {
+    *n_live_host = 0;
+    GSDFT_CUDA(cudaMemsetAsync(seg_i, 0, (M + 1) * sizeof(int64_t), st));
+    GSDFT_CUDA(cudaMemsetAsync(seg_j, 0, (M + 1) * sizeof(int64_t), st));
+    return GSDFT_OK;
+  }
+  GSDFT_REQUIRE(pi && pj && w && live_idx && order_i && order_j, "null pointer");
+  live_flags_kernel<<<grid_1d(n, 256), 256, 0, st>>>(w, n, p.flags);
+  GSDFT_LAUNCHED("live_flags");
+  size_t tb = tmp;
+  GSDFT_CUDA(cub::DeviceSelect::Flagged(p.tmp, tb, thrust::counting_iterator<int32_t>(0), p.flags,
+                                        live_idx, p.n_sel, (int)n, st));
+  GSDFT_CUDA(cudaMemcpyAsync(n_live_host, p.n_sel, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+  GSDFT_CUDA(cudaStreamSynchronize(st));
+  int64_t nl = *n_live_host;
+  int eb = end_bit_for(M);
+  const int32_t* keysrc[2] = {pi, pj};
+  int32_t* order[2] = {order_i, order_j};
+  int64_t* seg[2] = {seg_i, seg_j};
+  for (int s = 0; s < 2; ++s) {
+    if (nl > 0) {
+      gather_keys_kernel<<<grid_1d(nl, 256), 256, 0, st>>>(keysrc[s], live_idx, nl, p.keys, p.iota);
+      GSDFT_LAUNCHED("gather_keys");
+      tb = tmp;
+      GSDFT_CUDA(cub::DeviceRadixSort::SortPairs(p.tmp, tb, p.keys, p.keys_sorted, p.iota, order[s],
+                                                 (int)nl, 0, eb, st));
+    }
+    segment_bounds_kernel<<<grid_1d(M + 1, 256), 256, 0, st>>>(p.keys_sorted, nl, M, seg[s]);
+    GSDFT_LAUNCHED("segment_bounds");
+  }
+  return GSDFT_OK;
+}

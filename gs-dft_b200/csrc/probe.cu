@@ -1,0 +1,40 @@
+// Launch accounting and the FP64 FMA throughput probe.
+#include <atomic>
+
+#include "common.cuh"
+
+namespace gsdft {
+
+static std::atomic<int64_t> g_launches{0};
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// 16 independent FMA chains per thread; the coefficients keep every value finite.
+__global__ void dfma_probe_kernel(double* out, int64_t iters) {
+  double a[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) a[k] = 1.0 + 1e-3 * (threadIdx.x + k);
+  const double m = 0.999999999, c = 1e-9;
+  for (int64_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int k = 0; k < 16; ++k) a[k] = fma(a[k], m, c);
+  }
+  double s = 0.0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) s += a[k];
+  out[blockIdx.x * (int64_t)blockDim.x + threadIdx.x] = s;
+}
+
+}  // namespace gsdft
+
+using namespace gsdft;
+
+extern "C" int64_t gsdft_kernel_launches(void) { return g_launches.load(); }
+
+extern "C" int gsdft_dfma_probe(double* out, int64_t iters, int blocks, int threads,
+                                gsdft_stream_t stream) {
+  GSDFT_REQUIRE(out && iters > 0 && blocks > 0 && threads > 0 && threads <= 1024, "bad arguments");
+  dfma_probe_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(out, iters);
+  GSDFT_LAUNCHED("dfma_probe");
+  return GSDFT_OK;
+}

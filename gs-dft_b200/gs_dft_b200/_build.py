@@ -1,0 +1,66 @@
+"""Build ``libgsdft_b200.so`` in-tree from ``gs-dft_b200/csrc`` with nvcc for sm_100a.
+
+Usage: ``python -m gs_dft_b200._build`` (or ``__graft_entry__.build()``). Cross-compiles without a
+GPU. Incremental: an object is rebuilt when its source or any header is newer.
+"""
+from __future__ import annotations
+
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(os.path.dirname(PKG), "csrc")
+ROOT = os.path.dirname(os.path.dirname(PKG))
+INCLUDE = os.path.join(ROOT, "include")
+LIB = os.path.join(PKG, "libgsdft_b200.so")
+OBJDIR = os.path.join(os.path.dirname(PKG), "_build")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+    "-I" + INCLUDE, "-I" + CSRC,
+]
+
+
+def nvcc() -> str:
+    exe = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(exe):
+        raise RuntimeError("nvcc not found; the CUDA 12.9 toolkit is required to build")
+    return exe
+
+
+def _newest_header() -> float:
+    hs = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))
+    hs += glob.glob(os.path.join(INCLUDE, "*.h"))
+    return max((os.path.getmtime(h) for h in hs), default=0.0)
+
+
+def build(verbose: bool = False, extra_flags: list[str] | None = None) -> str:
+    os.makedirs(OBJDIR, exist_ok=True)
+    srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    hdr = _newest_header()
+    objs = []
+    for s in srcs:
+        o = os.path.join(OBJDIR, os.path.basename(s)[:-3] + ".o")
+        objs.append(o)
+        if os.path.exists(o) and os.path.getmtime(o) >= max(os.path.getmtime(s), hdr):
+            continue
+        cmd = [nvcc(), *NVCC_FLAGS, *(extra_flags or []), "-c", s, "-o", o]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    if (not os.path.exists(LIB)
+            or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)):
+        cmd = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", LIB,
+               "-lcusolver", "-lcublas", "-lcudart"]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))

@@ -1,0 +1,191 @@
+"""Device-resident RI-J engine: one pair list, one frozen aux basis, repeated J-builds.
+
+Holds every buffer the per-step path needs (pair plan, pair records, reverse-pass sums, gradients,
+workspace), allocated once per refresh, so a step allocates nothing. A step is
+
+    splat quantities -> pair prep (A_hat, P, KN, eigenframe, q) -> gamma (fused 3-centre contraction)
+    -> [allreduce gamma] -> d, E_J (metric solve) -> reverse pass over (pair x aux) -> pair chain
+    -> per-splat reductions -> chart reverse -> [allreduce gradients]
+
+which is the single-device screened DF step of the reference (gs_dft/coulomb/ri.py:436-494 under
+jax.value_and_grad, gs_dft/ks/train.py:367-382) with the gradient written out.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from .._lib import REC_FIELDS, SIDE_FIELDS, VJP_FIELDS, lib, ptr, stream_handle
+
+F64 = torch.float64
+
+
+def _i64():
+    return ctypes.c_int64(0)
+
+
+@dataclass
+class PairPlan:
+    """Refresh-time grouping of a pair list (live entries, by-pi and by-pj orders)."""
+
+    n: int
+    n_live: int
+    live_idx: torch.Tensor
+    order_i: torch.Tensor
+    seg_i: torch.Tensor
+    order_j: torch.Tensor
+    seg_j: torch.Tensor
+
+
+def make_plan(pi: torch.Tensor, pj: torch.Tensor, w: torch.Tensor, M: int) -> PairPlan:
+    dev = pi.device
+    n = int(pi.shape[0])
+    live = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    oi = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    oj = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    si = torch.empty(M + 1, dtype=torch.int64, device=dev)
+    sj = torch.empty(M + 1, dtype=torch.int64, device=dev)
+    ws_bytes = lib.gsdft_pair_plan_workspace_size(n, M)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    nl = _i64()
+    lib.call("gsdft_pair_plan", ptr(pi), ptr(pj), ptr(w), n, M, ptr(live), ctypes.byref(nl),
+             ptr(oi), ptr(si), ptr(oj), ptr(sj), ptr(ws), ws_bytes, stream_handle(dev))
+    return PairPlan(n=n, n_live=int(nl.value), live_idx=live, order_i=oi, seg_i=si, order_j=oj,
+                    seg_j=sj)
+
+
+def splat_quantities(quat, log_scale):
+    """(A9 (M,9), N (M)) on the device."""
+    M = int(quat.shape[0])
+    A9 = torch.empty((M, 9), dtype=F64, device=quat.device)
+    N = torch.empty(M, dtype=F64, device=quat.device)
+    lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), M, ptr(A9), ptr(N),
+             stream_handle(quat.device))
+    return A9, N
+
+
+class RIJEngine:
+    """Repeated screened RI-J builds on a fixed (pair list, aux, factor).
+
+    Args:
+        pi, pj: int32 pair indices (device); w: float64 weights (0 = padding; 1 ordered; 2 unique).
+        M: number of splats; n_occ: occupied orbitals.
+        beta, R, KN: the aux quantities; L: lower Cholesky factor of V + lam I (row-major).
+    """
+
+    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L):
+        self.device = pi.device
+        self.M, self.n_occ = int(M), int(n_occ)
+        self.pi = pi.contiguous()
+        self.pj = pj.contiguous()
+        self.w = w.to(F64).contiguous()
+        self.beta, self.R, self.KN, self.L = beta, R, KN, L
+        self.n_aux = int(beta.shape[0])
+        self.plan = make_plan(self.pi, self.pj, self.w, self.M)
+        dev, nl, n = self.device, self.plan.n_live, self.plan.n
+        e = lambda *s: torch.empty(s, dtype=F64, device=dev)
+        self.A9, self.N = e(self.M, 9), e(self.M)
+        self.rec = e(max(nl, 1), REC_FIELDS)
+        self.sums = e(max(nl, 1), VJP_FIELDS)
+        self.side = e(max(nl, 1), SIDE_FIELDS)
+        self.J = e(max(n, 1))
+        self.gamma, self.d, self.E = e(self.n_aux), e(self.n_aux), e(1)
+        self.gA6, self.gmu, self.gN = e(self.M, 6), e(self.M, 3), e(self.M)
+        self.g_quat, self.g_log = e(self.M, 4), e(self.M, 3)
+        self.g_C = e(self.M, max(self.n_occ, 1))
+        self.ws_bytes = max(lib.gsdft_j_forward_workspace_size(nl, self.n_aux),
+                            lib.gsdft_j_vjp_workspace_size(nl, self.n_aux),
+                            lib.gsdft_j_solve_workspace_size(self.n_aux), 256)
+        self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        # Optional CUDA-event brackets around the two integral kernels (recorded on the current
+        # stream, the one the kernels are launched on): {"forward": [(start, end)], "vjp": [...]}.
+        self.timing = False
+        self.events = {"forward": [], "vjp": []}
+
+    def _bracket(self, name):
+        if not self.timing:
+            return None
+        st = torch.cuda.current_stream(self.device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        self.events[name].append((a, b))
+        return b
+
+    def kernel_ms(self, name):
+        """Mean event time (ms) of the bracketed launches of ``name`` recorded so far."""
+        ev = self.events[name]
+        return sum(a.elapsed_time(b) for a, b in ev) / max(len(ev), 1)
+
+    # -- stages -----------------------------------------------------------------------------------
+    def forward_local(self, quat, log_scale, centers, C_occ, occ):
+        """Splat quantities, pair prep and this device's gamma (before any allreduce)."""
+        s = stream_handle(self.device)
+        nl = self.plan.n_live
+        lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),
+                 ptr(self.N), s)
+        lib.call("gsdft_pair_prep", ptr(self.A9), ptr(centers), ptr(self.N), self.M, ptr(self.pi),
+                 ptr(self.pj), ptr(self.w), ptr(self.plan.live_idx), nl, ptr(C_occ), ptr(occ),
+                 self.n_occ, ptr(self.rec), s)
+        end = self._bracket("forward")
+        lib.call("gsdft_j_forward", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
+                 self.n_aux, ptr(self.gamma), ptr(self.ws), self.ws_bytes, s)
+        if end is not None:
+            end.record(torch.cuda.current_stream(self.device))
+        return self.gamma
+
+    def solve(self):
+        """d = (L L^T)^-1 gamma, E = 1/2 gamma.d (replicated tail)."""
+        lib.call("gsdft_j_solve", ptr(self.L), ptr(self.gamma), self.n_aux, ptr(self.d),
+                 ptr(self.E), ptr(self.ws), self.ws_bytes, stream_handle(self.device))
+        return self.E, self.d
+
+    def backward_local(self, centers, C_occ, occ, g_E=None):
+        """This device's pre-chart splat cotangents (gA6, gmu, gN), J per list entry and g_C."""
+        s = stream_handle(self.device)
+        nl = self.plan.n_live
+        end = self._bracket("vjp")
+        lib.call("gsdft_j_vjp", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
+                 ptr(self.d), ptr(g_E), self.n_aux, ptr(self.sums), ptr(self.ws), self.ws_bytes, s)
+        if end is not None:
+            end.record(torch.cuda.current_stream(self.device))
+        lib.call("gsdft_pair_chain", ptr(self.A9), ptr(centers), ptr(self.N), self.M,
+                 ptr(self.pi), ptr(self.pj), ptr(self.plan.live_idx), nl, self.plan.n,
+                 ptr(self.rec), ptr(self.sums), ptr(self.side), ptr(self.J), s)
+        lib.call("gsdft_splat_reduce", ptr(self.side), ptr(self.plan.order_i),
+                 ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl, self.M,
+                 ptr(self.gA6), ptr(self.gmu), ptr(self.gN), s)
+        if self.n_occ > 0:
+            lib.call("gsdft_density_grad", ptr(self.pi), ptr(self.pj), ptr(self.w),
+                     ptr(self.plan.live_idx), ptr(self.J), ptr(self.plan.order_i),
+                     ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl,
+                     self.M, ptr(C_occ), ptr(occ), self.n_occ, ptr(self.g_C), s)
+        return self.gA6, self.gmu, self.gN, self.g_C
+
+    def chart(self, quat, log_scale):
+        lib.call("gsdft_chart_vjp", ptr(quat), ptr(log_scale), ptr(self.gA6), ptr(self.gN),
+                 self.M, ptr(self.g_quat), ptr(self.g_log), stream_handle(self.device))
+        return self.g_quat, self.g_log
+
+    # -- whole step -------------------------------------------------------------------------------
+    def step(self, quat, log_scale, centers, C_occ, occ, grad=True, g_E=None):
+        """Single-device J-build + gradient. Returns a dict of device tensors (views of the
+        engine's buffers: copy them before the next step if they must persist)."""
+        self.forward_local(quat, log_scale, centers, C_occ, occ)
+        self.solve()
+        out = dict(E=self.E, gamma=self.gamma, d=self.d)
+        if grad:
+            self.backward_local(centers, C_occ, occ, g_E)
+            self.chart(quat, log_scale)
+            out.update(J=self.J, g_quat=self.g_quat, g_log_scale=self.g_log, g_centers=self.gmu,
+                       g_C=self.g_C[:, :self.n_occ], gA6=self.gA6, gN=self.gN)
+        return out
+
+
+def check_device_status(clear=True):
+    """Raise if a kernel's bounded wait ran out since the last check."""
+    st = ctypes.c_int(0)
+    lib.call("gsdft_device_status", ctypes.byref(st), 1 if clear else 0)
+    if st.value:
+        raise RuntimeError(f"gs_dft_b200 device status {st.value}: a bulk-copy wait timed out")

@@ -1,0 +1,100 @@
+"""Refresh state and the Coulomb-only builder.
+
+``SplatState`` / ``refresh`` mirror gs_dft/ks/energy.py:121-139 and :421-474 for the fields the
+screened DF Coulomb needs (pairs, aux, cholV); the pad rule mirrors gs_dft/ks/train.py:356-359.
+``CoulombKS`` carries the ``coulomb`` / ``screen`` / ``mesh`` arguments of ``SplatKS``
+(gs_dft/ks/energy.py:166-173) and evaluates the Hartree term E_J of a model; the rest of the
+Kohn-Sham energy (kinetic, external, XC) is outside this library.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from ..basis.isotropic import IsotropicSplat, init_product_aux
+from ..basis.spectral import Splat
+from ..coulomb.engine import RIJEngine
+from ..coulomb.ri import aux_cholesky
+from ..screening.pairs import count_significant, neighbor_pairs, pair_weight, stripe_pairs
+from .terms import DFSpec, Pairlist, ScreenedProductDFCoulomb
+
+
+def pad_rule(n0: int, pad: float, G: int) -> int:
+    """pad_to = ceil(pad * n0 / G) * G (gs_dft/ks/train.py:356-359)."""
+    return -(-int(pad * n0) // G) * G
+
+
+@dataclass
+class SplatModel:
+    """Trainable model: splats + MO coefficients + occupations (gs_dft/ks/energy.py:109-118)."""
+
+    basis: Splat
+    C: torch.Tensor
+    occupations: torch.Tensor
+
+
+@dataclass
+class SplatState:
+    """Refresh products: pair list, frozen product aux, factor of V + lam I."""
+
+    pairs: tuple | None = None
+    aux: IsotropicSplat | None = None
+    cholV: torch.Tensor | None = None
+    _engine: RIJEngine | None = field(default=None, repr=False)
+
+    def engine_for(self, basis, C_occ) -> RIJEngine:
+        """The device engine for this state's pairs/aux/factor (built once, reused per step)."""
+        if self._engine is None:
+            pi, pj, valid = self.pairs
+            beta, R, KN = self.aux.quantities()
+            self._engine = RIJEngine(pi.to(torch.int32).contiguous(), pj.to(torch.int32).contiguous(),
+                                     pair_weight(valid).contiguous(), basis.n_basis,
+                                     int(C_occ.shape[1]), beta, R.contiguous(), KN, self.cholV)
+        return self._engine
+
+
+def refresh(ks, basis: Splat, *, pad_to: int | None = None,
+            like: SplatState | None = None) -> SplatState:
+    """Rebuild the refresh products for the current splats (host cadence).
+
+    ``like=previous_state`` inherits the previous pad so shapes stay constant.
+    """
+    if pad_to is None and like is not None and like.pairs is not None:
+        pad_to = int(like.pairs[0].shape[0])
+    screen: Pairlist = ks.screen
+    pairs = neighbor_pairs(basis, eps=screen.eps, pad_to=pad_to, unique=screen.unique)
+    G = int(getattr(ks, "n_devices", 1) or 1)
+    if G > 1:
+        pairs = stripe_pairs(*pairs, G)
+    c: ScreenedProductDFCoulomb = ks.coulomb
+    aux = init_product_aux(basis, scales=c.scales, diagonal_only=c.diagonal,
+                           pi=pairs[0], pj=pairs[1], valid=pairs[2])
+    cholV = aux_cholesky(aux, c.lam)
+    return SplatState(pairs=pairs, aux=aux, cholV=cholV)
+
+
+class CoulombKS:
+    """The Hartree term of ``SplatKS(system, xc, grid=..., coulomb=df(), screen=pairlist())``:
+    ``ks(model, state) -> E_J`` (differentiable in the model's splats and C)."""
+
+    def __init__(self, *, coulomb: DFSpec | None = None, screen: Pairlist | None = None,
+                 n_devices: int = 1):
+        coulomb = coulomb or DFSpec()
+        if not isinstance(coulomb, DFSpec):
+            raise TypeError(f"coulomb must come from df(), got {coulomb!r}")
+        if screen is None:
+            raise ValueError("the B200 RI-J path is the screened path: pass screen=pairlist(...)")
+        self.screen = screen
+        self.coulomb = ScreenedProductDFCoulomb.from_spec(coulomb, skip_pad=screen.skip_pad)
+        self.n_devices = int(n_devices)
+
+    def initial_pad(self, basis: Splat) -> int:
+        n0 = count_significant(basis, self.screen.eps, self.screen.unique)
+        return pad_rule(n0, self.screen.pad, self.n_devices)
+
+    def __call__(self, model: SplatModel, state: SplatState):
+        if state is None or state.pairs is None or state.aux is None:
+            raise ValueError("coulomb=df() needs the refresh state: see refresh(ks, basis).")
+        e_j, _ = self.coulomb.energy(model.basis, model.C, None, model.occupations, state)
+        return e_j

@@ -1,0 +1,227 @@
+/*
+ * gsdft_b200.h — C ABI of the B200-native screened density-fitted Coulomb (RI-J) path.
+ *
+ * Replaces the JAX hot path of andresguzco/gs-dft: the significant-pair list, the product auxiliary
+ * basis with its Coulomb metric and Cholesky factor, the fused 3-centre (aux | splat-pair) fit-vector
+ * contraction gamma, the metric solve, and the analytic backward pass to the splat chart parameters.
+ *
+ * Conventions (every entry point):
+ *   - all pointers are DEVICE pointers unless the name ends in _host; FP64 arrays are row-major;
+ *   - buffers are owned and allocated by the caller; no entry point allocates device memory. Scratch
+ *     comes from an explicit workspace whose size the matching *_workspace_size() returns;
+ *   - work is enqueued on `stream` (the last argument). Only gsdft_pairs_count / gsdft_pairs_build /
+ *     gsdft_pair_plan / gsdft_aux_cholesky synchronise the stream, to read back integers (pair counts,
+ *     the factorisation status), exactly where the reference syncs to the host
+ *     (gs_dft/screening/pairs.py:279,305);
+ *   - the return value is a status: 0 = GSDFT_OK, otherwise an error code; gsdft_last_error_string()
+ *     describes the last failure on the calling thread;
+ *   - outputs are deterministic: identical inputs give bit-identical outputs (no floating-point
+ *     atomics; every reduction has a fixed order).
+ *
+ * Layouts:
+ *   quat (M,4), log_scale (M,3), centers (M,3)           splat chart parameters
+ *   A9 (M,9) row-major 3x3 precision, N (M)              splat quantities
+ *   pi, pj int32 (n), w double (n)                       pair list; w = 0/1 (ordered) or 0/1/2 (unique)
+ *   beta (Naux), R (Naux,3), KN (Naux)                   isotropic aux: exponent, centre, normalisation
+ *   V / L (Naux,Naux)                                     metric; L = lower Cholesky factor, row-major
+ *   C_occ (M,n_occ), occ (n_occ)                         occupied orbitals and occupations
+ *   gA6 (M,6)                                             symmetric cotangent [xx,yy,zz,xy,xz,yz]
+ */
+#ifndef GSDFT_B200_H
+#define GSDFT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* gsdft_stream_t; /* = cudaStream_t */
+
+enum {
+  GSDFT_OK = 0,
+  GSDFT_ERR_ARG = 1,       /* bad shape, size, pointer or workspace */
+  GSDFT_ERR_CUDA = 2,      /* a CUDA runtime call or launch failed */
+  GSDFT_ERR_OVERFLOW = 3,  /* more significant pairs than the headroom allows */
+  GSDFT_ERR_LINALG = 4     /* the metric is not positive definite, or a library call failed */
+};
+
+/* Fields of one live pair's record, stored record-major: rec[a * GSDFT_REC_FIELDS + f]
+ * (144 bytes per pair, so any tile of records is a 16-byte-aligned contiguous block). */
+enum {
+  GSDFT_REC_L0 = 0, GSDFT_REC_L1, GSDFT_REC_L2,                     /* eigenvalues of A_hat */
+  GSDFT_REC_U00, GSDFT_REC_U01, GSDFT_REC_U02,                      /* eigenvectors (columns) */
+  GSDFT_REC_U10, GSDFT_REC_U11, GSDFT_REC_U12,
+  GSDFT_REC_U20, GSDFT_REC_U21, GSDFT_REC_U22,
+  GSDFT_REC_P0, GSDFT_REC_P1, GSDFT_REC_P2,                         /* product centre */
+  GSDFT_REC_QK,                                                     /* q * KN * pref */
+  GSDFT_REC_Q,                                                      /* q = w sum occ C_i C_j */
+  GSDFT_REC_KN,                                                     /* KN * pref */
+  GSDFT_REC_FIELDS
+};
+
+/* Per-live-pair sums of the reverse pass, stored record-major: sums[a * GSDFT_VJP_FIELDS + f]. */
+enum {
+  GSDFT_VJP_SJ = 0,
+  GSDFT_VJP_SD0, GSDFT_VJP_SD1, GSDFT_VJP_SD2,
+  GSDFT_VJP_SV0, GSDFT_VJP_SV1, GSDFT_VJP_SV2,
+  GSDFT_VJP_SZ00, GSDFT_VJP_SZ11, GSDFT_VJP_SZ22, GSDFT_VJP_SZ01, GSDFT_VJP_SZ02, GSDFT_VJP_SZ12,
+  GSDFT_VJP_FIELDS
+};
+
+#define GSDFT_SIDE_FIELDS 20 /* per live pair: i-side (gA6, gmu3, gN) then j-side */
+
+const char* gsdft_last_error_string(void);
+int gsdft_version(void);
+
+/* Reads (and with clear != 0 resets) the library's device status word on the current device:
+ * nonzero when a kernel's bounded wait on a bulk copy ran out (the kernel then abandoned its work
+ * and its outputs are invalid). Synchronises the device. No reference counterpart. */
+int gsdft_device_status(int* status_host, int clear);
+
+/* Cumulative number of kernels this library has launched in the process (all devices). Used to
+ * report how many of the library's own kernels ran in a timed region. No reference counterpart. */
+int64_t gsdft_kernel_launches(void);
+
+/* FP64 FMA throughput probe: blocks x threads threads each run 16 independent FMA chains for
+ * `iters` iterations (2 * 16 * iters flop per thread) and write one sum per thread to out
+ * (blocks * threads doubles). Measures the device's FP64 peak at the clocks of the run. No
+ * reference counterpart. */
+int gsdft_dfma_probe(double* out, int64_t iters, int blocks, int threads, gsdft_stream_t stream);
+
+/* ---- splat chart ------------------------------------------------------------------------------ */
+
+/* A = R(q) diag(exp l) R(q)^T, N = (8 exp(sum l) / pi^3)^(1/4).
+ * Replaces Splat.A / Splat.norm / full_quantities (gs_dft/basis/spectral.py:33-40,71-82;
+ * gs_dft/coulomb/stream.py:79-81). */
+int gsdft_splat_quantities(const double* quat, const double* log_scale, int64_t M, double* A9,
+                           double* N, gsdft_stream_t stream);
+
+/* Reverse of the chart: (gA6, gN) -> (g_quat, g_log_scale). The jax.grad of the same chart
+ * (gs_dft/basis/spectral.py:33-40,71-82), written out. */
+int gsdft_chart_vjp(const double* quat, const double* log_scale, const double* gA6,
+                    const double* gN, int64_t M, double* g_quat, double* g_log_scale,
+                    gsdft_stream_t stream);
+
+/* ---- significant-pair list ------------------------------------------------------------------- */
+
+size_t gsdft_pairs_workspace_size(int64_t M, int64_t pad_to);
+
+/* Number of pairs with |S_ij| > eps (j >= i when unique). Replaces _count_significant
+ * (gs_dft/screening/pairs.py:103-118). Synchronises the stream. */
+int gsdft_pairs_count(const double* A9, const double* mu, const double* N, int64_t M, double eps,
+                      int unique, int64_t* n_sig_host, void* ws, size_t ws_bytes,
+                      gsdft_stream_t stream);
+
+/* The lexsorted significant list padded to pad_to with (0,0,w=0); if more than pad_to pairs are
+ * significant, keeps the pad_to largest |S| (ties by ascending flat index), re-lexsorted; fails
+ * with GSDFT_ERR_OVERFLOW above 2*pad_to. eps < 0 keeps every pair. Replaces neighbor_pairs with
+ * pad_to (gs_dft/screening/pairs.py:225-315, 155-164, 318-322). Synchronises the stream. */
+int gsdft_pairs_build(const double* A9, const double* mu, const double* N, int64_t M, double eps,
+                      int unique, int64_t pad_to, int32_t* pi, int32_t* pj, double* w,
+                      int64_t* n_sig_host, void* ws, size_t ws_bytes, gsdft_stream_t stream);
+
+/* Round-robin deal of a padded list over G devices, new[g*d + j] = old[j*G + g]; identity when
+ * G <= 1 or n % G != 0. Replaces stripe_pairs (gs_dft/ks/shard.py:146-166). */
+int gsdft_stripe_pairs(const int32_t* pi, const int32_t* pj, const double* w, int64_t n, int G,
+                       int32_t* pi_out, int32_t* pj_out, double* w_out, gsdft_stream_t stream);
+
+/* Refresh-time plan of a pair list: the live entries (w != 0) in list order, and the grouping of
+ * live entries by pi and by pj (stable) used by the deterministic per-splat reductions.
+ * order_i/order_j (n_live) index live entries; seg_i/seg_j (M+1) are segment offsets.
+ * Synchronises the stream (returns n_live). No reference counterpart (the reference scatters with
+ * segment_sum inside autodiff). */
+size_t gsdft_pair_plan_workspace_size(int64_t n, int64_t M);
+int gsdft_pair_plan(const int32_t* pi, const int32_t* pj, const double* w, int64_t n, int64_t M,
+                    int32_t* live_idx, int64_t* n_live_host, int32_t* order_i, int64_t* seg_i,
+                    int32_t* order_j, int64_t* seg_j, void* ws, size_t ws_bytes,
+                    gsdft_stream_t stream);
+
+/* ---- auxiliary basis, metric, factor ------------------------------------------------------------ */
+
+/* Frozen product aux: per listed pair (pi == NULL: the M self-products), alpha0 = det(A_hat)^(1/3)
+ * (1 on zero-weight entries), centre = product centre; log_alpha = log(alpha0 * s) for each scale s,
+ * scale-major (Naux = n * n_scales). Replaces init_product_aux (gs_dft/basis/isotropic.py:81-116). */
+int gsdft_product_aux(const double* A9, const double* mu, const double* N, int64_t M,
+                      const int32_t* pi, const int32_t* pj, const double* w, int64_t n_pairs,
+                      const double* scales_host, int n_scales, double* log_alpha, double* R,
+                      gsdft_stream_t stream);
+
+/* beta = exp(log_alpha), KN = (2 beta / pi)^(3/4). Replaces IsotropicSplat.alpha/.norm and
+ * aux_quantities (gs_dft/basis/isotropic.py:30-39; gs_dft/coulomb/ri.py:238-240). */
+int gsdft_aux_quantities(const double* log_alpha, int64_t n_aux, double* beta, double* KN,
+                         gsdft_stream_t stream);
+
+/* V_PQ = KN_P KN_Q 2 pi^2.5 / (b_P b_Q sqrt(b_P + b_Q)) F0(b_P b_Q/(b_P+b_Q) |R_P - R_Q|^2),
+ * F0 from erf. Replaces aux_metric / coulomb_block (gs_dft/coulomb/ri.py:63-123,267-275). */
+int gsdft_aux_metric(const double* beta, const double* R, const double* KN, int64_t n_aux,
+                     double* V, gsdft_stream_t stream);
+
+/* In place: V <- lower Cholesky factor of V + lam I (row-major; the strict upper triangle is
+ * zeroed). Replaces aux_cholesky / shift_diag / _chol_donated (gs_dft/coulomb/ri.py:243-264).
+ * Fails with GSDFT_ERR_LINALG if V + lam I is not positive definite. Synchronises the stream. */
+size_t gsdft_aux_cholesky_workspace_size(int64_t n_aux);
+int gsdft_aux_cholesky(double* V, int64_t n_aux, double lam, void* ws, size_t ws_bytes,
+                       gsdft_stream_t stream);
+
+/* ---- per-step J-build ---------------------------------------------------------------------------- */
+
+/* Per live pair: A_hat, P, KN (gs_dft/coulomb/stream.py:203-215), the eigen-decomposition of A_hat
+ * (gs_dft/coulomb/ri.py:145), and q = w sum_o occ_o C_io C_jo (gs_dft/coulomb/ri.py:456).
+ * rec is (n_live, GSDFT_REC_FIELDS). */
+int gsdft_pair_prep(const double* A9, const double* mu, const double* N, int64_t M,
+                    const int32_t* pi, const int32_t* pj, const double* w,
+                    const int32_t* live_idx, int64_t n_live, const double* C_occ,
+                    const double* occ, int64_t n_occ, double* rec, gsdft_stream_t stream);
+
+/* gamma_P = sum_a (P|a) q_a over the live pairs, the 3-centre integral fused with the contraction
+ * (never stored). Replaces df_coulomb_gamma_screened + full_isobra_block
+ * (gs_dft/coulomb/ri.py:436-469, 126-185). */
+size_t gsdft_j_forward_workspace_size(int64_t n_live, int64_t n_aux);
+int gsdft_j_forward(const double* rec, int64_t n_live, const double* beta, const double* R,
+                    const double* KN, int64_t n_aux, double* gamma, void* ws, size_t ws_bytes,
+                    gsdft_stream_t stream);
+
+/* d = (L L^T)^-1 gamma, E = 1/2 gamma.d (E is a device scalar). Replaces df_coulomb_solve with
+ * cholV (gs_dft/coulomb/ri.py:472-482). */
+size_t gsdft_j_solve_workspace_size(int64_t n_aux);
+int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d, double* E,
+                  void* ws, size_t ws_bytes, gsdft_stream_t stream);
+
+/* Reverse pass over (live pair x aux): with dbar = g_E * d (g_E device scalar, NULL = 1), the
+ * per-pair sums (GSDFT_VJP_FIELDS, n_live) from which J_a = sum_P (P|a) dbar_P and the cotangents
+ * of A_hat, P, KN follow; sums is (n_live, GSDFT_VJP_FIELDS). Replaces the node reverse nodes_bwd and the eigh / dp2 autodiff
+ * (gs_dft/coulomb/ri.py:145-147,190-222). */
+size_t gsdft_j_vjp_workspace_size(int64_t n_live, int64_t n_aux);
+int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta, const double* R,
+                const double* KN, const double* d, const double* g_E, int64_t n_aux,
+                double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream);
+
+/* Chain per live pair: sums -> cotangents of A_hat, P, KN -> per-side (A_i, mu_i, N_i), (A_j, mu_j,
+ * N_j) contributions side (n_live, GSDFT_SIDE_FIELDS); J (n, list order; 0 on dead entries). The
+ * reverse of gs_dft/coulomb/stream.py:203-215. */
+int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
+                     const int32_t* pi, const int32_t* pj, const int32_t* live_idx,
+                     int64_t n_live, int64_t n, const double* rec, const double* sums,
+                     double* side, double* J, gsdft_stream_t stream);
+
+/* Deterministic per-splat sums of the side contributions (plan groupings) -> gA6 (M,6), gmu (M,3),
+ * gN (M). Replaces the segment scatter of JAX autodiff through A[pi], A[pj]. */
+int gsdft_splat_reduce(const double* side, const int32_t* order_i, const int64_t* seg_i,
+                       const int32_t* order_j, const int64_t* seg_j, int64_t n_live, int64_t M,
+                       double* gA6, double* gmu, double* gN, gsdft_stream_t stream);
+
+/* g_C[i,o] = occ_o (sum_{a: pi=i} J_a w_a C[pj_a,o] + sum_{a: pj=i} J_a w_a C[pi_a,o]): the gradient
+ * through q_a (gs_dft/coulomb/ri.py:456). */
+int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const double* w,
+                       const int32_t* live_idx, const double* J, const int32_t* order_i,
+                       const int64_t* seg_i, const int32_t* order_j, const int64_t* seg_j,
+                       int64_t n_live, int64_t M, const double* C_occ, const double* occ,
+                       int64_t n_occ, double* g_C, gsdft_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GSDFT_B200_H */

@@ -574,3 +574,98 @@ def refresh(quat, log_scale, centers, eps, lam, pad_to=None, unique=False, scale
     L = aux_cholesky(V, lam)
     return dict(pi=pi, pj=pj, valid=valid, n_sig=n_sig, log_alpha=log_alpha, R=R,
                 aux_q=aux_q, V=V, L=L)
+
+# ----------------------------------------------------------------------------------------------
+#  The same step with the O(N_aux x N_pairs) loops in C + OpenMP (gsdft_oracle_c.c): the checker at
+#  sizes the NumPy loops cannot reach, and the multi-core CPU baseline.
+# ----------------------------------------------------------------------------------------------
+_CLIB = None
+
+
+def c_lib():
+    """Load (building with ``make`` if needed) oracle/libgsdft_oracle.so."""
+    global _CLIB
+    if _CLIB is None:
+        import ctypes
+        import os
+        import subprocess
+        here = os.path.dirname(os.path.abspath(__file__))
+        path = os.path.join(here, "libgsdft_oracle.so")
+        if not os.path.exists(path):
+            subprocess.run(["make", "-C", here], check=True, capture_output=True)
+        lib = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        lib.orc_set_nodes.argtypes = [P, P]
+        lib.orc_gamma.argtypes = [P, ctypes.c_int64, P, P, P, ctypes.c_int64, P]
+        lib.orc_vjp.argtypes = [P, ctypes.c_int64, P, P, P, ctypes.c_int64, P]
+        t = np.ascontiguousarray(QUAD_T)
+        w = np.ascontiguousarray(QUAD_W)
+        lib.orc_set_nodes(t.ctypes.data, w.ctypes.data)
+        _CLIB = (lib, t, w)
+    return _CLIB[0]
+
+
+def pair_records(q_splat, C_occ, occ, pi, pj, valid):
+    """Per live pair: [lam(3), U(9, columns = eigenvectors), P(3), KN, q] and the live indices."""
+    w = np.asarray(valid, np.float64)
+    live = np.nonzero(w != 0)[0]
+    ci, cj = pi[live], pj[live]
+    Ah, Pa, KN = full_pair_quantities(q_splat, ci, cj)
+    Lam, U = np.linalg.eigh(Ah)
+    qa = pair_density(C_occ, occ, ci, cj, w[live])
+    rec = np.concatenate([Lam, U.reshape(-1, 9), Pa, KN[:, None], qa[:, None]], axis=1)
+    return np.ascontiguousarray(rec), live
+
+
+def energy_and_grad_c(sys_arrays, aux_q, L, pi, pj, valid, want_grad=True):
+    """energy_and_grad with the heavy loops in C/OpenMP. Same outputs."""
+    lib = c_lib()
+    quat, log_scale, centers, C_occ, occ = sys_arrays
+    qs = full_quantities(quat, log_scale, centers)
+    beta, R, KN_aux = (np.ascontiguousarray(a, dtype=np.float64) for a in aux_q)
+    rec, live = pair_records(qs, C_occ, occ, pi, pj, valid)
+    nl, na = rec.shape[0], beta.shape[0]
+    gamma = np.zeros(na)
+    lib.orc_gamma(rec.ctypes.data, nl, beta.ctypes.data, R.ctypes.data, KN_aux.ctypes.data, na,
+                  gamma.ctypes.data)
+    E, dvec = df_coulomb_solve(gamma, L)
+    out = dict(E=E, gamma=gamma, d=dvec)
+    if not want_grad:
+        return out
+    cP = np.ascontiguousarray(dvec * KN_aux)
+    sums = np.zeros((nl, 13))
+    lib.orc_vjp(rec.ctypes.data, nl, beta.ctypes.data, R.ctypes.data, cP.ctypes.data, na,
+                sums.ctypes.data)
+    Lam, U, KNa, qa = rec[:, 0:3], rec[:, 3:12].reshape(-1, 3, 3), rec[:, 15], rec[:, 16]
+    kn = KNa * PREF
+    qk = qa * kn
+    Mkl = np.empty((nl, 3, 3))
+    for (k, l), f in {(0, 0): 7, (1, 1): 8, (2, 2): 9, (0, 1): 10, (0, 2): 11, (1, 2): 12}.items():
+        Mkl[:, k, l] = Mkl[:, l, k] = -qk * sums[:, f]
+    for k in range(3):
+        Mkl[:, k, k] -= 0.5 * qk * sums[:, 1 + k]
+    Abar = np.einsum("bik,bkl,bjl->bij", U, Mkl, U)
+    Pe = 2.0 * qk[:, None] * Lam * sums[:, 4:7]
+    Pbar = np.einsum("bik,bk->bi", U, Pe)
+    KNbar = qa * PREF * sums[:, 0]
+    J = np.zeros(pi.shape[0])
+    J[live] = kn * sums[:, 0]
+    ci, cj = pi[live], pj[live]
+    gAi, gAj, gmui, gmuj, gNi, gNj = _pair_chain(qs, ci, cj, Abar, Pbar, KNbar)
+    M = centers.shape[0]
+    gA, gmu, gN = np.zeros((M, 3, 3)), np.zeros((M, 3)), np.zeros(M)
+    np.add.at(gA, ci, gAi)
+    np.add.at(gA, cj, gAj)
+    np.add.at(gmu, ci, gmui)
+    np.add.at(gmu, cj, gmuj)
+    np.add.at(gN, ci, gNi)
+    np.add.at(gN, cj, gNj)
+    w = np.asarray(valid, np.float64)[live]
+    s = (J[live] * w)[:, None] * occ[None, :]
+    gC = np.zeros_like(C_occ)
+    np.add.at(gC, ci, s * C_occ[cj])
+    np.add.at(gC, cj, s * C_occ[ci])
+    g_quat, g_log = chart_vjp(quat, log_scale, gA, gN)
+    out.update(J=J, g_quat=g_quat, g_log_scale=g_log, g_centers=gmu, g_C=gC, gA=gA, gmu=gmu,
+               gN=gN)
+    return out

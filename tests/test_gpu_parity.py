@@ -1,0 +1,289 @@
+"""CUDA path vs the CPU oracle on seeded inputs, through the C ABI (``gs_dft_b200`` host layer).
+
+Tolerances: integer and index work (pair lists, plans) is bit-exact; FP64 values agree within the
+north-star bound, relative 1e-10 with an absolute floor of 1e-12 times the array's scale (E_J,
+gamma, J, gradients). Golden cases come from executing the reference's own source
+(tests/golden/make_golden.py)."""
+import numpy as np
+import pytest
+
+import gsdft_oracle as O
+from conftest import load_golden
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL_REL = 1e-10, 1e-12
+
+
+def close(got, want, rtol=RTOL, atol_rel=ATOL_REL):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    scale = max(np.abs(want).max(), 1e-300) if want.size else 1.0
+    np.testing.assert_allclose(got, want, rtol=rtol, atol=atol_rel * scale)
+
+
+@pytest.fixture(scope="module")
+def g():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import gs_dft_b200
+    gs_dft_b200._lib.lib.load()
+    return gs_dft_b200
+
+
+def dev(a, dtype=torch.float64):
+    return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype, device="cuda")
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+def splats(g, d):
+    return g.Splat(dev(d["quat"]), dev(d["log_scale"]), dev(d["centers"]))
+
+
+CASES = ["ref_rand24.npz", "ref_rand48.npz", "ref_co2.npz"]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_chart(g, case):
+    d = load_golden(case)
+    s = splats(g, d)
+    A, _, N = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+    close(host(s.A), A, rtol=1e-14, atol_rel=1e-15)
+    close(host(s.norm), N, rtol=1e-14)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_pair_lists_bit_exact(g, case):
+    d = load_golden(case)
+    s = splats(g, d)
+    q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+    eps = float(d["eps"])
+    M = s.n_basis
+    n = d["ord_pi"].size
+    assert g.screening.count_significant(s, eps) == n
+    for pad, unique, keys in ((None, False, ("ord_pi", "ord_pj")), (n + 37, False, ("pad_pi", "pad_pj")),
+                              (None, True, ("uni_pi", "uni_pj"))):
+        pi, pj, v = g.neighbor_pairs(s, eps=eps, pad_to=pad, unique=unique)
+        opi, opj, ov, _ = O.neighbor_pairs(q, eps=eps, pad_to=pad, unique=unique)
+        np.testing.assert_array_equal(host(pi), opi)
+        np.testing.assert_array_equal(host(pj), opj)
+        np.testing.assert_array_equal(host(v), ov)
+        np.testing.assert_array_equal(host(pi), d[keys[0]])   # and the reference's own list
+        np.testing.assert_array_equal(host(pj), d[keys[1]])
+    # overflow: keep the pad largest |S|, ties by flat index, re-lexsorted
+    for unique in (False, True):
+        nn = O.count_significant(q, M, eps, unique)
+        pad = nn // 2 + 1
+        pi, pj, v = g.neighbor_pairs(s, eps=eps, pad_to=pad, unique=unique)
+        opi, opj, ov, _ = O.neighbor_pairs(q, eps=eps, pad_to=pad, unique=unique)
+        np.testing.assert_array_equal(host(pi), opi)
+        np.testing.assert_array_equal(host(pj), opj)
+    # eps < 0: every ordered pair, padded
+    pi, pj, v = g.neighbor_pairs(s, eps=-1.0, pad_to=M * M + 11)
+    np.testing.assert_array_equal(host(pi), d["all_pi"])
+    np.testing.assert_array_equal(host(pj), d["all_pj"])
+    np.testing.assert_array_equal(host(v), d["all_v"])
+
+
+def test_pair_list_guard_band(g):
+    """No screening decision sits within 1e-12 relative of eps on the golden systems, so the
+    bit-exact agreement above does not hinge on last-bit rounding."""
+    for case in CASES:
+        d = load_golden(case)
+        q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+        M = q[1].shape[0]
+        pi = np.repeat(np.arange(M), M)
+        pj = np.tile(np.arange(M), M)
+        s = O.canonical_abs_overlap(q, pi, pj)
+        assert np.sum(np.abs(s / float(d["eps"]) - 1.0) < 1e-12) == 0
+
+
+def test_overflow_beyond_headroom_raises(g):
+    d = load_golden("ref_rand24.npz")
+    s = splats(g, d)
+    n = d["ord_pi"].size
+    with pytest.raises(ValueError):
+        g.neighbor_pairs(s, eps=float(d["eps"]), pad_to=n // 3)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_aux_metric_factor(g, case):
+    d = load_golden(case)
+    s = splats(g, d)
+    aux = g.init_product_aux(s)
+    close(host(aux.log_alpha), d["aux_log_alpha"], rtol=1e-13, atol_rel=1e-14)
+    close(host(aux.centers), d["aux_R"], rtol=1e-12, atol_rel=1e-13)
+    V = g.aux_metric(aux)
+    close(host(V), d["V"], rtol=1e-12, atol_rel=1e-13)
+    L = g.aux_cholesky(aux, float(d["lam"]))
+    Lo = O.aux_cholesky(O.aux_metric(*O.aux_quantities(host(aux.log_alpha), host(aux.centers))),
+                        float(d["lam"]))
+    close(host(L), Lo, rtol=1e-8, atol_rel=1e-9)       # a factor of an ill-conditioned V
+    assert np.all(np.triu(host(L), 1) == 0.0)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_gamma_energy_vs_reference(g, case):
+    d = load_golden(case)
+    s = splats(g, d)
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, float(d["lam"]))
+    pi, pj, v = dev(d["pad_pi"], torch.int32), dev(d["pad_pj"], torch.int32), dev(d["pad_v"], torch.bool)
+    C, occ = dev(d["C_occ"]), dev(d["occ"])
+    gamma = g.df_coulomb_gamma_screened(s, C, occ, aux, pi, pj, valid=v)
+    close(host(gamma), d["gamma"])
+    E = g.df_coulomb_solve(gamma, aux, cholV=L)
+    close(float(E), float(d["E"]))
+    E2 = g.df_coulomb_energy_screened(s, C, occ, aux, pi, pj, valid=v, cholV=L)
+    close(float(E2), float(d["E"]))
+    # unique weights reproduce the ordered gamma (gs-dft tests/unit/test_pair_tricks.py:81-100)
+    gu = g.df_coulomb_gamma_screened(s, C, occ, aux, dev(d["uni_pi"], torch.int32),
+                                     dev(d["uni_pj"], torch.int32), valid=dev(d["uni_w"]))
+    close(host(gu), d["gamma_unique"])
+
+
+def _oracle_grad(d, pi, pj, v):
+    q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    L = O.aux_cholesky(O.aux_metric(*aq), float(d["lam"]))
+    return O.energy_and_grad((d["quat"], d["log_scale"], d["centers"], d["C_occ"], d["occ"]),
+                             aq, L, pi, pj, v)
+
+
+@pytest.mark.parametrize("case", ["ref_rand24.npz", "ref_rand48.npz", "ref_co2.npz"])
+@pytest.mark.parametrize("unique", [False, True])
+def test_energy_and_gradient_vs_oracle(g, case, unique):
+    d = load_golden(case)
+    key = ("uni_pi", "uni_pj", "uni_w") if unique else ("pad_pi", "pad_pj", "pad_v")
+    pi, pj, v = d[key[0]], d[key[1]], d[key[2]]
+    ref = _oracle_grad(d, pi, pj, v)
+    s = splats(g, d)
+    for t in (s.quat, s.log_scale, s.centers):
+        t.requires_grad_(True)
+    C = dev(d["C_occ"]).requires_grad_(True)
+    occ = dev(d["occ"])
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, float(d["lam"]))
+    vt = dev(v) if unique else dev(v, torch.bool)
+    E = g.df_coulomb_energy_screened(s, C, occ, aux, dev(pi, torch.int32), dev(pj, torch.int32),
+                                     valid=vt, cholV=L)
+    E.backward()
+    close(float(E), ref["E"])
+    close(host(s.quat.grad), ref["g_quat"])
+    close(host(s.log_scale.grad), ref["g_log_scale"])
+    close(host(s.centers.grad), ref["g_centers"])
+    close(host(C.grad), ref["g_C"])
+
+
+def test_gradient_matches_reference_finite_differences(g):
+    d = load_golden("ref_grad.npz")
+    q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=float(d["eps"]))
+    s = splats(g, d)
+    for t in (s.quat, s.log_scale, s.centers):
+        t.requires_grad_(True)
+    C = dev(d["C_occ"]).requires_grad_(True)
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, float(d["lam"]))
+    E = g.df_coulomb_energy_screened(s, C, dev(d["occ"]), aux, dev(pi, torch.int32),
+                                     dev(pj, torch.int32), valid=dev(v, torch.bool), cholV=L)
+    E.backward()
+    close(float(E), float(d["E"]), rtol=1e-12)
+    for got, k in ((s.quat.grad, "g_quat"), (s.log_scale.grad, "g_log_scale"),
+                   (s.centers.grad, "g_centers"), (C.grad, "g_C")):
+        np.testing.assert_allclose(host(got), d[k], rtol=0, atol=2e-9 * np.abs(d[k]).max())
+
+
+def test_engine_step_j_vector_and_determinism(g):
+    """J_a = sum_P (P|a) d_P per list entry (0 on padding); two steps are bit-identical."""
+    d = load_golden("ref_rand48.npz")
+    pi, pj, v = d["pad_pi"], d["pad_pj"], d["pad_v"]
+    ref = _oracle_grad(d, pi, pj, v)
+    s = splats(g, d)
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, float(d["lam"]))
+    beta, R, KN = aux.quantities()
+    eng = g.RIJEngine(dev(pi, torch.int32), dev(pj, torch.int32), dev(v), s.n_basis,
+                      d["C_occ"].shape[1], beta, R.contiguous(), KN, L)
+    C, occ = dev(d["C_occ"]), dev(d["occ"])
+    outs = []
+    for _ in range(2):
+        o = eng.step(s.quat, s.log_scale, s.centers, C, occ)
+        outs.append({k: host(t).copy() for k, t in o.items()})
+    close(outs[0]["J"][:pi.size], ref["J"])
+    for k in outs[0]:
+        np.testing.assert_array_equal(outs[0][k], outs[1][k])
+    from gs_dft_b200.coulomb.engine import check_device_status
+    check_device_status()
+
+
+def test_sub_list_linearity(g):
+    """gamma is linear in the pair list: gamma(list) = gamma(first half) + gamma(second half)."""
+    d = load_golden("ref_co2.npz")
+    s = splats(g, d)
+    aux = g.init_product_aux(s)
+    C, occ = dev(d["C_occ"]), dev(d["occ"])
+    pi, pj = dev(d["ord_pi"], torch.int32), dev(d["ord_pj"], torch.int32)
+    n = pi.shape[0]
+    full = g.df_coulomb_gamma_screened(s, C, occ, aux, pi, pj)
+    h = n // 2
+    a = g.df_coulomb_gamma_screened(s, C, occ, aux, pi[:h], pj[:h])
+    b = g.df_coulomb_gamma_screened(s, C, occ, aux, pi[h:], pj[h:])
+    close(host(a + b), host(full), rtol=1e-12)
+
+
+def test_refresh_and_coulomb_ks(g):
+    """refresh(ks, basis) + ks(model, state) through the drop-in surface, against the oracle."""
+    d = load_golden("ref_rand48.npz")
+    s = splats(g, d)
+    ks = g.CoulombKS(coulomb=g.df(), screen=g.pairlist(eps=float(d["eps"])))
+    pad = ks.initial_pad(s)
+    st = g.refresh(ks, s, pad_to=pad)
+    assert st.pairs[0].shape[0] == pad
+    st2 = g.refresh(ks, s, like=st)
+    assert st2.pairs[0].shape[0] == pad
+    model = g.SplatModel(basis=s, C=dev(d["C_occ"]), occupations=dev(d["occ"]))
+    E = ks(model, st)
+    q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=float(d["eps"]), pad_to=pad)
+    ref = _oracle_grad(d, pi, pj, v)
+    close(float(E), ref["E"])
+
+
+def test_ethanol_slice_vs_oracle(g):
+    """Configuration 1 (ethanol, M=600): the full refresh on the GPU, the pair list checked
+    bit-exactly against the oracle's, and the step on a 3000-pair slice checked against the oracle
+    (the full 600 x n_sig oracle would take minutes)."""
+    from gs_dft_b200.systems import make_config
+    sy = make_config(1)
+    s = g.Splat(dev(sy.quat), dev(sy.log_scale), dev(sy.centers))
+    pi, pj, v = g.neighbor_pairs(s, eps=sy.eps)
+    q = O.full_quantities(sy.quat, sy.log_scale, sy.centers)
+    opi, opj, ov, n_sig = O.neighbor_pairs(q, eps=sy.eps)
+    np.testing.assert_array_equal(host(pi), opi)
+    np.testing.assert_array_equal(host(pj), opj)
+    sl = slice(0, 3000)
+    C, occ = dev(sy.C_occ), dev(sy.occ)
+    for t in (s.quat, s.log_scale, s.centers):
+        t.requires_grad_(True)
+    Ct = C.clone().requires_grad_(True)
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, sy.lam)
+    E = g.df_coulomb_energy_screened(s, Ct, occ, aux, pi[sl].contiguous(), pj[sl].contiguous(),
+                                     valid=v[sl].contiguous(), cholV=L)
+    E.backward()
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    Lo = O.aux_cholesky(O.aux_metric(*aq), sy.lam)
+    ref = O.energy_and_grad((sy.quat, sy.log_scale, sy.centers, sy.C_occ, sy.occ), aq, Lo,
+                            opi[sl], opj[sl], ov[sl])
+    close(float(E), ref["E"])
+    close(host(s.quat.grad), ref["g_quat"])
+    close(host(s.log_scale.grad), ref["g_log_scale"])
+    close(host(s.centers.grad), ref["g_centers"])
+    close(host(Ct.grad), ref["g_C"])
