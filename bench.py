@@ -38,8 +38,8 @@ L2_FLUSH_BYTES = 256 << 20
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20)
-    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--steps", type=int, default=60)
+    p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--config", type=int, default=1)
     p.add_argument("--no-e2e", action="store_true")
@@ -64,7 +64,7 @@ class Clocks:
         try:
             self.p = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", str(self.index), "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-i", str(self.index), "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
 
@@ -86,7 +86,7 @@ class Clocks:
                 sm.append(float(r[1]))
                 mx = max(mx, float(r[2]))
                 for k, n in enumerate(names):
-                    if "Active" in r[5 + k] or r[5 + k].strip() == "1":
+                    if r[5 + k].strip() in ("Active", "1"):
                         reasons.add(n)
             except (ValueError, IndexError):
                 continue
@@ -252,9 +252,10 @@ def main():
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches0 = lib.gsdft_kernel_launches()
+    clocks.start()
+    time.sleep(0.5)           # let the sampler come up before the timed region
     barrier()
     torch.cuda.synchronize()
-    clocks.start()
     for k in range(args.steps):
         flush.fill_(float(k))
         starts[k].record()

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <math.h>
 #include <stdio.h>
 
 #include "quad_table.h"
@@ -74,6 +75,27 @@ struct Sizer {
 };
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
+
+// Number of splits S of a second axis that best fills whole waves: `base` independent work items
+// become base*S items of 1/S the work each; resident capacity is `cap` CTAs. Returns the smallest
+// S in [1, max_s] within 1% of the best wave efficiency base*S / (ceil(base*S/cap) * cap).
+inline int best_splits(int64_t base, int64_t cap, int64_t max_s) {
+  if (cap < 1) cap = 1;
+  if (max_s < 1) max_s = 1;
+  double best = 0.0;
+  for (int64_t s = 1; s <= max_s; ++s) {
+    int64_t items = base * s;
+    int64_t waves = (items + cap - 1) / cap;
+    best = fmax(best, (double)items / (double)(waves * cap));
+  }
+  for (int64_t s = 1; s <= max_s; ++s) {
+    int64_t items = base * s;
+    int64_t waves = (items + cap - 1) / cap;
+    if ((double)items / (double)(waves * cap) >= best - 0.01) return (int)s;
+  }
+  return 1;
+}
 
 inline int grid_1d(int64_t n, int block) {
   int64_t g = (n + block - 1) / block;
@@ -162,40 +184,59 @@ __device__ __forceinline__ void pair_quantities_rn(const double* Ai, const doubl
 // ------------------------------------------------------------------------------------------------
 // Device: fast FP64 transcendentals for the node loop.
 //
-// exp2_nonpos(x) = 2^x for x <= 0. Reduction x = k + f with k = rint(x) (the 1.5*2^52 rounding
-// constant), 2^f from the degree-11 Chebyshev interpolant kExp2C (gen_constants.py), then the
-// exponent field is raised by k. x is clamped at -1020 so the result stays normal (the clamped
-// value, ~1e-307, is far below anything that reaches a sum).
+// wexp2<B>(a, t2, tab) = w_n 2^(a t2) for a t2 <= 0, table-driven (Tang, "Table-driven
+// implementation of the exponential function in IEEE floating-point arithmetic", ACM TOMS 15(2),
+// 1989). x = a t2 is never rounded on its own: kd = fma(a, t2, 1.5*2^(52-B)) rounds it to a multiple
+// n/2^B (n exact for |x| < 2^(31-B)), r = fma(a, t2, -n/2^B) is the reduced argument
+// (|r| <= 2^-(B+1)), and w_n 2^x = 2^k (w_n 2^(j/2^B)) p(r) with n = 2^B k + j. `tab` is node n's row
+// of kExp2WTab<B> in shared memory, so the quadrature weight comes for free; p is the Taylor
+// polynomial kExp2T5 (B = 6) or kExp2T4 (B = 8). Results below 2^-1000 are flushed to zero by
+// integer selects (nothing that small reaches a sum). 8-9 FP64 operations.
 // ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ double exp2_nonpos(double x) {
-  x = fmax(x, -1020.0);
-  const double kRound = 6755399441055744.0;   // 1.5 * 2^52
-  double kd = x + kRound;
-  int k = __double2loint(kd);
-  kd = kd - kRound;
-  double f = x - kd;
-  double p = kExp2C[11];
-  p = fma(p, f, kExp2C[10]);
-  p = fma(p, f, kExp2C[9]);
-  p = fma(p, f, kExp2C[8]);
-  p = fma(p, f, kExp2C[7]);
-  p = fma(p, f, kExp2C[6]);
-  p = fma(p, f, kExp2C[5]);
-  p = fma(p, f, kExp2C[4]);
-  p = fma(p, f, kExp2C[3]);
-  p = fma(p, f, kExp2C[2]);
-  p = fma(p, f, kExp2C[1]);
-  p = fma(p, f, kExp2C[0]);
-  int hi = __double2hiint(p) + (k << 20);
-  return __hiloint2double(hi, __double2loint(p));
+template <int B>
+__device__ __forceinline__ double wexp2(double a, double t2, const double* __restrict__ tab) {
+  const double kRound = 6755399441055744.0 / (double)(1 << B);  // 1.5 * 2^(52-B)
+  const double kd = fma(a, t2, kRound);
+  const int n = __double2loint(kd);
+  const double nd = kd - kRound;
+  const double r = fma(a, t2, -nd);
+  double p;
+  if (B == 8) {
+    p = kExp2T4[4];
+    p = fma(p, r, kExp2T4[3]);
+    p = fma(p, r, kExp2T4[2]);
+    p = fma(p, r, kExp2T4[1]);
+    p = fma(p, r, kExp2T4[0]);
+  } else {
+    p = kExp2T5[5];
+    p = fma(p, r, kExp2T5[4]);
+    p = fma(p, r, kExp2T5[3]);
+    p = fma(p, r, kExp2T5[2]);
+    p = fma(p, r, kExp2T5[1]);
+    p = fma(p, r, kExp2T5[0]);
+  }
+  const double v = tab[n & ((1 << B) - 1)] * p;
+  const int k = n >> B;
+  const bool keep = k >= -1000;
+  const int hi = keep ? __double2hiint(v) + (k << 20) : 0;
+  const int lo = keep ? __double2loint(v) : 0;
+  return __hiloint2double(hi, lo);
 }
 
-// rsqrt_pos(p) = 1/sqrt(p), p > 0 normal. Seed from the PTX instruction rsqrt.approx.f64, then one
+// Copy the per-node weighted tables kExp2WTab<B> (GSDFT_NQUAD x 2^B doubles) into shared memory
+// (all threads; the caller synchronises before use).
+template <int B>
+__device__ __forceinline__ void load_wexp2_tables(double* dst) {
+  const double* src = (B == 8) ? kExp2WTab8 : kExp2WTab6;
+  for (int k = threadIdx.x; k < GSDFT_NQUAD * (1 << B); k += blockDim.x) dst[k] = src[k];
+}
+
+// rsqrt_pos(p) = 1/sqrt(p), p > 0 normal. Seed from the PTX instruction rsqrt.approx.ftz.f64, then one
 // third-order (Halley-type) correction y = y0 (1 + e/2 + 3e^2/8), e = 1 - p y0^2, which triples the
 // number of correct bits of the seed.
 __device__ __forceinline__ double rsqrt_pos(double p) {
   double y0;
-  asm("rsqrt.approx.f64 %0, %1;" : "=d"(y0) : "d"(p));
+  asm("rsqrt.approx.ftz.f64 %0, %1;" : "=d"(y0) : "d"(p));
   double t = p * y0;
   double e = fma(-t, y0, 1.0);
   double c = fma(0.375, e, 0.5);

@@ -127,7 +127,15 @@ __global__ void pair_density_kernel(const int32_t* __restrict__ pi, const int32_
 // ------------------------------------------------------------------------------------------------
 constexpr int kFwThreads = 128;  // aux per CTA
 constexpr int kFwTile = 32;      // pair records per staged tile (32 x 144 B)
-constexpr int kFwNP = 2;         // pairs evaluated together per thread (independent chains)
+#ifndef GSDFT_FW_NP
+#define GSDFT_FW_NP 2
+#endif
+#ifndef GSDFT_FW_EXP2_BITS
+#define GSDFT_FW_EXP2_BITS 6
+#endif
+constexpr int kFwNP = GSDFT_FW_NP;  // pairs evaluated together per thread (independent chains)
+constexpr int kFwBits = GSDFT_FW_EXP2_BITS;  // 2^kFwBits-entry weighted exp2 table per node
+constexpr size_t kFwDynSmem = sizeof(double) * GSDFT_NQUAD * (1 << kFwBits);
 
 __global__ void __launch_bounds__(kFwThreads)
     j_forward_kernel(const double* __restrict__ rec, int64_t n_live,
@@ -136,6 +144,8 @@ __global__ void __launch_bounds__(kFwThreads)
                      double* __restrict__ partial) {
   __shared__ __align__(128) double tile[2][kFwTile * GSDFT_REC_FIELDS];
   __shared__ __align__(8) uint64_t bar[2];
+  extern __shared__ __align__(16) double etab[];  // GSDFT_NQUAD x 2^kFwBits weighted table
+  load_wexp2_tables<kFwBits>(etab);
   const int64_t P = blockIdx.x * (int64_t)kFwThreads + threadIdx.x;
   const bool has_aux = P < n_aux;
   const double b = has_aux ? beta[P] : 1.0;
@@ -208,8 +218,8 @@ __global__ void __launch_bounds__(kFwThreads)
           const double num = fma(m[p][0], p12, G0 * fma(m[p][1], G2, m[p][2] * G1));
           const double y = rsqrt_pos(prod);
           const double inv = y * y;
-          const double e = exp2_nonpos((num * inv) * t2);
-          coul[p] = fma(kQuadW[n] * y, e, coul[p]);
+          const double ew = wexp2<kFwBits>(num * inv, t2, etab + (n << kFwBits));
+          coul[p] = fma(y, ew, coul[p]);
         }
       }
 #pragma unroll
@@ -242,16 +252,21 @@ static int num_sms() {
   return sms;
 }
 
-// Pair splits for the forward grid: about 4 resident CTAs per SM over the aux tiles.
+// Pair splits of the forward grid: aux tiles x S CTAs filling whole waves of resident CTAs, with at
+// least two pair tiles per split.
 static int forward_splits(int64_t n_live, int64_t n_aux) {
+  static int per_sm = 0;
+  if (!per_sm) {
+    cudaFuncSetAttribute(j_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kFwDynSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, j_forward_kernel, kFwThreads,
+                                                  kFwDynSmem);
+    if (per_sm <= 0) per_sm = 1;
+  }
   int64_t aux_tiles = (n_aux + kFwThreads - 1) / kFwThreads;
-  int64_t want = (int64_t)num_sms() * 4;
-  int64_t S = (want + aux_tiles - 1) / aux_tiles;
-  int64_t max_s = (n_live + kFwTile - 1) / kFwTile;
-  if (S > max_s) S = max_s;
-  if (S < 1) S = 1;
-  if (S > 4096) S = 4096;
-  return (int)S;
+  int64_t cap = (int64_t)num_sms() * per_sm;
+  int64_t max_s = imin64(4096, imax64(1, n_live / (2 * kFwTile)));
+  return best_splits(aux_tiles, cap, max_s);
 }
 
 }  // namespace gsdft
@@ -324,7 +339,8 @@ extern "C" int gsdft_j_forward(const double* rec, int64_t n_live, const double* 
   int64_t per_split = (n_live + S - 1) / S;
   per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
   dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
-  j_forward_kernel<<<grid, kFwThreads, 0, st>>>(rec, n_live, beta, R, KN, n_aux, per_split, partial);
+  j_forward_kernel<<<grid, kFwThreads, kFwDynSmem, st>>>(rec, n_live, beta, R, KN, n_aux,
+                                                         per_split, partial);
   GSDFT_LAUNCHED("j_forward");
   sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(partial, S, n_aux, gamma);
   GSDFT_LAUNCHED("sum_splits");

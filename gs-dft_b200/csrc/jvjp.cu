@@ -10,9 +10,25 @@
 
 namespace gsdft {
 
+// Tuning knobs (compile-time): minimum resident CTAs per SM for the reverse kernel's register
+// budget, and the size 2^bits of the per-node weighted exp2 table.
+#ifndef GSDFT_VJP_MINB
+#define GSDFT_VJP_MINB 0
+#endif
+#if GSDFT_VJP_MINB > 0
+#define GSDFT_VJP_BOUNDS __launch_bounds__(kVjpThreads, GSDFT_VJP_MINB)
+#else
+#define GSDFT_VJP_BOUNDS __launch_bounds__(kVjpThreads)
+#endif
+#ifndef GSDFT_VJP_EXP2_BITS
+#define GSDFT_VJP_EXP2_BITS 6
+#endif
+
 constexpr int kAuxRec = 8;        // [beta, -log2e beta, R0, R1, R2, dbar KN, beta^2, 0]
 constexpr int kVjpThreads = 128;  // pairs per CTA (one per thread)
 constexpr int kVjpTile = 64;      // aux records per staged tile (64 x 64 B)
+constexpr int kVjpBits = GSDFT_VJP_EXP2_BITS;
+constexpr size_t kVjpDynSmem = sizeof(double) * GSDFT_NQUAD * (1 << kVjpBits);
 
 __global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const double* __restrict__ R,
                                     const double* __restrict__ KN, const double* __restrict__ d,
@@ -33,11 +49,13 @@ __global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const doubl
   o[7] = 0.0;
 }
 
-__global__ void __launch_bounds__(kVjpThreads)
+__global__ void GSDFT_VJP_BOUNDS
     j_vjp_kernel(const double* __restrict__ rec, int64_t n_live, const double* __restrict__ auxr,
                  int64_t n_aux, int64_t per_split, double* __restrict__ out) {
   __shared__ __align__(128) double tile[2][kVjpTile * kAuxRec];
   __shared__ __align__(8) uint64_t bar[2];
+  extern __shared__ __align__(16) double etab[];  // GSDFT_NQUAD x 2^kVjpBits weighted table
+  load_wexp2_tables<kVjpBits>(etab);
   const int64_t a = blockIdx.x * (int64_t)kVjpThreads + threadIdx.x;
   const bool live = a < n_live;
   const int64_t aa = live ? a : 0;
@@ -83,28 +101,27 @@ __global__ void __launch_bounds__(kVjpThreads)
       const double* ar = tl + k * kAuxRec;
       const double b = ar[0], cP = ar[1], dk = ar[5], b2 = ar[6];
       const double d0 = ar[2] - Pc[0], d1 = ar[3] - Pc[1], d2 = ar[4] - Pc[2];
-      double y[3], m[3], g[3], h[3];
+      double y[3], m[3];
 #pragma unroll
       for (int c = 0; c < 3; ++c) {
         y[c] = U[c] * d0 + U[3 + c] * d1 + U[6 + c] * d2;
         m[c] = (cP * L[c]) * (y[c] * y[c]);
-        g[c] = L[c] * b;
-        h[c] = L[c] + b;
       }
       double cf = 0.0, B[3] = {0, 0, 0}, C[3] = {0, 0, 0}, Z[6] = {0, 0, 0, 0, 0, 0};
 #pragma unroll
       for (int n = 0; n < GSDFT_NQUAD; ++n) {
         const double t2 = kQuadT2[n], t4 = kQuadT4[n];
-        const double G0 = fma(t2, h[0], g[0]);
-        const double G1 = fma(t2, h[1], g[1]);
-        const double G2 = fma(t2, h[2], g[2]);
+        // Gamma_k = lam_k (beta + t^2) + t^2 beta, rebuilt from two per-node scalars
+        const double sn = b + t2, un = t2 * b;
+        const double G0 = fma(L[0], sn, un);
+        const double G1 = fma(L[1], sn, un);
+        const double G2 = fma(L[2], sn, un);
         const double p12 = G1 * G2, p02 = G0 * G2, p01 = G0 * G1;
         const double prod = G0 * p12;
         const double num = fma(m[0], p12, fma(m[1], p02, m[2] * p01));
         const double yy = rsqrt_pos(prod);
         const double inv = yy * yy;
-        const double e = exp2_nonpos((num * inv) * t2);
-        const double f = (kQuadW[n] * yy) * e;
+                const double f = yy * wexp2<kVjpBits>(num * inv, t2, etab + (n << kVjpBits));
         cf += f;
         const double iG0 = p12 * inv, iG1 = p02 * inv, iG2 = p01 * inv;
         const double g0 = f * iG0, g1 = f * iG1, g2 = f * iG2;
@@ -357,16 +374,20 @@ static int vjp_num_sms() {
   return sms;
 }
 
-// Aux splits so that the grid has about 4 CTAs per SM even when the pair tiles alone are few.
+// Aux splits: pair tiles x S CTAs filling whole waves of resident CTAs (S <= 8, since the partial
+// sums take S x n_live x 13 doubles).
 static int vjp_splits(int64_t n_live, int64_t n_aux) {
+  static int per_sm = 0;
+  if (!per_sm) {
+    cudaFuncSetAttribute(j_vjp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)kVjpDynSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, j_vjp_kernel, kVjpThreads, kVjpDynSmem);
+    if (per_sm <= 0) per_sm = 1;
+  }
   int64_t tiles = (n_live + kVjpThreads - 1) / kVjpThreads;
-  int64_t want = (int64_t)vjp_num_sms() * 4;
-  int64_t S = (want + tiles - 1) / tiles;
-  int64_t max_s = (n_aux + kVjpTile - 1) / kVjpTile;
-  if (S > max_s) S = max_s;
-  if (S < 1) S = 1;
-  if (S > 64) S = 64;
-  return (int)S;
+  int64_t cap = (int64_t)vjp_num_sms() * per_sm;
+  int64_t max_s = imin64(8, imax64(1, n_aux / kVjpTile));
+  return best_splits(tiles, cap, max_s);
 }
 
 int device_status_vjp(int* out, int clear) {
@@ -406,7 +427,7 @@ extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta
   GSDFT_LAUNCHED("aux_vjp_pack");
   int64_t per_split = (n_aux + S - 1) / S;
   dim3 grid((unsigned)((n_live + kVjpThreads - 1) / kVjpThreads), (unsigned)S);
-  j_vjp_kernel<<<grid, kVjpThreads, 0, st>>>(rec, n_live, auxr, n_aux, per_split, part);
+  j_vjp_kernel<<<grid, kVjpThreads, kVjpDynSmem, st>>>(rec, n_live, auxr, n_aux, per_split, part);
   GSDFT_LAUNCHED("j_vjp");
   if (S > 1) {
     sum_vjp_splits_kernel<<<grid_1d(n_live * GSDFT_VJP_FIELDS, 256), 256, 0, st>>>(part, S, n_live,
