@@ -123,7 +123,7 @@ def cpu_sample_rate(sy, target_s=10.0, prob=None):
     t0 = time.perf_counter()
     O.energy_and_grad_c(sa, aq, L, pi[:k2], pj[:k2], v[:k2])
     dt = time.perf_counter() - t0
-    return n_aux * k2 / dt, k2, dt, len(os.sched_getaffinity(0))
+    return n_aux * k2 / dt, k2, dt, O.c_threads()
 
 
 def run_reference(args, rank, world):
@@ -144,7 +144,7 @@ def run_reference(args, rank, world):
         ts.append(time.perf_counter() - t0)
     t = sum(ts) / len(ts)
     val = n_aux * k / t / 1e9
-    cores = len(os.sched_getaffinity(0))
+    cores = O.c_threads()
     sample = (f"C/OpenMP restatement of the reference's RI-J step (oracle port; the JAX reference "
               f"cannot be installed offline): first {k} of {int((v != 0).sum())} live pairs x all "
               f"{n_aux} aux per step, energy + full gradient")

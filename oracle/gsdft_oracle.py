@@ -596,6 +596,10 @@ def c_lib():
         lib = ctypes.CDLL(path)
         P = ctypes.c_void_p
         lib.orc_set_nodes.argtypes = [P, P]
+        lib.orc_set_threads.argtypes = [ctypes.c_int]
+        lib.orc_get_threads.restype = ctypes.c_int
+        # every host core the process may run on (torchrun sets OMP_NUM_THREADS=1 per rank)
+        lib.orc_set_threads(len(os.sched_getaffinity(0)))
         lib.orc_gamma.argtypes = [P, ctypes.c_int64, P, P, P, ctypes.c_int64, P]
         lib.orc_vjp.argtypes = [P, ctypes.c_int64, P, P, P, ctypes.c_int64, P]
         t = np.ascontiguousarray(QUAD_T)
@@ -615,6 +619,11 @@ def pair_records(q_splat, C_occ, occ, pi, pj, valid):
     qa = pair_density(C_occ, occ, ci, cj, w[live])
     rec = np.concatenate([Lam, U.reshape(-1, 9), Pa, KN[:, None], qa[:, None]], axis=1)
     return np.ascontiguousarray(rec), live
+
+
+def c_threads():
+    """OpenMP threads the C oracle runs with."""
+    return int(c_lib().orc_get_threads())
 
 
 def energy_and_grad_c(sys_arrays, aux_q, L, pi, pj, valid, want_grad=True):

@@ -17,7 +17,14 @@
  * gsdft_oracle.py::_pair_vjp_integral for the derivation).
  */
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
+
+void orc_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+}
+
+int orc_get_threads(void) { return omp_get_max_threads(); }
 
 static double QT[20], QW[20];
 
