@@ -98,9 +98,10 @@ __global__ void pair_prep_kernel(const double* __restrict__ A9, const double* __
   o[GSDFT_REC_KN] = KN * kPref;
 }
 
-// q_a = w_a sum_o occ_o C_io C_jo, one warp per live pair (lanes stride o; fixed-order reduce).
+// q_a = w_a sum_o occ_o C_io C_jo, w_a the representative's (summed) weight; one warp per pair
+// (lanes stride o; fixed-order reduce).
 __global__ void pair_density_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
-                                    const double* __restrict__ w,
+                                    const double* __restrict__ rep_w,
                                     const int32_t* __restrict__ live_idx, int64_t n_live,
                                     const double* __restrict__ C, const double* __restrict__ occ,
                                     int64_t n_occ, double* __restrict__ rec) {
@@ -115,7 +116,7 @@ __global__ void pair_density_kernel(const int32_t* __restrict__ pi, const int32_
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (lane == 0) {
-    double q = w[e] * acc;
+    double q = rep_w[a] * acc;
     double* r = rec + a * GSDFT_REC_FIELDS;
     r[GSDFT_REC_Q] = q;
     r[GSDFT_REC_QK] = q * r[GSDFT_REC_KN];
@@ -153,6 +154,7 @@ __global__ void __launch_bounds__(kFwThreads)
   const double r1 = has_aux ? R[3 * P + 1] : 0.0;
   const double r2 = has_aux ? R[3 * P + 2] : 0.0;
   const double cP = -kLog2e * b;
+  const bool warp_active = __any_sync(0xffffffffu, has_aux);
   const int64_t a0 = blockIdx.y * per_split;
   const int64_t a1 = imin64(a0 + per_split, n_live);
   const int64_t npairs = a1 > a0 ? a1 - a0 : 0;
@@ -184,7 +186,8 @@ __global__ void __launch_bounds__(kFwThreads)
     if (!ok) break;
     const double* tl = tile[t & 1];
     const int cnt = (int)imin64(kFwTile, a1 - (a0 + (int64_t)t * kFwTile));
-    for (int k = 0; k < cnt; k += kFwNP) {
+    // a warp with no aux (the tail of the last aux tile) only takes part in the barriers
+    for (int k = 0; warp_active && k < cnt; k += kFwNP) {
       double m[kFwNP][3], g[kFwNP][3], h[kFwNP][3], qk[kFwNP], coul[kFwNP];
 #pragma unroll
       for (int p = 0; p < kFwNP; ++p) {
@@ -298,20 +301,20 @@ extern "C" int gsdft_device_status(int* status_host, int clear) {
 }
 
 extern "C" int gsdft_pair_prep(const double* A9, const double* mu, const double* N, int64_t M,
-                               const int32_t* pi, const int32_t* pj, const double* w,
-                               const int32_t* live_idx, int64_t n_live, const double* C_occ,
+                               const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                               const double* rep_w, int64_t n_rep, const double* C_occ,
                                const double* occ, int64_t n_occ, double* rec,
                                gsdft_stream_t stream) {
-  GSDFT_REQUIRE(M > 0 && n_live >= 0 && n_occ >= 0, "bad sizes");
-  if (n_live == 0) return GSDFT_OK;
-  GSDFT_REQUIRE(A9 && mu && N && pi && pj && w && live_idx && rec, "null pointer");
+  GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n_occ >= 0, "bad sizes");
+  if (n_rep == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(A9 && mu && N && pi && pj && rep_pos && rep_w && rec, "null pointer");
   GSDFT_REQUIRE(n_occ == 0 || (C_occ && occ), "null C_occ/occ");
   GSDFT_REQUIRE((reinterpret_cast<uintptr_t>(rec) & 15) == 0, "rec must be 16-byte aligned");
   cudaStream_t st = (cudaStream_t)stream;
-  pair_prep_kernel<<<grid_1d(n_live, 128), 128, 0, st>>>(A9, mu, N, pi, pj, live_idx, n_live, rec);
+  pair_prep_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(A9, mu, N, pi, pj, rep_pos, n_rep, rec);
   GSDFT_LAUNCHED("pair_prep");
-  pair_density_kernel<<<grid_1d(n_live * 32, 256), 256, 0, st>>>(pi, pj, w, live_idx, n_live,
-                                                                 C_occ, occ, n_occ, rec);
+  pair_density_kernel<<<grid_1d(n_rep * 32, 256), 256, 0, st>>>(pi, pj, rep_w, rep_pos, n_rep,
+                                                                C_occ, occ, n_occ, rec);
   GSDFT_LAUNCHED("pair_density");
   return GSDFT_OK;
 }

@@ -59,6 +59,7 @@ __global__ void GSDFT_VJP_BOUNDS
   const int64_t a = blockIdx.x * (int64_t)kVjpThreads + threadIdx.x;
   const bool live = a < n_live;
   const int64_t aa = live ? a : 0;
+  const bool warp_active = __any_sync(0xffffffffu, live);
   const double* rr = rec + aa * GSDFT_REC_FIELDS;
   double L[3], U[9], Pc[3];
 #pragma unroll
@@ -97,7 +98,8 @@ __global__ void GSDFT_VJP_BOUNDS
     if (!ok) break;
     const double* tl = tile[t & 1];
     const int cnt = (int)imin64(kVjpTile, P1 - (P0 + (int64_t)t * kVjpTile));
-    for (int k = 0; k < cnt; ++k) {
+    // a warp with no live pair (the tail of the last pair tile) only takes part in the barriers
+    for (int k = 0; warp_active && k < cnt; ++k) {
       const double* ar = tl + k * kAuxRec;
       const double b = ar[0], cP = ar[1], dk = ar[5], b2 = ar[6];
       const double d0 = ar[2] - Pc[0], d1 = ar[3] - Pc[1], d2 = ar[4] - Pc[2];
@@ -197,7 +199,8 @@ __device__ __forceinline__ void sym6_add_outer(double* s6, double c, const doubl
 __global__ void pair_chain_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
                                   const double* __restrict__ N, const int32_t* __restrict__ pi,
                                   const int32_t* __restrict__ pj,
-                                  const int32_t* __restrict__ live_idx, int64_t n_live,
+                                  const int32_t* __restrict__ live_idx,
+                                  const int32_t* __restrict__ twin, int64_t n_live,
                                   const double* __restrict__ rec, const double* __restrict__ sums,
                                   double* __restrict__ side, double* __restrict__ J) {
   int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -209,6 +212,7 @@ __global__ void pair_chain_kernel(const double* __restrict__ A9, const double* _
   const double q = r[GSDFT_REC_Q], kn = r[GSDFT_REC_KN], qk = r[GSDFT_REC_QK];
   const double SJ = sm[GSDFT_VJP_SJ];
   J[e] = kn * SJ;
+  if (twin[a] >= 0) J[twin[a]] = kn * SJ;  // the merged transpose carries the same integral
   const double KNbar = q * kPref * SJ;
   // eigenframe cotangent of A_hat: M_kl = -qk SZ_kl - 1/2 qk SD_k delta_kl
   double Mm[3][3];
@@ -336,11 +340,11 @@ __global__ void splat_reduce_kernel(const double* __restrict__ side,
   }
 }
 
-// g_C[s, o] = occ_o (sum_{pi=s} J w C[pj, o] + sum_{pj=s} J w C[pi, o]); one block per splat row,
-// threads over o, segments walked in order.
+// g_C[s, o] = occ_o (sum_{pi=s} J w C[pj, o] + sum_{pj=s} J w C[pi, o]) over representatives (w the
+// summed weight); one block per splat row, threads over o, segments walked in order.
 __global__ void density_grad_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
-                                    const double* __restrict__ w,
-                                    const int32_t* __restrict__ live_idx,
+                                    const int32_t* __restrict__ rep_pos,
+                                    const double* __restrict__ rep_w,
                                     const double* __restrict__ J,
                                     const int32_t* __restrict__ order_i,
                                     const int64_t* __restrict__ seg_i,
@@ -352,12 +356,14 @@ __global__ void density_grad_kernel(const int32_t* __restrict__ pi, const int32_
   for (int64_t o = threadIdx.x; o < n_occ; o += blockDim.x) {
     double acc = 0.0;
     for (int64_t e = seg_i[s]; e < seg_i[s + 1]; ++e) {
-      int64_t l = live_idx[order_i[e]];
-      acc = fma(J[l] * w[l], C[(int64_t)pj[l] * n_occ + o], acc);
+      const int32_t a = order_i[e];
+      const int64_t l = rep_pos[a];
+      acc = fma(J[l] * rep_w[a], C[(int64_t)pj[l] * n_occ + o], acc);
     }
     for (int64_t e = seg_j[s]; e < seg_j[s + 1]; ++e) {
-      int64_t l = live_idx[order_j[e]];
-      acc = fma(J[l] * w[l], C[(int64_t)pi[l] * n_occ + o], acc);
+      const int32_t a = order_j[e];
+      const int64_t l = rep_pos[a];
+      acc = fma(J[l] * rep_w[a], C[(int64_t)pi[l] * n_occ + o], acc);
     }
     gC[s * n_occ + o] = occ[o] * acc;
   }
@@ -438,19 +444,21 @@ extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta
 }
 
 extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
-                                const int32_t* pi, const int32_t* pj, const int32_t* live_idx,
-                                int64_t n_live, int64_t n, const double* rec, const double* sums,
-                                double* side, double* J, gsdft_stream_t stream) {
-  GSDFT_REQUIRE(M > 0 && n_live >= 0 && n >= n_live, "bad sizes");
+                                const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                                const int32_t* rep_twin, int64_t n_rep, int64_t n,
+                                const double* rec, const double* sums, double* side, double* J,
+                                gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n >= n_rep, "bad sizes");
   cudaStream_t st = (cudaStream_t)stream;
   if (n > 0) {
     GSDFT_REQUIRE(J, "null J");
     GSDFT_CUDA(cudaMemsetAsync(J, 0, n * sizeof(double), st));
   }
-  if (n_live == 0) return GSDFT_OK;
-  GSDFT_REQUIRE(A9 && mu && N && pi && pj && live_idx && rec && sums && side, "null pointer");
-  pair_chain_kernel<<<grid_1d(n_live, 128), 128, 0, st>>>(A9, mu, N, pi, pj, live_idx, n_live, rec,
-                                                          sums, side, J);
+  if (n_rep == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(A9 && mu && N && pi && pj && rep_pos && rep_twin && rec && sums && side,
+                "null pointer");
+  pair_chain_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(A9, mu, N, pi, pj, rep_pos, rep_twin,
+                                                         n_rep, rec, sums, side, J);
   GSDFT_LAUNCHED("pair_chain");
   return GSDFT_OK;
 }
@@ -468,20 +476,20 @@ extern "C" int gsdft_splat_reduce(const double* side, const int32_t* order_i, co
   return GSDFT_OK;
 }
 
-extern "C" int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const double* w,
-                                  const int32_t* live_idx, const double* J, const int32_t* order_i,
+extern "C" int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                                  const double* rep_w, const double* J, const int32_t* order_i,
                                   const int64_t* seg_i, const int32_t* order_j,
-                                  const int64_t* seg_j, int64_t n_live, int64_t M,
+                                  const int64_t* seg_j, int64_t n_rep, int64_t M,
                                   const double* C_occ, const double* occ, int64_t n_occ,
                                   double* g_C, gsdft_stream_t stream) {
-  GSDFT_REQUIRE(M > 0 && n_live >= 0 && n_occ >= 0, "bad sizes");
+  GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n_occ >= 0, "bad sizes");
   if (n_occ == 0) return GSDFT_OK;
   GSDFT_REQUIRE(seg_i && seg_j && C_occ && occ && g_C, "null pointer");
-  GSDFT_REQUIRE(n_live == 0 || (pi && pj && w && live_idx && J && order_i && order_j),
+  GSDFT_REQUIRE(n_rep == 0 || (pi && pj && rep_pos && rep_w && J && order_i && order_j),
                 "null pointer");
   int threads = n_occ >= 256 ? 256 : (int)((n_occ + 31) / 32 * 32);
   density_grad_kernel<<<(unsigned)M, threads, 0, (cudaStream_t)stream>>>(
-      pi, pj, w, live_idx, J, order_i, seg_i, order_j, seg_j, C_occ, occ, n_occ, g_C);
+      pi, pj, rep_pos, rep_w, J, order_i, seg_i, order_j, seg_j, C_occ, occ, n_occ, g_C);
   GSDFT_LAUNCHED("density_grad");
   return GSDFT_OK;
 }

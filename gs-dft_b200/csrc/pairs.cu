@@ -138,12 +138,72 @@ __global__ void live_flags_kernel(const double* __restrict__ w, int64_t n, char*
   if (k < n) flags[k] = w[k] != 0.0;
 }
 
-__global__ void gather_keys_kernel(const int32_t* __restrict__ key, const int32_t* __restrict__ live,
-                                   int64_t n_live, int32_t* __restrict__ out,
-                                   int32_t* __restrict__ iota) {
+__global__ void flat_keys_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                                 const int32_t* __restrict__ live, int64_t n_live, int64_t M,
+                                 int64_t* __restrict__ keys, int32_t* __restrict__ iota) {
   int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (a >= n_live) return;
-  out[a] = key[live[a]];
+  int32_t e = live[a];
+  keys[a] = (int64_t)pi[e] * M + pj[e];
+  iota[a] = (int32_t)a;
+}
+
+// Position of `key` in the sorted keys if it occurs exactly once, else -1.
+__device__ __forceinline__ int64_t find_unique(const int64_t* __restrict__ sk, int64_t n,
+                                               int64_t key) {
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    int64_t mid = (lo + hi) >> 1;
+    if (sk[mid] < key) lo = mid + 1; else hi = mid;
+  }
+  if (lo >= n || sk[lo] != key) return -1;
+  if (lo + 1 < n && sk[lo + 1] == key) return -1;
+  return lo;
+}
+
+// Twin merge: a live (i,j), i < j, whose transpose (j,i) is also live (each key occurring once)
+// becomes the representative of both; (j,i) is absorbed. Every other live entry represents itself.
+__global__ void twin_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                            const int32_t* __restrict__ live, int64_t n_live, int64_t M,
+                            const int64_t* __restrict__ sk, const int32_t* __restrict__ sv,
+                            int merge, char* __restrict__ is_rep, int32_t* __restrict__ twin) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_live) return;
+  int32_t e = live[a];
+  int64_t i = pi[e], j = pj[e];
+  int32_t tw = -1;
+  char rep = 1;
+  if (merge && i != j && find_unique(sk, n_live, i * M + j) >= 0) {
+    int64_t s = find_unique(sk, n_live, j * M + i);
+    if (s >= 0) {
+      if (i < j) tw = live[sv[s]];
+      else rep = 0;
+    }
+  }
+  is_rep[a] = rep;
+  twin[a] = tw;
+}
+
+__global__ void rep_gather_kernel(const int32_t* __restrict__ live, const int32_t* __restrict__ sel,
+                                  const int32_t* __restrict__ twin, const double* __restrict__ w,
+                                  int64_t n_rep, int32_t* __restrict__ rep_pos,
+                                  double* __restrict__ rep_w, int32_t* __restrict__ rep_twin) {
+  int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= n_rep) return;
+  int32_t a = sel[r];
+  int32_t e = live[a];
+  int32_t t = twin[a];
+  rep_pos[r] = e;
+  rep_twin[r] = t;
+  rep_w[r] = t >= 0 ? w[e] + w[t] : w[e];
+}
+
+__global__ void gather_keys_kernel(const int32_t* __restrict__ key, const int32_t* __restrict__ pos,
+                                   int64_t n, int32_t* __restrict__ out,
+                                   int32_t* __restrict__ iota) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n) return;
+  out[a] = key[pos[a]];
   iota[a] = (int32_t)a;
 }
 
@@ -158,12 +218,6 @@ __global__ void segment_bounds_kernel(const int32_t* __restrict__ sorted, int64_
     if (sorted[mid] < s) lo = mid + 1; else hi = mid;
   }
   seg[s] = lo;
-}
-
-static int end_bit_for(int64_t M) {
-  int b = 1;
-  while (b < 31 && (int64_t(1) << b) <= M) ++b;
-  return b;
 }
 
 struct PairsWs {
@@ -347,87 +401,150 @@ extern "C" int gsdft_stripe_pairs(const int32_t* pi, const int32_t* pj, const do
 }
 
 // ------------------------------------------------------------------------------------------------
-// Pair plan
+// Pair plan: representatives (live entries, transposed twins merged) and their groupings
 // ------------------------------------------------------------------------------------------------
 namespace {
-struct PlanWs {
+static int bits_for(int64_t v) {
+  int b = 1;
+  while (b < 63 && (int64_t(1) << b) <= v) ++b;
+  return b;
+}
+
+struct RepsWs {
   char* flags;
   int64_t* n_sel;
-  int32_t* keys;
-  int32_t* keys_sorted;
+  int32_t* live;
+  int64_t* keys;
+  int64_t* keys_sorted;
   int32_t* iota;
+  int32_t* vals_sorted;
+  char* is_rep;
+  int32_t* twin;
+  int32_t* sel;
   void* tmp;
   size_t tmp_bytes;
 };
 
-size_t plan_tmp_bytes(int64_t n) {
-  size_t a = 0, b = 0;
+size_t reps_tmp_bytes(int64_t n) {
+  size_t a = 0, b = 0, c = 0;
   cub::DeviceSelect::Flagged(nullptr, a, thrust::counting_iterator<int32_t>(0), (char*)nullptr,
                              (int32_t*)nullptr, (int64_t*)nullptr, (int)n);
-  cub::DeviceRadixSort::SortPairs(nullptr, b, (int32_t*)nullptr, (int32_t*)nullptr,
+  cub::DeviceRadixSort::SortPairs(nullptr, b, (int64_t*)nullptr, (int64_t*)nullptr,
                                   (int32_t*)nullptr, (int32_t*)nullptr, (int)n);
-  return a > b ? a : b;
+  cub::DeviceRadixSort::SortPairs(nullptr, c, (int32_t*)nullptr, (int32_t*)nullptr,
+                                  (int32_t*)nullptr, (int32_t*)nullptr, (int)n);
+  size_t m = a > b ? a : b;
+  return m > c ? m : c;
 }
 
 template <class C>
-void layout_plan(C& c, int64_t n, PlanWs* p, size_t tmp) {
+void layout_reps(C& c, int64_t n, RepsWs* p, size_t tmp) {
   auto f = c.template take<char>(n + 1);
   auto ns = c.template take<int64_t>(1);
-  auto k = c.template take<int32_t>(n + 1);
-  auto ks = c.template take<int32_t>(n + 1);
+  auto lv = c.template take<int32_t>(n + 1);
+  auto k = c.template take<int64_t>(n + 1);
+  auto ks = c.template take<int64_t>(n + 1);
   auto io = c.template take<int32_t>(n + 1);
+  auto vs = c.template take<int32_t>(n + 1);
+  auto ir = c.template take<char>(n + 1);
+  auto tw = c.template take<int32_t>(n + 1);
+  auto se = c.template take<int32_t>(n + 1);
   auto t = c.template take<char>(tmp);
-  if (p) *p = PlanWs{(char*)f, (int64_t*)ns, (int32_t*)k, (int32_t*)ks, (int32_t*)io, t, tmp};
+  if (p)
+    *p = RepsWs{(char*)f,      (int64_t*)ns,  (int32_t*)lv, (int64_t*)k,  (int64_t*)ks,
+                (int32_t*)io,  (int32_t*)vs,  (char*)ir,    (int32_t*)tw, (int32_t*)se,
+                t,             tmp};
 }
 }  // namespace
 
 extern "C" size_t gsdft_pair_plan_workspace_size(int64_t n, int64_t M) {
   (void)M;
   SizerP z;
-  layout_plan(z, n, nullptr, plan_tmp_bytes(n));
+  layout_reps(z, n, nullptr, reps_tmp_bytes(n));
   return z.s.off + 256;
 }
 
-extern "C" int gsdft_pair_plan(const int32_t* pi, const int32_t* pj, const double* w, int64_t n,
-                               int64_t M, int32_t* live_idx, int64_t* n_live_host, int32_t* order_i,
-                               int64_t* seg_i, int32_t* order_j, int64_t* seg_j, void* ws,
-                               size_t ws_bytes, gsdft_stream_t stream) {
-  GSDFT_REQUIRE(n >= 0 && n < (int64_t(1) << 31) && M > 0, "bad n or M");
-  GSDFT_REQUIRE(n_live_host && seg_i && seg_j, "null pointer");
+extern "C" int gsdft_pair_reps(const int32_t* pi, const int32_t* pj, const double* w, int64_t n,
+                               int64_t M, int merge_twins, int32_t* rep_pos, double* rep_w,
+                               int32_t* rep_twin, int64_t* n_rep_host, void* ws, size_t ws_bytes,
+                               gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n >= 0 && n < (int64_t(1) << 31) && M > 0 && M < (int64_t(1) << 31),
+                "bad n or M");
+  GSDFT_REQUIRE(n_rep_host, "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  PlanWs p;
-  size_t tmp = plan_tmp_bytes(n);
+  *n_rep_host = 0;
+  if (n == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(pi && pj && w && rep_pos && rep_w && rep_twin, "null pointer");
+  RepsWs p;
+  size_t tmp = reps_tmp_bytes(n);
   Carver c(ws, ws_bytes);
-  layout_plan(c, n, &p, tmp);
+  layout_reps(c, n, &p, tmp);
   if (!c.ok) return fail(GSDFT_ERR_ARG, "pair plan workspace too small (%zu < %zu)", ws_bytes, c.off);
-  if (n == 0) {
-    *n_live_host = 0;
-    GSDFT_CUDA(cudaMemsetAsync(seg_i, 0, (M + 1) * sizeof(int64_t), st));
-    GSDFT_CUDA(cudaMemsetAsync(seg_j, 0, (M + 1) * sizeof(int64_t), st));
-    return GSDFT_OK;
-  }
-  GSDFT_REQUIRE(pi && pj && w && live_idx && order_i && order_j, "null pointer");
   live_flags_kernel<<<grid_1d(n, 256), 256, 0, st>>>(w, n, p.flags);
   GSDFT_LAUNCHED("live_flags");
   size_t tb = tmp;
   GSDFT_CUDA(cub::DeviceSelect::Flagged(p.tmp, tb, thrust::counting_iterator<int32_t>(0), p.flags,
-                                        live_idx, p.n_sel, (int)n, st));
-  GSDFT_CUDA(cudaMemcpyAsync(n_live_host, p.n_sel, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+                                        p.live, p.n_sel, (int)n, st));
+  int64_t nl = 0;
+  GSDFT_CUDA(cudaMemcpyAsync(&nl, p.n_sel, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
   GSDFT_CUDA(cudaStreamSynchronize(st));
-  int64_t nl = *n_live_host;
-  int eb = end_bit_for(M);
+  if (nl == 0) return GSDFT_OK;
+  flat_keys_kernel<<<grid_1d(nl, 256), 256, 0, st>>>(pi, pj, p.live, nl, M, p.keys, p.iota);
+  GSDFT_LAUNCHED("flat_keys");
+  tb = tmp;
+  GSDFT_CUDA(cub::DeviceRadixSort::SortPairs(p.tmp, tb, p.keys, p.keys_sorted, p.iota,
+                                             p.vals_sorted, (int)nl, 0, bits_for(M * M), st));
+  twin_kernel<<<grid_1d(nl, 256), 256, 0, st>>>(pi, pj, p.live, nl, M, p.keys_sorted,
+                                                p.vals_sorted, merge_twins, p.is_rep, p.twin);
+  GSDFT_LAUNCHED("twin");
+  tb = tmp;
+  GSDFT_CUDA(cub::DeviceSelect::Flagged(p.tmp, tb, thrust::counting_iterator<int32_t>(0),
+                                        p.is_rep, p.sel, p.n_sel, (int)nl, st));
+  int64_t nr = 0;
+  GSDFT_CUDA(cudaMemcpyAsync(&nr, p.n_sel, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+  GSDFT_CUDA(cudaStreamSynchronize(st));
+  if (nr > 0) {
+    rep_gather_kernel<<<grid_1d(nr, 256), 256, 0, st>>>(p.live, p.sel, p.twin, w, nr, rep_pos,
+                                                        rep_w, rep_twin);
+    GSDFT_LAUNCHED("rep_gather");
+  }
+  *n_rep_host = nr;
+  return GSDFT_OK;
+}
+
+extern "C" size_t gsdft_pair_groups_workspace_size(int64_t n_rep, int64_t M) {
+  (void)M;
+  return gsdft_pair_plan_workspace_size(n_rep, M);
+}
+
+extern "C" int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                                 int64_t n_rep, int64_t M, int32_t* order_i, int64_t* seg_i,
+                                 int32_t* order_j, int64_t* seg_j, void* ws, size_t ws_bytes,
+                                 gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_rep >= 0 && n_rep < (int64_t(1) << 31) && M > 0, "bad n_rep or M");
+  GSDFT_REQUIRE(seg_i && seg_j, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  RepsWs p;
+  size_t tmp = reps_tmp_bytes(n_rep);
+  Carver c(ws, ws_bytes);
+  layout_reps(c, n_rep, &p, tmp);
+  if (!c.ok) return fail(GSDFT_ERR_ARG, "pair groups workspace too small (%zu < %zu)", ws_bytes, c.off);
+  GSDFT_REQUIRE(n_rep == 0 || (pi && pj && rep_pos && order_i && order_j), "null pointer");
+  int eb = bits_for(M);
   const int32_t* keysrc[2] = {pi, pj};
   int32_t* order[2] = {order_i, order_j};
   int64_t* seg[2] = {seg_i, seg_j};
+  int32_t* k32 = reinterpret_cast<int32_t*>(p.keys);
+  int32_t* k32s = reinterpret_cast<int32_t*>(p.keys_sorted);
   for (int s = 0; s < 2; ++s) {
-    if (nl > 0) {
-      gather_keys_kernel<<<grid_1d(nl, 256), 256, 0, st>>>(keysrc[s], live_idx, nl, p.keys, p.iota);
+    if (n_rep > 0) {
+      gather_keys_kernel<<<grid_1d(n_rep, 256), 256, 0, st>>>(keysrc[s], rep_pos, n_rep, k32, p.iota);
       GSDFT_LAUNCHED("gather_keys");
-      tb = tmp;
-      GSDFT_CUDA(cub::DeviceRadixSort::SortPairs(p.tmp, tb, p.keys, p.keys_sorted, p.iota, order[s],
-                                                 (int)nl, 0, eb, st));
+      size_t tb = tmp;
+      GSDFT_CUDA(cub::DeviceRadixSort::SortPairs(p.tmp, tb, k32, k32s, p.iota, order[s],
+                                                 (int)n_rep, 0, eb, st));
     }
-    segment_bounds_kernel<<<grid_1d(M + 1, 256), 256, 0, st>>>(p.keys_sorted, nl, M, seg[s]);
+    segment_bounds_kernel<<<grid_1d(M + 1, 256), 256, 0, st>>>(k32s, n_rep, M, seg[s]);
     GSDFT_LAUNCHED("segment_bounds");
   }
   return GSDFT_OK;

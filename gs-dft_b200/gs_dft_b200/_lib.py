@@ -39,8 +39,11 @@ SIGNATURES = {
                                  _pi64, _c_p, _sz, _c_p]),
     "gsdft_stripe_pairs": (_i32, [_c_p, _c_p, _c_p, _i64, _i32, _c_p, _c_p, _c_p, _c_p]),
     "gsdft_pair_plan_workspace_size": (_sz, [_i64, _i64]),
-    "gsdft_pair_plan": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _c_p, _pi64, _c_p, _c_p, _c_p, _c_p,
-                               _c_p, _sz, _c_p]),
+    "gsdft_pair_reps": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _i32, _c_p, _c_p, _c_p, _pi64, _c_p,
+                               _sz, _c_p]),
+    "gsdft_pair_groups_workspace_size": (_sz, [_i64, _i64]),
+    "gsdft_pair_groups": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _sz,
+                                 _c_p]),
     "gsdft_product_aux": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64,
                                  ctypes.POINTER(ctypes.c_double), _i32, _c_p, _c_p, _c_p]),
     "gsdft_aux_quantities": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p]),
@@ -56,8 +59,8 @@ SIGNATURES = {
     "gsdft_j_vjp_workspace_size": (_sz, [_i64, _i64]),
     "gsdft_j_vjp": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _sz,
                            _c_p]),
-    "gsdft_pair_chain": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
-                                _c_p, _c_p, _c_p]),
+    "gsdft_pair_chain": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p,
+                                _c_p, _c_p, _c_p, _c_p]),
     "gsdft_splat_reduce": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p,
                                   _c_p]),
     "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64,

@@ -28,32 +28,55 @@ def _i64():
 
 @dataclass
 class PairPlan:
-    """Refresh-time grouping of a pair list (live entries, by-pi and by-pj orders)."""
+    """Refresh-time plan of a pair list: the representatives this device evaluates (a contiguous
+    slice of all of them) and their groupings by pi and by pj.
 
-    n: int
-    n_live: int
-    live_idx: torch.Tensor
+    A representative is a live entry (w != 0); with ``merge_twins`` a live (i,j), i < j, whose
+    transpose (j,i) is also live stands for both — the two carry the same integral — with the
+    summed weight, and J is written to both list positions."""
+
+    n: int              # list length
+    n_rep_total: int    # representatives over the whole list
+    r0: int             # this slice: representatives [r0, r1)
+    r1: int
+    rep_pos: torch.Tensor
+    rep_w: torch.Tensor
+    rep_twin: torch.Tensor
     order_i: torch.Tensor
     seg_i: torch.Tensor
     order_j: torch.Tensor
     seg_j: torch.Tensor
 
+    @property
+    def n_rep(self) -> int:
+        return self.r1 - self.r0
 
-def make_plan(pi: torch.Tensor, pj: torch.Tensor, w: torch.Tensor, M: int) -> PairPlan:
+
+def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: bool = True):
     dev = pi.device
     n = int(pi.shape[0])
-    live = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
-    oi = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
-    oj = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
-    si = torch.empty(M + 1, dtype=torch.int64, device=dev)
-    sj = torch.empty(M + 1, dtype=torch.int64, device=dev)
+    pos = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
+    rw = torch.empty(max(n, 1), dtype=torch.float64, device=dev)
+    tw = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
     ws_bytes = lib.gsdft_pair_plan_workspace_size(n, M)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
-    nl = _i64()
-    lib.call("gsdft_pair_plan", ptr(pi), ptr(pj), ptr(w), n, M, ptr(live), ctypes.byref(nl),
-             ptr(oi), ptr(si), ptr(oj), ptr(sj), ptr(ws), ws_bytes, stream_handle(dev))
-    return PairPlan(n=n, n_live=int(nl.value), live_idx=live, order_i=oi, seg_i=si, order_j=oj,
-                    seg_j=sj)
+    nr = _i64()
+    lib.call("gsdft_pair_reps", ptr(pi), ptr(pj), ptr(w), n, M, int(bool(merge_twins)), ptr(pos),
+             ptr(rw), ptr(tw), ctypes.byref(nr), ptr(ws), ws_bytes, stream_handle(dev))
+    n_rep = int(nr.value)
+    r0, r1 = n_rep * rank // world, n_rep * (rank + 1) // world
+    pos, rw, tw = pos[r0:max(r1, r0 + 1)], rw[r0:max(r1, r0 + 1)], tw[r0:max(r1, r0 + 1)]
+    k = r1 - r0
+    oi = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
+    oj = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
+    si = torch.empty(M + 1, dtype=torch.int64, device=dev)
+    sj = torch.empty(M + 1, dtype=torch.int64, device=dev)
+    gb = lib.gsdft_pair_groups_workspace_size(k, M)
+    gws = torch.empty(gb, dtype=torch.uint8, device=dev)
+    lib.call("gsdft_pair_groups", ptr(pi), ptr(pj), ptr(pos), k, M, ptr(oi), ptr(si), ptr(oj),
+             ptr(sj), ptr(gws), gb, stream_handle(dev))
+    return PairPlan(n=n, n_rep_total=n_rep, r0=r0, r1=r1, rep_pos=pos, rep_w=rw, rep_twin=tw,
+                    order_i=oi, seg_i=si, order_j=oj, seg_j=sj)
 
 
 def splat_quantities(quat, log_scale):
@@ -73,9 +96,11 @@ class RIJEngine:
         pi, pj: int32 pair indices (device); w: float64 weights (0 = padding; 1 ordered; 2 unique).
         M: number of splats; n_occ: occupied orbitals.
         beta, R, KN: the aux quantities; L: lower Cholesky factor of V + lam I (row-major).
+        rank, world: this device evaluates representatives [n_rep*rank//world, n_rep*(rank+1)//world).
+        merge_twins: evaluate each (i,j)/(j,i) pair of a live transposed twin once (same integral).
     """
 
-    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L):
+    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1, merge_twins=True):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi = pi.contiguous()
@@ -83,8 +108,8 @@ class RIJEngine:
         self.w = w.to(F64).contiguous()
         self.beta, self.R, self.KN, self.L = beta, R, KN, L
         self.n_aux = int(beta.shape[0])
-        self.plan = make_plan(self.pi, self.pj, self.w, self.M)
-        dev, nl, n = self.device, self.plan.n_live, self.plan.n
+        self.plan = make_plan(self.pi, self.pj, self.w, self.M, rank, world, merge_twins)
+        dev, nl, n = self.device, self.plan.n_rep, self.plan.n
         e = lambda *s: torch.empty(s, dtype=F64, device=dev)
         self.A9, self.N = e(self.M, 9), e(self.M)
         self.rec = e(max(nl, 1), REC_FIELDS)
@@ -122,12 +147,12 @@ class RIJEngine:
     def forward_local(self, quat, log_scale, centers, C_occ, occ):
         """Splat quantities, pair prep and this device's gamma (before any allreduce)."""
         s = stream_handle(self.device)
-        nl = self.plan.n_live
+        nl = self.plan.n_rep
         lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),
                  ptr(self.N), s)
         lib.call("gsdft_pair_prep", ptr(self.A9), ptr(centers), ptr(self.N), self.M, ptr(self.pi),
-                 ptr(self.pj), ptr(self.w), ptr(self.plan.live_idx), nl, ptr(C_occ), ptr(occ),
-                 self.n_occ, ptr(self.rec), s)
+                 ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_w), nl, ptr(C_occ),
+                 ptr(occ), self.n_occ, ptr(self.rec), s)
         end = self._bracket("forward")
         lib.call("gsdft_j_forward", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
                  self.n_aux, ptr(self.gamma), ptr(self.ws), self.ws_bytes, s)
@@ -144,21 +169,21 @@ class RIJEngine:
     def backward_local(self, centers, C_occ, occ, g_E=None):
         """This device's pre-chart splat cotangents (gA6, gmu, gN), J per list entry and g_C."""
         s = stream_handle(self.device)
-        nl = self.plan.n_live
+        nl = self.plan.n_rep
         end = self._bracket("vjp")
         lib.call("gsdft_j_vjp", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
                  ptr(self.d), ptr(g_E), self.n_aux, ptr(self.sums), ptr(self.ws), self.ws_bytes, s)
         if end is not None:
             end.record(torch.cuda.current_stream(self.device))
         lib.call("gsdft_pair_chain", ptr(self.A9), ptr(centers), ptr(self.N), self.M,
-                 ptr(self.pi), ptr(self.pj), ptr(self.plan.live_idx), nl, self.plan.n,
-                 ptr(self.rec), ptr(self.sums), ptr(self.side), ptr(self.J), s)
+                 ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_twin), nl,
+                 self.plan.n, ptr(self.rec), ptr(self.sums), ptr(self.side), ptr(self.J), s)
         lib.call("gsdft_splat_reduce", ptr(self.side), ptr(self.plan.order_i),
                  ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl, self.M,
                  ptr(self.gA6), ptr(self.gmu), ptr(self.gN), s)
         if self.n_occ > 0:
-            lib.call("gsdft_density_grad", ptr(self.pi), ptr(self.pj), ptr(self.w),
-                     ptr(self.plan.live_idx), ptr(self.J), ptr(self.plan.order_i),
+            lib.call("gsdft_density_grad", ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos),
+                     ptr(self.plan.rep_w), ptr(self.J), ptr(self.plan.order_i),
                      ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl,
                      self.M, ptr(C_occ), ptr(occ), self.n_occ, ptr(self.g_C), s)
         return self.gA6, self.gmu, self.gN, self.g_C

@@ -6,11 +6,12 @@ Replaces the DF branch of gs_dft/ks/shard.py:169-245 (``shard_map`` over mesh ax
 per-step replica ``pmean`` of gs_dft/ks/shard.py:44-65, which is not needed because every rank
 computes bit-identical replicated values.
 
-Partition: contiguous ranges of the (lexsorted) list, balanced on LIVE pairs — every live pair
-costs the same N_aux integrals, and zero-weight padding costs nothing, so equal live counts are
-equal work; contiguity keeps each rank's per-splat scatter local. The reference instead deals the
-padded list round-robin (``stripe_pairs``) because its padding is appended; striped lists are
-accepted too (a stripe is just a different order of the same pairs).
+Partition: every rank builds the same refresh-time plan of the whole list (live entries, with each
+(i,j)/(j,i) twin merged into one representative) and evaluates a contiguous slice of the
+representatives, equal to within one: every representative costs the same N_aux integrals and
+padding costs nothing, so equal counts are equal work, and contiguity keeps each rank's per-splat
+scatter local. The reference instead deals the padded list round-robin (``stripe_pairs``) because
+its padding is appended; striped lists are accepted too (a stripe only reorders the same pairs).
 """
 from __future__ import annotations
 
@@ -19,25 +20,7 @@ import torch
 from ..coulomb.engine import RIJEngine
 from ..screening.pairs import pair_weight, stripe_pairs
 
-__all__ = ["partition_pairs", "ShardedRIJ", "stripe_pairs"]
-
-
-def partition_pairs(valid: torch.Tensor, G: int) -> list[tuple[int, int]]:
-    """G contiguous [start, end) ranges of the list with live counts equal to within one."""
-    w = pair_weight(valid)
-    n = int(w.shape[0])
-    live = (w != 0).to(torch.int64)
-    csum = torch.cumsum(live, 0)
-    total = int(csum[-1].item()) if n else 0
-    bounds = [0]
-    for g in range(1, G):
-        target = (total * g) // G
-        # first index whose prefix live count exceeds the target
-        k = int(torch.searchsorted(csum, torch.tensor([target], device=csum.device),
-                                   right=True).item()) if n else 0
-        bounds.append(min(max(k, bounds[-1]), n))
-    bounds.append(n)
-    return [(bounds[g], bounds[g + 1]) for g in range(G)]
+__all__ = ["ShardedRIJ", "stripe_pairs"]
 
 
 class ShardedRIJ:
@@ -50,15 +33,11 @@ class ShardedRIJ:
     def __init__(self, pi, pj, valid, M, n_occ, beta, R, KN, L, rank: int, world: int,
                  group=None, engine_cls=RIJEngine):
         self.rank, self.world, self.group = rank, world, group
-        self.ranges = partition_pairs(valid, world)
-        s, e = self.ranges[rank]
-        w = pair_weight(valid)
-        self.engine = engine_cls(pi[s:e].contiguous(), pj[s:e].contiguous(), w[s:e].contiguous(),
-                                 M, n_occ, beta, R, KN, L)
+        self.engine = engine_cls(pi.contiguous(), pj.contiguous(), pair_weight(valid).contiguous(),
+                                 M, n_occ, beta, R, KN, L, rank=rank, world=world)
         self.M, self.n_occ = int(M), int(n_occ)
-        dev = pi.device
         self.packed = torch.empty(10 * self.M + self.M * max(self.n_occ, 1),
-                                  dtype=torch.float64, device=dev)
+                                  dtype=torch.float64, device=pi.device)
 
     def step(self, quat, log_scale, centers, C_occ, occ, grad=True):
         import torch.distributed as dist

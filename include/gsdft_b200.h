@@ -127,16 +127,27 @@ int gsdft_pairs_build(const double* A9, const double* mu, const double* N, int64
 int gsdft_stripe_pairs(const int32_t* pi, const int32_t* pj, const double* w, int64_t n, int G,
                        int32_t* pi_out, int32_t* pj_out, double* w_out, gsdft_stream_t stream);
 
-/* Refresh-time plan of a pair list: the live entries (w != 0) in list order, and the grouping of
- * live entries by pi and by pj (stable) used by the deterministic per-splat reductions.
- * order_i/order_j (n_live) index live entries; seg_i/seg_j (M+1) are segment offsets.
- * Synchronises the stream (returns n_live). No reference counterpart (the reference scatters with
- * segment_sum inside autodiff). */
+/* Refresh-time plan of a pair list, step 1 — representatives: the live entries (w != 0) in list
+ * order, where with merge_twins != 0 a live (i,j), i < j, whose transpose (j,i) is also live (each
+ * occurring once) represents both: the two carry the same 3-centre integral, so the pair is
+ * evaluated once with the summed weight, and J is written to both list positions. rep_pos (list
+ * position), rep_w (summed weight), rep_twin (list position of the merged transpose or -1), each
+ * n_rep long (at most the live count). Synchronises the stream (returns n_rep). The identity is the
+ * one behind the reference's unique-pair mode (gs_dft/screening/pairs.py:229-233; its test
+ * tests/unit/test_pair_tricks.py:81-100); the reference evaluates both orientations. */
 size_t gsdft_pair_plan_workspace_size(int64_t n, int64_t M);
-int gsdft_pair_plan(const int32_t* pi, const int32_t* pj, const double* w, int64_t n, int64_t M,
-                    int32_t* live_idx, int64_t* n_live_host, int32_t* order_i, int64_t* seg_i,
-                    int32_t* order_j, int64_t* seg_j, void* ws, size_t ws_bytes,
-                    gsdft_stream_t stream);
+int gsdft_pair_reps(const int32_t* pi, const int32_t* pj, const double* w, int64_t n, int64_t M,
+                    int merge_twins, int32_t* rep_pos, double* rep_w, int32_t* rep_twin,
+                    int64_t* n_rep_host, void* ws, size_t ws_bytes, gsdft_stream_t stream);
+
+/* Step 2 — groupings of a contiguous slice of representatives (all of them on one device, one
+ * rank's share on several): order_i / order_j (n_rep) list the slice's representatives stably
+ * sorted by pi / pj, seg_i / seg_j (M+1) are the segment offsets. Used by the deterministic
+ * per-splat reductions (the reference scatters with segment sums inside autodiff). */
+size_t gsdft_pair_groups_workspace_size(int64_t n_rep, int64_t M);
+int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos, int64_t n_rep,
+                      int64_t M, int32_t* order_i, int64_t* seg_i, int32_t* order_j,
+                      int64_t* seg_j, void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
 /* ---- auxiliary basis, metric, factor ------------------------------------------------------------ */
 
@@ -167,19 +178,20 @@ int gsdft_aux_cholesky(double* V, int64_t n_aux, double lam, void* ws, size_t ws
 
 /* ---- per-step J-build ---------------------------------------------------------------------------- */
 
-/* Per live pair: A_hat, P, KN (gs_dft/coulomb/stream.py:203-215), the eigen-decomposition of A_hat
- * (gs_dft/coulomb/ri.py:145), and q = w sum_o occ_o C_io C_jo (gs_dft/coulomb/ri.py:456).
- * rec is (n_live, GSDFT_REC_FIELDS). */
+/* Per pair representative: A_hat, P, KN (gs_dft/coulomb/stream.py:203-215), the eigen-decomposition of A_hat
+ * (gs_dft/coulomb/ri.py:145), and q = w sum_o occ_o C_io C_jo (gs_dft/coulomb/ri.py:456), for
+ * each representative (w its summed weight).
+ * rec is (n_rep, GSDFT_REC_FIELDS). */
 int gsdft_pair_prep(const double* A9, const double* mu, const double* N, int64_t M,
-                    const int32_t* pi, const int32_t* pj, const double* w,
-                    const int32_t* live_idx, int64_t n_live, const double* C_occ,
-                    const double* occ, int64_t n_occ, double* rec, gsdft_stream_t stream);
+                    const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                    const double* rep_w, int64_t n_rep, const double* C_occ, const double* occ,
+                    int64_t n_occ, double* rec, gsdft_stream_t stream);
 
-/* gamma_P = sum_a (P|a) q_a over the live pairs, the 3-centre integral fused with the contraction
+/* gamma_P = sum_a (P|a) q_a over the pair representatives, the 3-centre integral fused with the contraction
  * (never stored). Replaces df_coulomb_gamma_screened + full_isobra_block
  * (gs_dft/coulomb/ri.py:436-469, 126-185). */
-size_t gsdft_j_forward_workspace_size(int64_t n_live, int64_t n_aux);
-int gsdft_j_forward(const double* rec, int64_t n_live, const double* beta, const double* R,
+size_t gsdft_j_forward_workspace_size(int64_t n_rep, int64_t n_aux);
+int gsdft_j_forward(const double* rec, int64_t n_rep, const double* beta, const double* R,
                     const double* KN, int64_t n_aux, double* gamma, void* ws, size_t ws_bytes,
                     gsdft_stream_t stream);
 
@@ -189,35 +201,36 @@ size_t gsdft_j_solve_workspace_size(int64_t n_aux);
 int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d, double* E,
                   void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
-/* Reverse pass over (live pair x aux): with dbar = g_E * d (g_E device scalar, NULL = 1), the
- * per-pair sums (GSDFT_VJP_FIELDS, n_live) from which J_a = sum_P (P|a) dbar_P and the cotangents
- * of A_hat, P, KN follow; sums is (n_live, GSDFT_VJP_FIELDS). Replaces the node reverse nodes_bwd and the eigh / dp2 autodiff
+/* Reverse pass over (representative x aux): with dbar = g_E * d (g_E device scalar, NULL = 1), the
+ * per-pair sums, (n_rep, GSDFT_VJP_FIELDS), from which J_a = sum_P (P|a) dbar_P and the cotangents
+ * of A_hat, P, KN follow. Replaces the node reverse nodes_bwd and the eigh / dp2 autodiff
  * (gs_dft/coulomb/ri.py:145-147,190-222). */
-size_t gsdft_j_vjp_workspace_size(int64_t n_live, int64_t n_aux);
-int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta, const double* R,
+size_t gsdft_j_vjp_workspace_size(int64_t n_rep, int64_t n_aux);
+int gsdft_j_vjp(const double* rec, int64_t n_rep, const double* beta, const double* R,
                 const double* KN, const double* d, const double* g_E, int64_t n_aux,
                 double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
-/* Chain per live pair: sums -> cotangents of A_hat, P, KN -> per-side (A_i, mu_i, N_i), (A_j, mu_j,
- * N_j) contributions side (n_live, GSDFT_SIDE_FIELDS); J (n, list order; 0 on dead entries). The
+/* Chain per representative: sums -> cotangents of A_hat, P, KN -> per-side (A_i, mu_i, N_i), (A_j, mu_j,
+ * N_j) contributions side (n_rep, GSDFT_SIDE_FIELDS); J (n, list order: written at each
+ * representative's position and at its merged transpose's; 0 on zero-weight entries). The
  * reverse of gs_dft/coulomb/stream.py:203-215. */
 int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
-                     const int32_t* pi, const int32_t* pj, const int32_t* live_idx,
-                     int64_t n_live, int64_t n, const double* rec, const double* sums,
-                     double* side, double* J, gsdft_stream_t stream);
+                     const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                     const int32_t* rep_twin, int64_t n_rep, int64_t n, const double* rec,
+                     const double* sums, double* side, double* J, gsdft_stream_t stream);
 
 /* Deterministic per-splat sums of the side contributions (plan groupings) -> gA6 (M,6), gmu (M,3),
  * gN (M). Replaces the segment scatter of JAX autodiff through A[pi], A[pj]. */
 int gsdft_splat_reduce(const double* side, const int32_t* order_i, const int64_t* seg_i,
-                       const int32_t* order_j, const int64_t* seg_j, int64_t n_live, int64_t M,
+                       const int32_t* order_j, const int64_t* seg_j, int64_t n_rep, int64_t M,
                        double* gA6, double* gmu, double* gN, gsdft_stream_t stream);
 
 /* g_C[i,o] = occ_o (sum_{a: pi=i} J_a w_a C[pj_a,o] + sum_{a: pj=i} J_a w_a C[pi_a,o]): the gradient
  * through q_a (gs_dft/coulomb/ri.py:456). */
-int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const double* w,
-                       const int32_t* live_idx, const double* J, const int32_t* order_i,
+int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                       const double* rep_w, const double* J, const int32_t* order_i,
                        const int64_t* seg_i, const int32_t* order_j, const int64_t* seg_j,
-                       int64_t n_live, int64_t M, const double* C_occ, const double* occ,
+                       int64_t n_rep, int64_t M, const double* C_occ, const double* occ,
                        int64_t n_occ, double* g_C, gsdft_stream_t stream);
 
 #ifdef __cplusplus

@@ -50,3 +50,22 @@ def test_product_path_has_no_cpu_fallback():
                 src = open(os.path.join(dirpath, f)).read()
                 assert not re.search(r"^\s*(import|from)\s+\S*oracle", src, re.M), f
                 assert "gsdft_oracle" not in src, f
+
+
+def header_arities():
+    """{function: parameter count} parsed from the header's prototypes."""
+    text = open(HEADER).read()
+    out = {}
+    for m in re.finditer(r"^(?:int64_t|int|size_t|const char\*)\s+(gsdft_\w+)\s*\(([^;]*?)\);",
+                         text, re.M | re.S):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_arity_matches_header():
+    from gs_dft_b200._lib import SIGNATURES
+    ar = header_arities()
+    assert sorted(ar) == header_functions()
+    for name, (_, args) in SIGNATURES.items():
+        assert len(args) == ar[name], f"{name}: ctypes {len(args)} args, header {ar[name]}"

@@ -287,3 +287,51 @@ def test_ethanol_slice_vs_oracle(g):
     close(host(s.log_scale.grad), ref["g_log_scale"])
     close(host(s.centers.grad), ref["g_centers"])
     close(host(Ct.grad), ref["g_C"])
+
+
+def test_twin_merge_matches_unmerged_and_halves_the_work(g):
+    """(i,j) and (j,i) carry the same integral: the plan evaluates each live transposed twin once
+    with the summed weight. Outputs agree with the unmerged evaluation (and with the oracle, which
+    evaluates every ordered entry) to 1e-10; a unique list has no twins to merge."""
+    d = load_golden("ref_co2.npz")
+    pi, pj, v = d["pad_pi"], d["pad_pj"], d["pad_v"]
+    s = splats(g, d)
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, float(d["lam"]))
+    beta, R, KN = aux.quantities()
+    C, occ = dev(d["C_occ"]), dev(d["occ"])
+    outs = {}
+    for merge in (True, False):
+        eng = g.RIJEngine(dev(pi, torch.int32), dev(pj, torch.int32), dev(v), s.n_basis,
+                          d["C_occ"].shape[1], beta, R.contiguous(), KN, L, merge_twins=merge)
+        o = eng.step(s.quat, s.log_scale, s.centers, C, occ)
+        outs[merge] = ({k: host(t).copy() for k, t in o.items()}, eng.plan)
+    n_live = int(v.sum())
+    n_diag = int(np.sum((pi == pj) & v))
+    assert outs[False][1].n_rep_total == n_live
+    assert outs[True][1].n_rep_total == n_diag + (n_live - n_diag) // 2
+    for k in ("E", "gamma", "J", "g_quat", "g_log_scale", "g_centers", "g_C"):
+        close(outs[True][0][k], outs[False][0][k])
+    ref = _oracle_grad(d, pi, pj, v)
+    close(outs[True][0]["J"][:pi.size], ref["J"])
+    ui, uj, uw = d["uni_pi"], d["uni_pj"], d["uni_w"]
+    eng = g.RIJEngine(dev(ui, torch.int32), dev(uj, torch.int32), dev(uw), s.n_basis,
+                      d["C_occ"].shape[1], beta, R.contiguous(), KN, L)
+    assert eng.plan.n_rep_total == int((uw != 0).sum())
+
+
+def test_sharded_slices_cover_the_representatives(g):
+    """Rank slices of the plan partition the representatives contiguously and evenly."""
+    d = load_golden("ref_rand48.npz")
+    pi, pj, v = dev(d["pad_pi"], torch.int32), dev(d["pad_pj"], torch.int32), dev(d["pad_v"])
+    from gs_dft_b200.coulomb.engine import make_plan
+    M = d["quat"].shape[0]
+    full = make_plan(pi, pj, v, M)
+    for world in (2, 3, 8):
+        sl = [make_plan(pi, pj, v, M, r, world) for r in range(world)]
+        assert sl[0].r0 == 0 and sl[-1].r1 == full.n_rep_total
+        assert all(sl[k].r1 == sl[k + 1].r0 for k in range(world - 1))
+        sizes = [p.n_rep for p in sl]
+        assert max(sizes) - min(sizes) <= 1
+        got = np.concatenate([host(p.rep_pos[:p.n_rep]) for p in sl])
+        np.testing.assert_array_equal(got, host(full.rep_pos[:full.n_rep]))

@@ -29,8 +29,12 @@ def _full(g6):
 class OracleEngine:
     """CPU stand-in for RIJEngine with the same stage methods, computed by the oracle."""
 
-    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L):
-        self.pi, self.pj, self.w = pi.numpy(), pj.numpy(), w.numpy()
+    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1):
+        # this rank's contiguous share of the live entries (the sum over pairs is order-free)
+        live = np.nonzero(w.numpy() != 0)[0]
+        r0, r1 = len(live) * rank // world, len(live) * (rank + 1) // world
+        sel = live[r0:r1]
+        self.pi, self.pj, self.w = pi.numpy()[sel], pj.numpy()[sel], w.numpy()[sel]
         self.M, self.n_occ = M, n_occ
         self.aq = (beta.numpy(), R.numpy(), KN.numpy())
         self.L = L.numpy()
@@ -103,7 +107,6 @@ def _run(rank, world, port, out):
     o = sh.step(T(s.quat), T(s.log_scale), T(s.centers), T(s.C_occ), T(s.occ))
     res = {k: o[k].numpy().copy() for k in ("E", "gamma", "g_quat", "g_log_scale", "g_centers",
                                                "g_C")}
-    res["ranges"] = np.array(sh.ranges)
     if world > 1:
         dist.destroy_process_group()
     np.savez(out.format(rank=rank, world=world), **res)
@@ -125,21 +128,3 @@ def test_two_rank_gloo_equals_single_rank(tmp_path):
         two = np.load(out.format(rank=r, world=2))
         for k in ("E", "gamma", "g_quat", "g_log_scale", "g_centers", "g_C"):
             np.testing.assert_allclose(two[k], one[k], rtol=1e-12, atol=1e-12 * np.abs(one[k]).max())
-    rr = np.load(out.format(rank=0, world=2))["ranges"]
-    assert rr[0][0] == 0 and rr[-1][1] == _problem()[1].shape[0] and rr[0][1] == rr[1][0]
-
-
-def test_partition_balances_live_pairs():
-    from gs_dft_b200.ks.shard import partition_pairs
-    v = torch.zeros(103, dtype=torch.bool)
-    v[:61] = True
-    for G in (1, 2, 3, 4, 8):
-        rg = partition_pairs(v, G)
-        assert rg[0][0] == 0 and rg[-1][1] == 103
-        counts = [int(v[s:e].sum()) for s, e in rg]
-        assert sum(counts) == 61 and max(counts) - min(counts) <= 1
-        assert all(rg[k][1] == rg[k + 1][0] for k in range(G - 1))
-    w = torch.tensor([2.0, 1.0, 0.0, 2.0, 0.0, 0.0, 1.0])
-    rg = partition_pairs(w, 2)
-    counts = [int((w[s:e] != 0).sum()) for s, e in rg]
-    assert max(counts) - min(counts) <= 1
