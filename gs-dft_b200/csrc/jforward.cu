@@ -2,6 +2,8 @@
 //   gamma_P = sum_a (P|a) q_a,   (P|a) = KN_P KN_a pref sum_t w_t (G0 G1 G2)^(-1/2) exp(-t^2 S),
 // the 3-centre integral never stored. Reference: gs_dft/coulomb/ri.py:126-185 (block + nodes),
 // :436-469 (gamma stream), gs_dft/coulomb/stream.py:203-215 (pair quantities), ri.py:456 (q).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace gsdft {
@@ -347,5 +349,79 @@ extern "C" int gsdft_j_forward(const double* rec, int64_t n_live, const double* 
   GSDFT_LAUNCHED("j_forward");
   sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(partial, S, n_aux, gamma);
   GSDFT_LAUNCHED("sum_splits");
+  return GSDFT_OK;
+}
+
+// ------------------------------------------------------------------------------------------------
+// No-allocation variant of gsdft_j_forward.
+//
+// For callers that cannot allocate device memory at call time and cannot hand in a workspace —
+// for example a handler running inside a framework that owns the device memory pool (XLA
+// preallocates most of the GPU for its own allocator, so a cudaMalloc from inside a custom call can
+// fail or fragment that pool), or a caller with a fixed memory budget decided up front. The
+// per-split partial sums that gsdft_j_forward keeps in its workspace live here in one fixed array
+// of kNoAllocScratchDoubles doubles (8 MiB) that every device holds from library load until exit.
+// ------------------------------------------------------------------------------------------------
+namespace gsdft {
+
+constexpr int64_t kNoAllocScratchDoubles = int64_t(1) << 20;
+static __device__ __align__(256) double g_forward_scratch[kNoAllocScratchDoubles];
+
+static std::mutex g_scratch_mu;
+static double* g_scratch_dev[256];  // device address of g_forward_scratch, per device ordinal
+
+// The host-side name g_forward_scratch is only a stand-in for the device array; its device address
+// is looked up once per device (with that device current) and cached.
+static int forward_scratch(double** out) {
+  int dev = 0;
+  GSDFT_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 256) return fail(GSDFT_ERR_ARG, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_dev[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_forward_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(GSDFT_ERR_CUDA, "cudaGetSymbolAddress(forward scratch) on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_scratch_dev[dev] = static_cast<double*>(p);
+  }
+  *out = g_scratch_dev[dev];
+  return GSDFT_OK;
+}
+
+}  // namespace gsdft
+
+extern "C" int gsdft_j_forward_noalloc(const double* rec, int64_t n_rep, const double* beta,
+                                       const double* R, const double* KN, int64_t n_aux,
+                                       double* gamma, gsdft_stream_t stream) {
+  using namespace gsdft;
+  GSDFT_REQUIRE(n_rep >= 0 && n_aux > 0, "bad sizes");
+  if (n_aux > kNoAllocScratchDoubles)
+    return fail(GSDFT_ERR_ARG,
+                "gsdft_j_forward_noalloc: n_aux = %lld exceeds the fixed scratch of %lld doubles; "
+                "use gsdft_j_forward with a workspace",
+                (long long)n_aux, (long long)kNoAllocScratchDoubles);
+  GSDFT_REQUIRE(beta && R && KN && gamma, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  double* scratch = nullptr;
+  int rc = forward_scratch(&scratch);
+  if (rc) return rc;
+  if (n_rep == 0) {
+    GSDFT_CUDA(cudaMemsetAsync(gamma, 0, n_aux * sizeof(double), st));
+    return GSDFT_OK;
+  }
+  GSDFT_REQUIRE(rec && (reinterpret_cast<uintptr_t>(rec) & 15) == 0, "rec must be 16-byte aligned");
+  // Every entry the reduction reads (S rows of n_aux) is written by the kernel first, so the
+  // array needs no clearing; the split count is capped so the partial sums fit.
+  int64_t S = forward_splits(n_rep, n_aux);
+  S = imin64(S, kNoAllocScratchDoubles / n_aux);
+  int64_t per_split = (n_rep + S - 1) / S;
+  per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
+  dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
+  j_forward_kernel<<<grid, kFwThreads, kFwDynSmem, st>>>(rec, n_rep, beta, R, KN, n_aux, per_split,
+                                                         scratch);
+  GSDFT_LAUNCHED("j_forward_noalloc");
+  sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(scratch, (int)S, n_aux, gamma);
+  GSDFT_LAUNCHED("sum_splits_noalloc");
   return GSDFT_OK;
 }

@@ -54,6 +54,7 @@ SIGNATURES = {
                                _i64, _c_p, _c_p]),
     "gsdft_j_forward_workspace_size": (_sz, [_i64, _i64]),
     "gsdft_j_forward": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_j_forward_noalloc": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p]),
     "gsdft_j_solve_workspace_size": (_sz, [_i64]),
     "gsdft_j_solve": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_j_vjp_workspace_size": (_sz, [_i64, _i64]),

@@ -195,6 +195,20 @@ int gsdft_j_forward(const double* rec, int64_t n_rep, const double* beta, const 
                     const double* KN, int64_t n_aux, double* gamma, void* ws, size_t ws_bytes,
                     gsdft_stream_t stream);
 
+/* gsdft_j_forward without a workspace and without allocating: for callers that cannot allocate
+ * device memory at call time and cannot pass a workspace — for instance a handler inside a framework
+ * that owns the device memory pool (XLA preallocates most of the GPU for its own allocator, so a
+ * cudaMalloc from a custom call can fail or fragment that pool), or code with a fixed memory budget.
+ * The per-split partial sums live in one fixed device array of 2^20 doubles (8 MiB) that every GPU
+ * loading the library holds until the process exits; n_aux above 2^20 is rejected (GSDFT_ERR_ARG).
+ * The first call on each device looks up that array's device address (cudaGetSymbolAddress), so
+ * make the first call on a device before any stream capture. All calls share the array and it keeps
+ * the last call's contents (nothing in it needs to start at zero): calls whose work overlaps on the
+ * GPU — concurrent streams, or several host threads on one device — race on it and must be
+ * serialised by the caller. No counterpart in the reference. */
+int gsdft_j_forward_noalloc(const double* rec, int64_t n_rep, const double* beta, const double* R,
+                            const double* KN, int64_t n_aux, double* gamma, gsdft_stream_t stream);
+
 /* d = (L L^T)^-1 gamma, E = 1/2 gamma.d (E is a device scalar). Replaces df_coulomb_solve with
  * cholV (gs_dft/coulomb/ri.py:472-482). */
 size_t gsdft_j_solve_workspace_size(int64_t n_aux);
