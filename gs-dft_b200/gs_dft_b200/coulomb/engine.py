@@ -133,7 +133,9 @@ class RIJEngine:
         if not self.timing:
             return None
         st = torch.cuda.current_stream(self.device)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # external: inside a CUDA-graph capture these become event-record nodes that time replays
+        a = torch.cuda.Event(enable_timing=True, external=True)
+        b = torch.cuda.Event(enable_timing=True, external=True)
         a.record(st)
         self.events[name].append((a, b))
         return b
@@ -206,6 +208,31 @@ class RIJEngine:
             out.update(J=self.J, g_quat=self.g_quat, g_log_scale=self.g_log, g_centers=self.gmu,
                        g_C=self.g_C[:, :self.n_occ], gA6=self.gA6, gN=self.gN)
         return out
+
+
+class StepGraph:
+    """A whole J-build + gradient step captured once in a CUDA graph and replayed.
+
+    ``step_fn`` launches every kernel (the library's, cuBLAS, and — for a sharded step — the NCCL
+    allreduces) on the current stream and returns a dict of output tensors. Its input tensors are
+    read at their captured addresses: copy new parameters into them before ``replay()``. The
+    outputs are the captured buffers, overwritten by every replay."""
+
+    def __init__(self, step_fn, warmup: int = 2):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                step_fn()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = step_fn()
+
+    def replay(self):
+        self.graph.replay()
+        return self.out
 
 
 def check_device_status(clear=True):
