@@ -199,14 +199,14 @@ def main():
 
     import gs_dft_b200 as g
     from gs_dft_b200._lib import lib, ptr, stream_handle
-    from gs_dft_b200.coulomb.engine import StepGraph, check_device_status
+    from gs_dft_b200.coulomb.engine import check_device_status
     from gs_dft_b200.ks.shard import ShardedRIJ
     from gs_dft_b200.systems import make_config
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
     sy = make_config(args.config)
     t = lambda a: torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64, device=dev)
     quat, log_scale, centers, C, occ = (t(sy.quat), t(sy.log_scale), t(sy.centers), t(sy.C_occ),
@@ -245,11 +245,12 @@ def main():
     torch.cuda.synchronize()
     check_device_status()
 
-    # ---- the step captured once as a CUDA graph (kernels, cuBLAS solve, NCCL allreduces), with
-    # event brackets around the two integral kernels captured inside it -----------------------------
+    # ---- the step captured as CUDA graphs (one graph on one GPU; on several, the compute segments
+    # between the two NCCL allreduces, which stay eager), with event brackets around the two
+    # integral kernels captured inside them -------------------------------------------------------
     eng.timing = True
     eng.events = {"forward": [], "vjp": []}
-    graph = StepGraph(step, warmup=1)
+    graph = sh.capture(quat, log_scale, centers, C, occ)
     eng.timing = False
     cap = {k: v[-1] for k, v in eng.events.items()}   # the bracket events captured in the graph
     for _ in range(args.warmup):
@@ -297,7 +298,10 @@ def main():
                           barrier)
 
     peak = dfma_peak(torch, lib, ptr, stream_handle)
+    del graph                 # release every CUDA graph before the process group goes away
+    torch.cuda.synchronize()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
         return
@@ -326,7 +330,8 @@ def main():
                                   "with the summed weight (same integral; outputs unchanged to "
                                   "1e-10); value counts N_aux x live ordered pairs per step"),
                    "parallelism": f"pair-partition x{world}", "l2": "flushed between steps",
-                   "execution": "step captured once as a CUDA graph (library kernels, cuBLAS solve, NCCL allreduces) and replayed"},
+                   "execution": ("step replayed from CUDA graphs: one graph on 1 GPU; on N GPUs the "
+                                 "compute segments between the two NCCL allreduces, which run eagerly")},
         "refresh_s": refresh_s,
         "kernel_ms": {"j_forward": t_fwd, "j_vjp": t_vjp},
         "roofline": {"bound": "fp64", "kernel": dom, "achieved": achieved / 1e12,

@@ -254,7 +254,16 @@ __device__ __forceinline__ double rsqrt_pos(double p) {
 static __device__ int g_device_status;
 
 constexpr int kStatusMbarTimeout = 1;
-constexpr long long kMbarMaxPolls = 1LL << 22;
+// A wait gives up after 2 s of wall-clock time (the %globaltimer nanosecond clock), and in any case
+// after 2^30 polls; a healthy tile copy completes in microseconds.
+constexpr unsigned long long kMbarTimeoutNs = 2000000000ull;
+constexpr unsigned kMbarMaxPolls = 1u << 30;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -288,7 +297,8 @@ __device__ __forceinline__ void fence_proxy_async() {
 // Returns true once phase `parity` of `bar` has completed; false (status set) after the limit.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   uint32_t addr = smem_u32(bar);
-  for (long long it = 0; it < kMbarMaxPolls; ++it) {
+  unsigned long long t0 = 0;
+  for (unsigned it = 0; it < kMbarMaxPolls; ++it) {
     uint32_t done;
     asm volatile(
         "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
@@ -297,6 +307,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((it & 255u) == 0u) {
+      const unsigned long long t = global_ns();
+      if (it == 0u) t0 = t;
+      else if (t - t0 > kMbarTimeoutNs) break;
+    }
   }
   atomicExch(&g_device_status, kStatusMbarTimeout);
   return false;

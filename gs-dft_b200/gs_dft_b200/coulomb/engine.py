@@ -213,18 +213,19 @@ class RIJEngine:
 class StepGraph:
     """A whole J-build + gradient step captured once in a CUDA graph and replayed.
 
-    ``step_fn`` launches every kernel (the library's, cuBLAS, and — for a sharded step — the NCCL
-    allreduces) on the current stream and returns a dict of output tensors. Its input tensors are
+    ``step_fn`` launches every kernel (the library's and cuBLAS; never a collective) on the current
+    stream and returns its outputs. Its input tensors are
     read at their captured addresses: copy new parameters into them before ``replay()``. The
     outputs are the captured buffers, overwritten by every replay."""
 
     def __init__(self, step_fn, warmup: int = 2):
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for _ in range(warmup):
-                step_fn()
-        torch.cuda.current_stream().wait_stream(side)
+        if warmup:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                for _ in range(warmup):
+                    step_fn()
+            torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):

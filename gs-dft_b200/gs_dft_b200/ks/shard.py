@@ -39,30 +39,82 @@ class ShardedRIJ:
         self.packed = torch.empty(10 * self.M + self.M * max(self.n_occ, 1),
                                   dtype=torch.float64, device=pi.device)
 
-    def step(self, quat, log_scale, centers, C_occ, occ, grad=True):
-        import torch.distributed as dist
+    # The step in three parts around its two collectives, so that the compute parts can be
+    # captured as CUDA graphs while the NCCL allreduces stay eager.
+    def _forward(self, quat, log_scale, centers, C_occ, occ):
+        return self.engine.forward_local(quat, log_scale, centers, C_occ, occ)
+
+    def _middle(self, centers, C_occ, occ):
         eng = self.engine
-        gamma = eng.forward_local(quat, log_scale, centers, C_occ, occ)
-        if self.world > 1:
-            dist.all_reduce(gamma, op=dist.ReduceOp.SUM, group=self.group)
         E, d = eng.solve()
-        out = dict(E=E, gamma=gamma, d=d)
-        if not grad:
-            return out
         gA6, gmu, gN, gC = eng.backward_local(centers, C_occ, occ)
-        M = self.M
-        p = self.packed
+        M, p = self.M, self.packed
         p[:6 * M].copy_(gA6.reshape(-1))
         p[6 * M:9 * M].copy_(gmu.reshape(-1))
         p[9 * M:10 * M].copy_(gN)
         if self.n_occ:
             p[10 * M:].copy_(gC[:, :self.n_occ].reshape(-1))
-        if self.world > 1:
-            dist.all_reduce(p, op=dist.ReduceOp.SUM, group=self.group)
+        return E, d
+
+    def _tail(self, quat, log_scale):
+        eng, M, p = self.engine, self.M, self.packed
         eng.gA6.copy_(p[:6 * M].view(M, 6))
         eng.gmu.copy_(p[6 * M:9 * M].view(M, 3))
         eng.gN.copy_(p[9 * M:10 * M])
-        g_quat, g_log = eng.chart(quat, log_scale)
-        out.update(J_local=eng.J, g_quat=g_quat, g_log_scale=g_log, g_centers=eng.gmu,
-                   g_C=p[10 * M:].view(M, -1)[:, :self.n_occ])
-        return out
+        return eng.chart(quat, log_scale)
+
+    def _allreduce(self, t):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+
+    def _outputs(self, E, d, g_quat, g_log):
+        M, eng = self.M, self.engine
+        return dict(E=E, gamma=eng.gamma, d=d, J_local=eng.J, g_quat=g_quat, g_log_scale=g_log,
+                    g_centers=eng.gmu, g_C=self.packed[10 * M:].view(M, -1)[:, :self.n_occ])
+
+    def step(self, quat, log_scale, centers, C_occ, occ, grad=True):
+        gamma = self._forward(quat, log_scale, centers, C_occ, occ)
+        self._allreduce(gamma)
+        if not grad:
+            E, d = self.engine.solve()
+            return dict(E=E, gamma=gamma, d=d)
+        E, d = self._middle(centers, C_occ, occ)
+        self._allreduce(self.packed)
+        g_quat, g_log = self._tail(quat, log_scale)
+        return self._outputs(E, d, g_quat, g_log)
+
+    def capture(self, quat, log_scale, centers, C_occ, occ):
+        """The step as CUDA graphs: one graph on a single device; on several, three graphs (the
+        compute before, between and after the two allreduces) with the NCCL allreduces issued
+        eagerly in between — collectives are never captured. Inputs are read at the given tensors'
+        addresses: copy new parameters into them before ``replay()``."""
+        from ..coulomb.engine import StepGraph
+        if self.world == 1:
+            return StepGraph(lambda: self.step(quat, log_scale, centers, C_occ, occ))
+        return _SegmentedStep(self, quat, log_scale, centers, C_occ, occ)
+
+
+class _SegmentedStep:
+    """Three captured compute segments with eager NCCL allreduces between them."""
+
+    def __init__(self, sh, quat, log_scale, centers, C_occ, occ):
+        import torch
+        from ..coulomb.engine import StepGraph
+        # eager warm-up of the whole step (collectives included) on the current stream
+        for _ in range(2):
+            sh.step(quat, log_scale, centers, C_occ, occ)
+        torch.cuda.synchronize()
+        self.sh = sh
+        self.gA = StepGraph(lambda: sh._forward(quat, log_scale, centers, C_occ, occ), warmup=0)
+        self.gB = StepGraph(lambda: sh._middle(centers, C_occ, occ), warmup=0)
+        self.gC = StepGraph(lambda: sh._tail(quat, log_scale), warmup=0)
+
+    def replay(self):
+        sh = self.sh
+        gamma = self.gA.replay()
+        sh._allreduce(gamma)
+        E, d = self.gB.replay()
+        sh._allreduce(sh.packed)
+        g_quat, g_log = self.gC.replay()
+        return sh._outputs(E, d, g_quat, g_log)
