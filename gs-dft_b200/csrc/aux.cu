@@ -110,6 +110,88 @@ __global__ void half_dot_kernel(const double* __restrict__ g, const double* __re
   if (threadIdx.x == 0) *E = 0.5 * s[0];
 }
 
+// One-CTA blocked triangular solves for the per-step tail, N_aux <= kSmallSolveMax:
+// L y = gamma (forward), L^T d = y (backward), E = 1/2 gamma.d. Blocks of 32 rows: the panel of
+// rows below/right of the solved part is applied with coalesced reads of row-major L (a warp per row
+// for the forward sweep, warps over rows and lanes over the block's columns for the backward
+// sweep), then the 32x32 diagonal triangle is solved inside one warp. The solution lives in shared
+// memory; every reduction has a fixed order.
+// --- per-step solve through inverse factors -------------------------------------------------------
+// With X = L^-1 and XT = L^-T (row-major, computed once per refresh), d = XT (X gamma) and
+// E = 1/2 |X gamma|^2 = 1/2 gamma.(L L^T)^-1 gamma are two triangular mat-vecs: every row is
+// independent, so they spread over the SMs instead of walking a dependent chain of substitution
+// steps. One warp per row; each lane keeps four partial sums; the warp's shuffle tree fixes the
+// summation order (bitwise reproducible).
+constexpr int kTriWarps = 4;
+
+__global__ void identity_kernel(double* X, int64_t n) {
+  const int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (k < n * n) X[k] = (k / n == k % n) ? 1.0 : 0.0;
+}
+
+// XT[j][i] = X[i][j] through a 32x33 shared tile (coalesced both ways).
+__global__ void transpose_kernel(const double* __restrict__ X, int64_t n, double* __restrict__ XT) {
+  __shared__ double t[32][33];
+  const int64_t r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t r = r0 + k, c = c0 + threadIdx.x;
+    if (r < n && c < n) t[k][threadIdx.x] = X[r * n + c];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t r = c0 + k, c = r0 + threadIdx.x;
+    if (r < n && c < n) XT[r * n + c] = t[threadIdx.x][k];
+  }
+}
+
+// y[i] = sum_{j in row i's triangle} A[i][j] x[j]: columns [0, i] (kLower) or [i, n) (upper).
+// With E != nullptr, block 0 also writes E = 1/2 x.x.
+template <bool kLower>
+__global__ void __launch_bounds__(kTriWarps * 32)
+    tri_rows_kernel(const double* __restrict__ A, const double* __restrict__ x, int64_t n,
+                    double* __restrict__ y, double* __restrict__ E) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i = blockIdx.x * (int64_t)kTriWarps + warp;
+  if (i < n) {
+    const double* row = A + i * n;
+    const int64_t lo = kLower ? 0 : i, hi = kLower ? i + 1 : n;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    int64_t j = lo + lane;
+    for (; j + 96 < hi; j += 128) {
+      a0 = fma(row[j], x[j], a0);
+      a1 = fma(row[j + 32], x[j + 32], a1);
+      a2 = fma(row[j + 64], x[j + 64], a2);
+      a3 = fma(row[j + 96], x[j + 96], a3);
+    }
+    for (; j < hi; j += 32) a0 = fma(row[j], x[j], a0);
+    double v = (a0 + a1) + (a2 + a3);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) y[i] = v;
+  }
+  if (E != nullptr && blockIdx.x == 0) {
+    __shared__ double part[kTriWarps];
+    double a0 = 0.0, a1 = 0.0;
+    int64_t k = threadIdx.x;
+    for (; k + kTriWarps * 32 < n; k += 2 * kTriWarps * 32) {
+      a0 = fma(x[k], x[k], a0);
+      a1 = fma(x[k + kTriWarps * 32], x[k + kTriWarps * 32], a1);
+    }
+    if (k < n) a0 = fma(x[k], x[k], a0);
+    double v = a0 + a1;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) part[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double sum = 0.0;
+#pragma unroll
+      for (int w = 0; w < kTriWarps; ++w) sum += part[w];
+      *E = 0.5 * sum;
+    }
+  }
+}
+
 // Library handles, one per device, created on first use.
 struct Handles {
   cusolverDnHandle_t solver = nullptr;
@@ -252,5 +334,53 @@ extern "C" int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux
     return fail(GSDFT_ERR_LINALG, "cublasDtrsv (backward) failed");
   half_dot_kernel<<<1, 1024, 0, st>>>(gamma, d, n_aux, E);
   GSDFT_LAUNCHED("half_dot");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv2,
+                                     gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_aux > 0 && n_aux <= GSDFT_SOLVE_INV_MAX, "n_aux out of range");
+  GSDFT_REQUIRE(L && Linv2, "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = n_aux;
+  double* X = Linv2;
+  double* XT = Linv2 + n * n;
+  identity_kernel<<<grid_1d(n * n, 256), 256, 0, st>>>(X, n);
+  GSDFT_LAUNCHED("identity");
+  Handles* h = nullptr;
+  int rc = get_handles(&h);
+  if (rc) return rc;
+  cublasSetStream(h->blas, st);
+  // Column-major, the row-major lower L is U = L^T (upper) and the row-major X is X^T. U Y = I gives
+  // Y = L^-T, i.e. X = L^-1 row-major.
+  const double one = 1.0;
+  if (cublasDtrsm(h->blas, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N,
+                  CUBLAS_DIAG_NON_UNIT, (int)n, (int)n, &one, L, (int)n, X, (int)n) !=
+      CUBLAS_STATUS_SUCCESS)
+    return fail(GSDFT_ERR_LINALG, "cublasDtrsm failed");
+  const dim3 tg((unsigned)((n + 31) / 32), (unsigned)((n + 31) / 32));
+  transpose_kernel<<<tg, dim3(32, 8), 0, st>>>(X, n, XT);
+  GSDFT_LAUNCHED("transpose");
+  return GSDFT_OK;
+}
+
+extern "C" size_t gsdft_j_solve_inv_workspace_size(int64_t n_aux) {
+  return ((size_t)imax64(n_aux, 1) * sizeof(double) + 255) & ~(size_t)255;
+}
+
+extern "C" int gsdft_j_solve_inv(const double* Linv2, const double* gamma, int64_t n_aux, double* d,
+                                 double* E, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_aux > 0 && n_aux <= GSDFT_SOLVE_INV_MAX, "n_aux out of range");
+  GSDFT_REQUIRE(Linv2 && gamma && d && E && ws, "null pointer");
+  GSDFT_REQUIRE(ws_bytes >= gsdft_j_solve_inv_workspace_size(n_aux), "workspace too small");
+  GSDFT_REQUIRE(d != gamma, "d must not alias gamma");
+  cudaStream_t st = (cudaStream_t)stream;
+  const int64_t n = n_aux;
+  double* y = static_cast<double*>(ws);
+  const unsigned grid = (unsigned)((n + kTriWarps - 1) / kTriWarps);
+  tri_rows_kernel<true><<<grid, kTriWarps * 32, 0, st>>>(Linv2, gamma, n, y, nullptr);
+  GSDFT_LAUNCHED("tri_rows");
+  tri_rows_kernel<false><<<grid, kTriWarps * 32, 0, st>>>(Linv2 + n * n, y, n, d, E);
+  GSDFT_LAUNCHED("tri_rows");
   return GSDFT_OK;
 }

@@ -125,6 +125,27 @@ __global__ void pair_density_kernel(const int32_t* __restrict__ pi, const int32_
   }
 }
 
+// The same for few orbitals (n_occ <= 32): one thread per pair, orbitals in order.
+__global__ void pair_density_thread_kernel(const int32_t* __restrict__ pi,
+                                           const int32_t* __restrict__ pj,
+                                           const double* __restrict__ rep_w,
+                                           const int32_t* __restrict__ live_idx, int64_t n_live,
+                                           const double* __restrict__ C,
+                                           const double* __restrict__ occ, int64_t n_occ,
+                                           double* __restrict__ rec) {
+  int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_live) return;
+  int64_t e = live_idx[a];
+  const double* ci = C + (int64_t)pi[e] * n_occ;
+  const double* cj = C + (int64_t)pj[e] * n_occ;
+  double acc = 0.0;
+  for (int64_t o = 0; o < n_occ; ++o) acc = fma(occ[o] * ci[o], cj[o], acc);
+  double q = rep_w[a] * acc;
+  double* r = rec + a * GSDFT_REC_FIELDS;
+  r[GSDFT_REC_Q] = q;
+  r[GSDFT_REC_QK] = q * r[GSDFT_REC_KN];
+}
+
 // ------------------------------------------------------------------------------------------------
 // Forward: one aux per thread (registers), pair-record tiles staged in shared memory by bulk copy.
 // ------------------------------------------------------------------------------------------------
@@ -241,9 +262,17 @@ __global__ void sum_splits_kernel(const double* __restrict__ partial, int S, int
                                   double* __restrict__ out) {
   int64_t P = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (P >= n) return;
-  double acc = 0.0;
-  for (int s = 0; s < S; ++s) acc += partial[s * n + P];
-  out[P] = acc;
+  // four independent partial sums, combined in a fixed order
+  double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+  int s = 0;
+  for (; s + 3 < S; s += 4) {
+    a0 += partial[(int64_t)s * n + P];
+    a1 += partial[(int64_t)(s + 1) * n + P];
+    a2 += partial[(int64_t)(s + 2) * n + P];
+    a3 += partial[(int64_t)(s + 3) * n + P];
+  }
+  for (; s < S; ++s) a0 += partial[(int64_t)s * n + P];
+  out[P] = (a0 + a1) + (a2 + a3);
 }
 
 static int num_sms() {
@@ -315,8 +344,13 @@ extern "C" int gsdft_pair_prep(const double* A9, const double* mu, const double*
   cudaStream_t st = (cudaStream_t)stream;
   pair_prep_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(A9, mu, N, pi, pj, rep_pos, n_rep, rec);
   GSDFT_LAUNCHED("pair_prep");
-  pair_density_kernel<<<grid_1d(n_rep * 32, 256), 256, 0, st>>>(pi, pj, rep_w, rep_pos, n_rep,
-                                                                C_occ, occ, n_occ, rec);
+  if (n_occ <= 32) {
+    pair_density_thread_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(pi, pj, rep_w, rep_pos, n_rep,
+                                                                   C_occ, occ, n_occ, rec);
+  } else {
+    pair_density_kernel<<<grid_1d(n_rep * 32, 256), 256, 0, st>>>(pi, pj, rep_w, rep_pos, n_rep,
+                                                                  C_occ, occ, n_occ, rec);
+  }
   GSDFT_LAUNCHED("pair_density");
   return GSDFT_OK;
 }

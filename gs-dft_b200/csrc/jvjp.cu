@@ -200,9 +200,11 @@ __global__ void pair_chain_kernel(const double* __restrict__ A9, const double* _
                                   const double* __restrict__ N, const int32_t* __restrict__ pi,
                                   const int32_t* __restrict__ pj,
                                   const int32_t* __restrict__ live_idx,
-                                  const int32_t* __restrict__ twin, int64_t n_live,
+                                  const int32_t* __restrict__ twin,
+                                  const double* __restrict__ rep_w, int64_t n_live,
                                   const double* __restrict__ rec, const double* __restrict__ sums,
-                                  double* __restrict__ side, double* __restrict__ J) {
+                                  double* __restrict__ side, double* __restrict__ J,
+                                  double* __restrict__ jw) {
   int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (a >= n_live) return;
   const double* r = rec + a * GSDFT_REC_FIELDS;
@@ -213,6 +215,7 @@ __global__ void pair_chain_kernel(const double* __restrict__ A9, const double* _
   const double SJ = sm[GSDFT_VJP_SJ];
   J[e] = kn * SJ;
   if (twin[a] >= 0) J[twin[a]] = kn * SJ;  // the merged transpose carries the same integral
+  jw[a] = (kn * SJ) * rep_w[a];            // J w, the weight of q_a's gradient
   const double KNbar = q * kPref * SJ;
   // eigenframe cotangent of A_hat: M_kl = -qk SZ_kl - 1/2 qk SD_k delta_kl
   double Mm[3][3];
@@ -340,32 +343,96 @@ __global__ void splat_reduce_kernel(const double* __restrict__ side,
   }
 }
 
-// g_C[s, o] = occ_o (sum_{pi=s} J w C[pj, o] + sum_{pj=s} J w C[pi, o]) over representatives (w the
-// summed weight); one block per splat row, threads over o, segments walked in order.
-__global__ void density_grad_kernel(const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
-                                    const int32_t* __restrict__ rep_pos,
-                                    const double* __restrict__ rep_w,
-                                    const double* __restrict__ J,
-                                    const int32_t* __restrict__ order_i,
-                                    const int64_t* __restrict__ seg_i,
-                                    const int32_t* __restrict__ order_j,
-                                    const int64_t* __restrict__ seg_j, const double* __restrict__ C,
-                                    const double* __restrict__ occ, int64_t n_occ,
-                                    double* __restrict__ gC) {
+// g_C[s, o] = occ_o sum_{e in s's by-pi and by-pj segments} (J w)_e C[partner_e, o], partner_e
+// the other splat of entry e's representative. One block of kDgWarps warps per splat row.
+// Few orbitals (n_occ <= 32): lanes take segment entries, each lane accumulates the whole row in
+// registers, then a fixed-order reduction over lanes and warps. Many orbitals: warps take entries,
+// lanes cover o in strides of 32, warps' partial rows added in warp order. Deterministic either way.
+constexpr int kDgWarps = 8;
+constexpr int kDgMaxOcc = 512;   // orbitals per pass of the shared-memory row buffer
+
+template <int NO>
+__global__ void __launch_bounds__(kDgWarps * 32)
+    density_grad_small_kernel(const int32_t* __restrict__ order_i,
+                              const int64_t* __restrict__ seg_i,
+                              const int32_t* __restrict__ partner_i,
+                              const int32_t* __restrict__ order_j,
+                              const int64_t* __restrict__ seg_j,
+                              const int32_t* __restrict__ partner_j, const double* __restrict__ jw,
+                              const double* __restrict__ C, const double* __restrict__ occ,
+                              int n_occ, double* __restrict__ gC) {
+  __shared__ double part[kDgWarps][NO];
   const int64_t s = blockIdx.x;
-  for (int64_t o = threadIdx.x; o < n_occ; o += blockDim.x) {
-    double acc = 0.0;
-    for (int64_t e = seg_i[s]; e < seg_i[s + 1]; ++e) {
-      const int32_t a = order_i[e];
-      const int64_t l = rep_pos[a];
-      acc = fma(J[l] * rep_w[a], C[(int64_t)pj[l] * n_occ + o], acc);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i0 = seg_i[s], ni = seg_i[s + 1] - i0;
+  const int64_t j0 = seg_j[s], nj = seg_j[s + 1] - j0;
+  double acc[NO];
+#pragma unroll
+  for (int o = 0; o < NO; ++o) acc[o] = 0.0;
+  for (int64_t e = threadIdx.x; e < ni + nj; e += kDgWarps * 32) {
+    const bool is_i = e < ni;
+    const int64_t k = is_i ? i0 + e : j0 + (e - ni);
+    const double w = jw[is_i ? order_i[k] : order_j[k]];
+    const double* crow = C + (int64_t)(is_i ? partner_i[k] : partner_j[k]) * n_occ;
+#pragma unroll
+    for (int o = 0; o < NO; ++o)
+      if (o < n_occ) acc[o] = fma(w, crow[o], acc[o]);
+  }
+#pragma unroll
+  for (int o = 0; o < NO; ++o) {
+    double v = acc[o];
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) part[warp][o] = v;
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < n_occ; o += blockDim.x) {
+    double sum = 0.0;
+#pragma unroll
+    for (int w = 0; w < kDgWarps; ++w) sum += part[w][o];
+    gC[s * n_occ + o] = occ[o] * sum;
+  }
+}
+
+__global__ void __launch_bounds__(kDgWarps * 32)
+    density_grad_kernel(const int32_t* __restrict__ order_i, const int64_t* __restrict__ seg_i,
+                        const int32_t* __restrict__ partner_i,
+                        const int32_t* __restrict__ order_j, const int64_t* __restrict__ seg_j,
+                        const int32_t* __restrict__ partner_j, const double* __restrict__ jw,
+                        const double* __restrict__ C, const double* __restrict__ occ,
+                        int64_t n_occ, double* __restrict__ gC) {
+  __shared__ double part[kDgWarps][kDgMaxOcc / 32][32];
+  const int64_t s = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t i0 = seg_i[s], ni = seg_i[s + 1] - i0;
+  const int64_t j0 = seg_j[s], nj = seg_j[s + 1] - j0;
+  for (int64_t ob = 0; ob < n_occ; ob += kDgMaxOcc) {
+    const int nchunk = (int)((imin64(kDgMaxOcc, n_occ - ob) + 31) / 32);
+    double acc[kDgMaxOcc / 32];
+#pragma unroll
+    for (int c = 0; c < kDgMaxOcc / 32; ++c) acc[c] = 0.0;
+    for (int64_t e = warp; e < ni + nj; e += kDgWarps) {
+      const bool is_i = e < ni;
+      const int64_t k = is_i ? i0 + e : j0 + (e - ni);
+      const double w = jw[is_i ? order_i[k] : order_j[k]];
+      const double* crow = C + (int64_t)(is_i ? partner_i[k] : partner_j[k]) * n_occ + ob;
+#pragma unroll
+      for (int c = 0; c < kDgMaxOcc / 32; ++c) {
+        const int64_t o = (int64_t)c * 32 + lane;
+        if (c < nchunk && ob + o < n_occ) acc[c] = fma(w, crow[o], acc[c]);
+      }
     }
-    for (int64_t e = seg_j[s]; e < seg_j[s + 1]; ++e) {
-      const int32_t a = order_j[e];
-      const int64_t l = rep_pos[a];
-      acc = fma(J[l] * rep_w[a], C[(int64_t)pi[l] * n_occ + o], acc);
+#pragma unroll
+    for (int c = 0; c < kDgMaxOcc / 32; ++c)
+      if (c < nchunk) part[warp][c][lane] = acc[c];
+    __syncthreads();
+    for (int64_t o = threadIdx.x; o < imin64(kDgMaxOcc, n_occ - ob); o += blockDim.x) {
+      double sum = 0.0;
+#pragma unroll
+      for (int w = 0; w < kDgWarps; ++w) sum += part[w][o >> 5][o & 31];
+      gC[s * n_occ + ob + o] = occ[ob + o] * sum;
     }
-    gC[s * n_occ + o] = occ[o] * acc;
+    __syncthreads();
   }
 }
 
@@ -445,9 +512,9 @@ extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta
 
 extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
                                 const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
-                                const int32_t* rep_twin, int64_t n_rep, int64_t n,
-                                const double* rec, const double* sums, double* side, double* J,
-                                gsdft_stream_t stream) {
+                                const int32_t* rep_twin, const double* rep_w, int64_t n_rep,
+                                int64_t n, const double* rec, const double* sums, double* side,
+                                double* J, double* jw, gsdft_stream_t stream) {
   GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n >= n_rep, "bad sizes");
   cudaStream_t st = (cudaStream_t)stream;
   if (n > 0) {
@@ -455,10 +522,11 @@ extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double
     GSDFT_CUDA(cudaMemsetAsync(J, 0, n * sizeof(double), st));
   }
   if (n_rep == 0) return GSDFT_OK;
-  GSDFT_REQUIRE(A9 && mu && N && pi && pj && rep_pos && rep_twin && rec && sums && side,
+  GSDFT_REQUIRE(A9 && mu && N && pi && pj && rep_pos && rep_twin && rep_w && rec && sums &&
+                    side && jw,
                 "null pointer");
   pair_chain_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(A9, mu, N, pi, pj, rep_pos, rep_twin,
-                                                         n_rep, rec, sums, side, J);
+                                                         rep_w, n_rep, rec, sums, side, J, jw);
   GSDFT_LAUNCHED("pair_chain");
   return GSDFT_OK;
 }
@@ -476,20 +544,26 @@ extern "C" int gsdft_splat_reduce(const double* side, const int32_t* order_i, co
   return GSDFT_OK;
 }
 
-extern "C" int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
-                                  const double* rep_w, const double* J, const int32_t* order_i,
-                                  const int64_t* seg_i, const int32_t* order_j,
-                                  const int64_t* seg_j, int64_t n_rep, int64_t M,
-                                  const double* C_occ, const double* occ, int64_t n_occ,
-                                  double* g_C, gsdft_stream_t stream) {
+extern "C" int gsdft_density_grad(const int32_t* order_i, const int64_t* seg_i,
+                                  const int32_t* partner_i, const int32_t* order_j,
+                                  const int64_t* seg_j, const int32_t* partner_j, const double* jw,
+                                  int64_t n_rep, int64_t M, const double* C_occ, const double* occ,
+                                  int64_t n_occ, double* g_C, gsdft_stream_t stream) {
   GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n_occ >= 0, "bad sizes");
   if (n_occ == 0) return GSDFT_OK;
   GSDFT_REQUIRE(seg_i && seg_j && C_occ && occ && g_C, "null pointer");
-  GSDFT_REQUIRE(n_rep == 0 || (pi && pj && rep_pos && rep_w && J && order_i && order_j),
-                "null pointer");
-  int threads = n_occ >= 256 ? 256 : (int)((n_occ + 31) / 32 * 32);
-  density_grad_kernel<<<(unsigned)M, threads, 0, (cudaStream_t)stream>>>(
-      pi, pj, rep_pos, rep_w, J, order_i, seg_i, order_j, seg_j, C_occ, occ, n_occ, g_C);
+  GSDFT_REQUIRE(n_rep == 0 || (order_i && partner_i && order_j && partner_j && jw), "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n_occ <= 16) {
+    density_grad_small_kernel<16><<<(unsigned)M, kDgWarps * 32, 0, st>>>(
+        order_i, seg_i, partner_i, order_j, seg_j, partner_j, jw, C_occ, occ, (int)n_occ, g_C);
+  } else if (n_occ <= 32) {
+    density_grad_small_kernel<32><<<(unsigned)M, kDgWarps * 32, 0, st>>>(
+        order_i, seg_i, partner_i, order_j, seg_j, partner_j, jw, C_occ, occ, (int)n_occ, g_C);
+  } else {
+    density_grad_kernel<<<(unsigned)M, kDgWarps * 32, 0, st>>>(
+        order_i, seg_i, partner_i, order_j, seg_j, partner_j, jw, C_occ, occ, n_occ, g_C);
+  }
   GSDFT_LAUNCHED("density_grad");
   return GSDFT_OK;
 }

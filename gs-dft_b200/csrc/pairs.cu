@@ -207,6 +207,15 @@ __global__ void gather_keys_kernel(const int32_t* __restrict__ key, const int32_
   iota[a] = (int32_t)a;
 }
 
+// partner[e] = the other splat of the representative at sorted position e (pj for the by-pi
+// grouping, pi for the by-pj grouping).
+__global__ void partner_kernel(const int32_t* __restrict__ other, const int32_t* __restrict__ pos,
+                               const int32_t* __restrict__ order, int64_t n,
+                               int32_t* __restrict__ partner) {
+  int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (e < n) partner[e] = other[pos[order[e]]];
+}
+
 // seg[s] = first position in the sorted keys with key >= s, s in [0, M].
 __global__ void segment_bounds_kernel(const int32_t* __restrict__ sorted, int64_t n, int64_t M,
                                       int64_t* __restrict__ seg) {
@@ -519,7 +528,8 @@ extern "C" size_t gsdft_pair_groups_workspace_size(int64_t n_rep, int64_t M) {
 
 extern "C" int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
                                  int64_t n_rep, int64_t M, int32_t* order_i, int64_t* seg_i,
-                                 int32_t* order_j, int64_t* seg_j, void* ws, size_t ws_bytes,
+                                 int32_t* partner_i, int32_t* order_j, int64_t* seg_j,
+                                 int32_t* partner_j, void* ws, size_t ws_bytes,
                                  gsdft_stream_t stream) {
   GSDFT_REQUIRE(n_rep >= 0 && n_rep < (int64_t(1) << 31) && M > 0, "bad n_rep or M");
   GSDFT_REQUIRE(seg_i && seg_j, "null pointer");
@@ -529,10 +539,13 @@ extern "C" int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int
   Carver c(ws, ws_bytes);
   layout_reps(c, n_rep, &p, tmp);
   if (!c.ok) return fail(GSDFT_ERR_ARG, "pair groups workspace too small (%zu < %zu)", ws_bytes, c.off);
-  GSDFT_REQUIRE(n_rep == 0 || (pi && pj && rep_pos && order_i && order_j), "null pointer");
+  GSDFT_REQUIRE(n_rep == 0 || (pi && pj && rep_pos && order_i && order_j && partner_i && partner_j),
+                "null pointer");
   int eb = bits_for(M);
   const int32_t* keysrc[2] = {pi, pj};
+  const int32_t* othersrc[2] = {pj, pi};
   int32_t* order[2] = {order_i, order_j};
+  int32_t* partner[2] = {partner_i, partner_j};
   int64_t* seg[2] = {seg_i, seg_j};
   int32_t* k32 = reinterpret_cast<int32_t*>(p.keys);
   int32_t* k32s = reinterpret_cast<int32_t*>(p.keys_sorted);
@@ -543,6 +556,9 @@ extern "C" int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int
       size_t tb = tmp;
       GSDFT_CUDA(cub::DeviceRadixSort::SortPairs(p.tmp, tb, k32, k32s, p.iota, order[s],
                                                  (int)n_rep, 0, eb, st));
+      partner_kernel<<<grid_1d(n_rep, 256), 256, 0, st>>>(othersrc[s], rep_pos, order[s], n_rep,
+                                                          partner[s]);
+      GSDFT_LAUNCHED("partner");
     }
     segment_bounds_kernel<<<grid_1d(M + 1, 256), 256, 0, st>>>(k32s, n_rep, M, seg[s]);
     GSDFT_LAUNCHED("segment_bounds");

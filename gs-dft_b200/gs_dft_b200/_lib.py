@@ -16,6 +16,7 @@ ERR_ARG, ERR_CUDA, ERR_OVERFLOW, ERR_LINALG = 1, 2, 3, 4
 REC_FIELDS = 18
 VJP_FIELDS = 13
 SIDE_FIELDS = 20
+SOLVE_INV_MAX = 16384   # GSDFT_SOLVE_INV_MAX
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -42,8 +43,8 @@ SIGNATURES = {
     "gsdft_pair_reps": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _i32, _c_p, _c_p, _c_p, _pi64, _c_p,
                                _sz, _c_p]),
     "gsdft_pair_groups_workspace_size": (_sz, [_i64, _i64]),
-    "gsdft_pair_groups": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _sz,
-                                 _c_p]),
+    "gsdft_pair_groups": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                 _c_p, _sz, _c_p]),
     "gsdft_product_aux": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64,
                                  ctypes.POINTER(ctypes.c_double), _i32, _c_p, _c_p, _c_p]),
     "gsdft_aux_quantities": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p]),
@@ -57,15 +58,18 @@ SIGNATURES = {
     "gsdft_j_forward_noalloc": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p]),
     "gsdft_j_solve_workspace_size": (_sz, [_i64]),
     "gsdft_j_solve": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_j_solve_inverse": (_i32, [_c_p, _i64, _c_p, _c_p]),
+    "gsdft_j_solve_inv_workspace_size": (_sz, [_i64]),
+    "gsdft_j_solve_inv": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_j_vjp_workspace_size": (_sz, [_i64, _i64]),
     "gsdft_j_vjp": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _sz,
                            _c_p]),
-    "gsdft_pair_chain": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p,
-                                _c_p, _c_p, _c_p, _c_p]),
+    "gsdft_pair_chain": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64,
+                                _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "gsdft_splat_reduce": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p,
                                   _c_p]),
-    "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64,
-                                  _c_p, _c_p, _i64, _c_p, _c_p]),
+    "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
+                                  _i64, _c_p, _c_p]),
 }
 
 

@@ -17,7 +17,8 @@ from dataclasses import dataclass
 
 import torch
 
-from .._lib import REC_FIELDS, SIDE_FIELDS, VJP_FIELDS, lib, ptr, stream_handle
+from .._lib import (REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, lib, ptr,
+                    stream_handle)
 
 F64 = torch.float64
 
@@ -44,8 +45,10 @@ class PairPlan:
     rep_twin: torch.Tensor
     order_i: torch.Tensor
     seg_i: torch.Tensor
+    partner_i: torch.Tensor
     order_j: torch.Tensor
     seg_j: torch.Tensor
+    partner_j: torch.Tensor
 
     @property
     def n_rep(self) -> int:
@@ -69,14 +72,16 @@ def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: boo
     k = r1 - r0
     oi = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
     oj = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
+    qi = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
+    qj = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
     si = torch.empty(M + 1, dtype=torch.int64, device=dev)
     sj = torch.empty(M + 1, dtype=torch.int64, device=dev)
     gb = lib.gsdft_pair_groups_workspace_size(k, M)
     gws = torch.empty(gb, dtype=torch.uint8, device=dev)
-    lib.call("gsdft_pair_groups", ptr(pi), ptr(pj), ptr(pos), k, M, ptr(oi), ptr(si), ptr(oj),
-             ptr(sj), ptr(gws), gb, stream_handle(dev))
+    lib.call("gsdft_pair_groups", ptr(pi), ptr(pj), ptr(pos), k, M, ptr(oi), ptr(si), ptr(qi),
+             ptr(oj), ptr(sj), ptr(qj), ptr(gws), gb, stream_handle(dev))
     return PairPlan(n=n, n_rep_total=n_rep, r0=r0, r1=r1, rep_pos=pos, rep_w=rw, rep_twin=tw,
-                    order_i=oi, seg_i=si, order_j=oj, seg_j=sj)
+                    order_i=oi, seg_i=si, partner_i=qi, order_j=oj, seg_j=sj, partner_j=qj)
 
 
 def splat_quantities(quat, log_scale):
@@ -98,9 +103,12 @@ class RIJEngine:
         beta, R, KN: the aux quantities; L: lower Cholesky factor of V + lam I (row-major).
         rank, world: this device evaluates representatives [n_rep*rank//world, n_rep*(rank+1)//world).
         merge_twins: evaluate each (i,j)/(j,i) pair of a live transposed twin once (same integral).
+        inverse_solve: form [L^-1, L^-T] once (O(n_aux^3)) so each step's solve is two parallel
+            mat-vecs; for engines that run many steps. Off: per-step triangular substitution.
     """
 
-    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1, merge_twins=True):
+    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1, merge_twins=True,
+                 inverse_solve=True):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi = pi.contiguous()
@@ -116,14 +124,22 @@ class RIJEngine:
         self.sums = e(max(nl, 1), VJP_FIELDS)
         self.side = e(max(nl, 1), SIDE_FIELDS)
         self.J = e(max(n, 1))
+        self.jw = e(max(nl, 1))
         self.gamma, self.d, self.E = e(self.n_aux), e(self.n_aux), e(1)
         self.gA6, self.gmu, self.gN = e(self.M, 6), e(self.M, 3), e(self.M)
         self.g_quat, self.g_log = e(self.M, 4), e(self.M, 3)
         self.g_C = e(self.M, max(self.n_occ, 1))
         self.ws_bytes = max(lib.gsdft_j_forward_workspace_size(nl, self.n_aux),
                             lib.gsdft_j_vjp_workspace_size(nl, self.n_aux),
-                            lib.gsdft_j_solve_workspace_size(self.n_aux), 256)
+                            lib.gsdft_j_solve_workspace_size(self.n_aux),
+                            lib.gsdft_j_solve_inv_workspace_size(self.n_aux), 256)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        # [L^-1, L^-T] once per refresh: the per-step solve is then two row-parallel mat-vecs
+        self.Linv2 = None
+        if inverse_solve and L is not None and self.n_aux <= SOLVE_INV_MAX:
+            self.Linv2 = e(2, self.n_aux, self.n_aux)
+            lib.call("gsdft_j_solve_inverse", ptr(self.L), self.n_aux, ptr(self.Linv2),
+                     stream_handle(dev))
         # Optional CUDA-event brackets around the two integral kernels (recorded on the current
         # stream, the one the kernels are launched on): {"forward": [(start, end)], "vjp": [...]}.
         self.timing = False
@@ -164,8 +180,13 @@ class RIJEngine:
 
     def solve(self):
         """d = (L L^T)^-1 gamma, E = 1/2 gamma.d (replicated tail)."""
-        lib.call("gsdft_j_solve", ptr(self.L), ptr(self.gamma), self.n_aux, ptr(self.d),
-                 ptr(self.E), ptr(self.ws), self.ws_bytes, stream_handle(self.device))
+        if self.Linv2 is not None:
+            lib.call("gsdft_j_solve_inv", ptr(self.Linv2), ptr(self.gamma), self.n_aux,
+                     ptr(self.d), ptr(self.E), ptr(self.ws), self.ws_bytes,
+                     stream_handle(self.device))
+        else:
+            lib.call("gsdft_j_solve", ptr(self.L), ptr(self.gamma), self.n_aux, ptr(self.d),
+                     ptr(self.E), ptr(self.ws), self.ws_bytes, stream_handle(self.device))
         return self.E, self.d
 
     def backward_local(self, centers, C_occ, occ, g_E=None):
@@ -178,16 +199,17 @@ class RIJEngine:
         if end is not None:
             end.record(torch.cuda.current_stream(self.device))
         lib.call("gsdft_pair_chain", ptr(self.A9), ptr(centers), ptr(self.N), self.M,
-                 ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_twin), nl,
-                 self.plan.n, ptr(self.rec), ptr(self.sums), ptr(self.side), ptr(self.J), s)
+                 ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_twin),
+                 ptr(self.plan.rep_w), nl, self.plan.n, ptr(self.rec), ptr(self.sums),
+                 ptr(self.side), ptr(self.J), ptr(self.jw), s)
         lib.call("gsdft_splat_reduce", ptr(self.side), ptr(self.plan.order_i),
                  ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl, self.M,
                  ptr(self.gA6), ptr(self.gmu), ptr(self.gN), s)
         if self.n_occ > 0:
-            lib.call("gsdft_density_grad", ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos),
-                     ptr(self.plan.rep_w), ptr(self.J), ptr(self.plan.order_i),
-                     ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl,
-                     self.M, ptr(C_occ), ptr(occ), self.n_occ, ptr(self.g_C), s)
+            lib.call("gsdft_density_grad", ptr(self.plan.order_i), ptr(self.plan.seg_i),
+                     ptr(self.plan.partner_i), ptr(self.plan.order_j), ptr(self.plan.seg_j),
+                     ptr(self.plan.partner_j), ptr(self.jw), nl, self.M, ptr(C_occ), ptr(occ),
+                     self.n_occ, ptr(self.g_C), s)
         return self.gA6, self.gmu, self.gN, self.g_C
 
     def chart(self, quat, log_scale):

@@ -78,7 +78,9 @@ def _pairs_w(pi, pj, valid):
 def _engine(splats, C_occ, aux, pi, pj, valid, L):
     beta, R, KN = aux.quantities()
     pi, pj, w = _pairs_w(pi, pj, valid)
-    return RIJEngine(pi, pj, w, splats.n_basis, int(C_occ.shape[1]), beta, R.contiguous(), KN, L)
+    # one-shot calls: substitution solve, no O(n_aux^3) inverse
+    return RIJEngine(pi, pj, w, splats.n_basis, int(C_occ.shape[1]), beta, R.contiguous(), KN, L,
+                     inverse_solve=False)
 
 
 def df_coulomb_gamma_screened(splats, C_occ, occ, aux, pi, pj, chunk=2048, valid=None,

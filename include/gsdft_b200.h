@@ -142,12 +142,15 @@ int gsdft_pair_reps(const int32_t* pi, const int32_t* pj, const double* w, int64
 
 /* Step 2 — groupings of a contiguous slice of representatives (all of them on one device, one
  * rank's share on several): order_i / order_j (n_rep) list the slice's representatives stably
- * sorted by pi / pj, seg_i / seg_j (M+1) are the segment offsets. Used by the deterministic
- * per-splat reductions (the reference scatters with segment sums inside autodiff). */
+ * sorted by pi / pj, seg_i / seg_j (M+1) are the segment offsets, partner_i / partner_j (n_rep)
+ * the other splat of each sorted entry (pj of the by-pi grouping, pi of the by-pj one). Used by
+ * the deterministic per-splat reductions (the reference scatters with segment sums inside
+ * autodiff). */
 size_t gsdft_pair_groups_workspace_size(int64_t n_rep, int64_t M);
 int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos, int64_t n_rep,
-                      int64_t M, int32_t* order_i, int64_t* seg_i, int32_t* order_j,
-                      int64_t* seg_j, void* ws, size_t ws_bytes, gsdft_stream_t stream);
+                      int64_t M, int32_t* order_i, int64_t* seg_i, int32_t* partner_i,
+                      int32_t* order_j, int64_t* seg_j, int32_t* partner_j, void* ws,
+                      size_t ws_bytes, gsdft_stream_t stream);
 
 /* ---- auxiliary basis, metric, factor ------------------------------------------------------------ */
 
@@ -215,6 +218,19 @@ size_t gsdft_j_solve_workspace_size(int64_t n_aux);
 int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d, double* E,
                   void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
+/* The same solve through inverse factors, for repeated steps on one factor. gsdft_j_solve_inverse
+ * (once per refresh) writes Linv2 (2, n_aux, n_aux) = [L^-1, L^-T], row-major, from the lower
+ * factor L (n_aux <= GSDFT_SOLVE_INV_MAX). gsdft_j_solve_inv then gives d = L^-T (L^-1 gamma) and
+ * E = 1/2 |L^-1 gamma|^2 (= 1/2 gamma.d) as two row-parallel triangular mat-vecs, with no
+ * sequential substitution. Same outputs as gsdft_j_solve to rounding (the factor's condition
+ * number times the unit roundoff). Replaces, per step, cho_solve in df_coulomb_solve
+ * (gs_dft/coulomb/ri.py:472-482). */
+#define GSDFT_SOLVE_INV_MAX 16384
+int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv2, gsdft_stream_t stream);
+size_t gsdft_j_solve_inv_workspace_size(int64_t n_aux);
+int gsdft_j_solve_inv(const double* Linv2, const double* gamma, int64_t n_aux, double* d, double* E,
+                      void* ws, size_t ws_bytes, gsdft_stream_t stream);
+
 /* Reverse pass over (representative x aux): with dbar = g_E * d (g_E device scalar, NULL = 1), the
  * per-pair sums, (n_rep, GSDFT_VJP_FIELDS), from which J_a = sum_P (P|a) dbar_P and the cotangents
  * of A_hat, P, KN follow. Replaces the node reverse nodes_bwd and the eigh / dp2 autodiff
@@ -226,12 +242,14 @@ int gsdft_j_vjp(const double* rec, int64_t n_rep, const double* beta, const doub
 
 /* Chain per representative: sums -> cotangents of A_hat, P, KN -> per-side (A_i, mu_i, N_i), (A_j, mu_j,
  * N_j) contributions side (n_rep, GSDFT_SIDE_FIELDS); J (n, list order: written at each
- * representative's position and at its merged transpose's; 0 on zero-weight entries). The
- * reverse of gs_dft/coulomb/stream.py:203-215. */
+ * representative's position and at its merged transpose's; 0 on zero-weight entries); jw (n_rep)
+ * = J times the representative's summed weight, the factor of q's gradient. The reverse of
+ * gs_dft/coulomb/stream.py:203-215. */
 int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
                      const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
-                     const int32_t* rep_twin, int64_t n_rep, int64_t n, const double* rec,
-                     const double* sums, double* side, double* J, gsdft_stream_t stream);
+                     const int32_t* rep_twin, const double* rep_w, int64_t n_rep, int64_t n,
+                     const double* rec, const double* sums, double* side, double* J, double* jw,
+                     gsdft_stream_t stream);
 
 /* Deterministic per-splat sums of the side contributions (plan groupings) -> gA6 (M,6), gmu (M,3),
  * gN (M). Replaces the segment scatter of JAX autodiff through A[pi], A[pj]. */
@@ -240,12 +258,12 @@ int gsdft_splat_reduce(const double* side, const int32_t* order_i, const int64_t
                        double* gA6, double* gmu, double* gN, gsdft_stream_t stream);
 
 /* g_C[i,o] = occ_o (sum_{a: pi=i} J_a w_a C[pj_a,o] + sum_{a: pj=i} J_a w_a C[pi_a,o]): the gradient
- * through q_a (gs_dft/coulomb/ri.py:456). */
-int gsdft_density_grad(const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
-                       const double* rep_w, const double* J, const int32_t* order_i,
-                       const int64_t* seg_i, const int32_t* order_j, const int64_t* seg_j,
-                       int64_t n_rep, int64_t M, const double* C_occ, const double* occ,
-                       int64_t n_occ, double* g_C, gsdft_stream_t stream);
+ * through q_a (gs_dft/coulomb/ri.py:456). jw from gsdft_pair_chain; groupings and partners from
+ * gsdft_pair_groups. Summed in a fixed order (bitwise reproducible). */
+int gsdft_density_grad(const int32_t* order_i, const int64_t* seg_i, const int32_t* partner_i,
+                       const int32_t* order_j, const int64_t* seg_j, const int32_t* partner_j,
+                       const double* jw, int64_t n_rep, int64_t M, const double* C_occ,
+                       const double* occ, int64_t n_occ, double* g_C, gsdft_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -69,3 +69,47 @@ def test_ctypes_arity_matches_header():
     assert sorted(ar) == header_functions()
     for name, (_, args) in SIGNATURES.items():
         assert len(args) == ar[name], f"{name}: ctypes {len(args)} args, header {ar[name]}"
+
+
+def test_python_constants_match_header():
+    """Record widths and the inverse-solve size limit used by the host layer equal the header's."""
+    from gs_dft_b200 import _lib
+    text = open(HEADER).read()
+    defs = dict(re.findall(r"^#define\s+(GSDFT_\w+)\s+(\d+)", text, re.M))
+    assert int(defs["GSDFT_SIDE_FIELDS"]) == _lib.SIDE_FIELDS
+    assert int(defs["GSDFT_SOLVE_INV_MAX"]) == _lib.SOLVE_INV_MAX
+    for enum, width in (("GSDFT_REC_FIELDS", _lib.REC_FIELDS), ("GSDFT_VJP_FIELDS", _lib.VJP_FIELDS)):
+        body = re.search(r"enum\s*\{([^}]*\b" + enum + r"\b[^}]*)\}", text).group(1)
+        body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+        names = [t.strip().split("=")[0].strip() for t in body.split(",") if t.strip()]
+        assert names.index(enum) == width, (enum, names)
+
+
+def test_host_modules_resolve_every_name():
+    """Every global name a host module's code loads is bound in that module or in builtins (a
+    missing import shows up here, on CPU, rather than on the first GPU call)."""
+    import builtins
+    import dis
+    import importlib
+    import pkgutil
+    import types
+    import gs_dft_b200
+
+    def globals_of(code):
+        out = {i.argval for i in dis.get_instructions(code) if i.opname in ("LOAD_GLOBAL", "LOAD_NAME")}
+        for c in code.co_consts:
+            if isinstance(c, types.CodeType):
+                out |= globals_of(c)
+        return out
+
+    missing = []
+    for info in pkgutil.walk_packages(gs_dft_b200.__path__, "gs_dft_b200."):
+        spec = importlib.util.find_spec(info.name)
+        if spec is None or not str(spec.origin).endswith(".py"):
+            continue
+        mod = importlib.import_module(info.name)
+        ns = set(vars(mod)) | set(dir(builtins))
+        code = compile(open(mod.__file__).read(), mod.__file__, "exec")
+        missing += [(info.name, n) for n in sorted(globals_of(code))
+                    if n not in ns and not n.startswith("__")]
+    assert not missing, missing

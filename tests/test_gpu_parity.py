@@ -146,6 +146,48 @@ def test_gamma_energy_vs_reference(g, case):
     close(host(gu), d["gamma_unique"])
 
 
+@pytest.mark.parametrize("cfg,M", [(1, None), (2, 1500)])
+def test_inverse_factor_solve(g, cfg, M):
+    """gsdft_j_solve_inv (two triangular mat-vecs on [L^-1, L^-T]) against cho_solve on the same
+    factor (copied to the host), against the substitution path, and bitwise across calls;
+    oversize n is rejected. The factor is the device's own: cond(V + lam I) reaches ~1e9 here, so
+    last-ulp differences between two metrics move d far more than the solve method does (the
+    end-to-end tests compare E and gradients with the reference)."""
+    from gs_dft_b200._lib import lib, ptr, stream_handle
+    from gs_dft_b200.systems import make_config
+    sy = make_config(cfg, M)
+    s = g.Splat(dev(sy.quat), dev(sy.log_scale), dev(sy.centers))
+    aux = g.init_product_aux(s)
+    L = g.aux_cholesky(aux, 1e-8)
+    n = int(L.shape[0])
+    aq = O.aux_quantities(host(aux.log_alpha), host(aux.centers))
+    V = O.aux_metric(*aq)
+    Lo = host(L)
+    rng = np.random.default_rng(cfg)
+    gam_h = V @ rng.standard_normal(n) + np.abs(rng.standard_normal(n))
+    E_ref, d_ref = O.df_coulomb_solve(gam_h, Lo)
+    gam = dev(gam_h)
+    Linv2 = torch.empty((2, n, n), dtype=torch.float64, device="cuda")
+    st = stream_handle(gam.device)
+    lib.call("gsdft_j_solve_inverse", ptr(L), n, ptr(Linv2), st)
+    wb = lib.gsdft_j_solve_inv_workspace_size(n)
+    ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
+    outs = []
+    for _ in range(2):
+        d_, E_ = torch.empty(n, dtype=torch.float64, device="cuda"), torch.empty(1, dtype=torch.float64, device="cuda")
+        lib.call("gsdft_j_solve_inv", ptr(Linv2), ptr(gam), n, ptr(d_), ptr(E_), ptr(ws), wb, st)
+        outs.append((host(d_), float(E_)))
+    close(outs[0][0], d_ref)
+    close(outs[0][1], E_ref)
+    assert np.array_equal(outs[0][0], outs[1][0]) and outs[0][1] == outs[1][1]
+    d2, E2 = torch.empty(n, dtype=torch.float64, device="cuda"), torch.empty(1, dtype=torch.float64, device="cuda")
+    lib.call("gsdft_j_solve", ptr(L), ptr(gam), n, ptr(d2), ptr(E2), None, 0, st)
+    close(outs[0][0], host(d2))
+    close(outs[0][1], float(E2))
+    with pytest.raises(g._lib.GsdftError):
+        lib.call("gsdft_j_solve_inverse", ptr(L), 16385, ptr(Linv2), st)
+
+
 def _oracle_grad(d, pi, pj, v):
     q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
     la, R = O.init_product_aux(q)
