@@ -32,6 +32,10 @@ UNIT = "G pair-aux integrals/s"
 # (gs_dft/coulomb/ri.py:146-151,175-185 forward; :204-220 plus the dp2 chain reverse).
 FLOP_FWD, FLOP_VJP = 706, 2050
 FP64_DATASHEET = 37e12
+# DRAM bytes (read + write) per launch of each integral kernel, from one ncu capture of this bench
+# at configuration 1 on one GPU (profiles/integral_kernels_ethanol.md gives the command). Only that
+# workload has a capture; other configs and N > 1 report null.
+NCU_TRAFFIC_CFG1_N1 = {"j_vjp_kernel": 22.364160e6 + 65.776128e6, "j_forward_kernel": 21.477120e6}
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -318,6 +322,12 @@ def main():
     t_dom = max(t_vjp, t_fwd)
     flop = (FLOP_VJP if t_vjp >= t_fwd else FLOP_FWD) * n_aux * n_eval_local
     achieved = flop / (t_dom * 1e-3)
+    # minimal DRAM bytes of one launch: pair records in (18 FP64) and, for the reverse, the 13 per-pair
+    # sums out; aux records (reverse: 8 FP64 packed; forward: beta, R, KN in and gamma out)
+    if dom == "j_vjp_kernel":
+        alg_bytes = n_eval_local * (18 + 13) * 8 + n_aux * 8 * 8
+    else:
+        alg_bytes = n_eval_local * 18 * 8 + n_aux * 6 * 8
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "s_per_step": ms_per_step * 1e-3,
@@ -339,7 +349,10 @@ def main():
                      "peak_source": "measured DFMA probe on this GPU in this run (MEASURED_PEAKS.json has no FP64 figure); datasheet 37 TFLOP/s",
                      "frac_of_datasheet": achieved / FP64_DATASHEET,
                      "flop_per_integral": FLOP_VJP if t_vjp >= t_fwd else FLOP_FWD,
-                     "traffic": None},
+                     "traffic": (NCU_TRAFFIC_CFG1_N1[dom] if (args.config == 1 and world == 1)
+                                 else None),
+                     "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
+                     "algorithmic_bytes": alg_bytes},
         "gpu_launches": int(launches),
         "clocks": clk,
     }
