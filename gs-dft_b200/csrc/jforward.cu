@@ -157,11 +157,20 @@ constexpr int kFwTile = 32;      // pair records per staged tile (32 x 144 B)
 #ifndef GSDFT_FW_EXP2_BITS
 #define GSDFT_FW_EXP2_BITS 6
 #endif
+// Minimum resident CTAs per SM for the register budget (0: the compiler's choice).
+#ifndef GSDFT_FW_MINB
+#define GSDFT_FW_MINB 0
+#endif
+#if GSDFT_FW_MINB > 0
+#define GSDFT_FW_BOUNDS __launch_bounds__(kFwThreads, GSDFT_FW_MINB)
+#else
+#define GSDFT_FW_BOUNDS __launch_bounds__(kFwThreads)
+#endif
 constexpr int kFwNP = GSDFT_FW_NP;  // pairs evaluated together per thread (independent chains)
 constexpr int kFwBits = GSDFT_FW_EXP2_BITS;  // 2^kFwBits-entry weighted exp2 table per node
 constexpr size_t kFwDynSmem = sizeof(double) * GSDFT_NQUAD * (1 << kFwBits);
 
-__global__ void __launch_bounds__(kFwThreads)
+__global__ void GSDFT_FW_BOUNDS
     j_forward_kernel(const double* __restrict__ rec, int64_t n_live,
                      const double* __restrict__ beta, const double* __restrict__ R,
                      const double* __restrict__ KN, int64_t n_aux, int64_t per_split,

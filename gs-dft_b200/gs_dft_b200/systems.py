@@ -12,7 +12,9 @@ Conventions (fixed here, kept everywhere):
 * per-axis widths sigma are log-uniform in [0.2, 3.0] Bohr, stored as
   ``log_scale = -2 ln(sigma) - ln 2`` (precision eigenvalue 1/(2 sigma^2));
 * quaternions are normalised 4-D Gaussians (uniform random rotations);
-* ``C_occ`` is the Q factor of an M x n_occ Gaussian, ``occ = 2``.
+* ``C_occ`` is the Q factor of an M x n_occ Gaussian, ``occ = 2``;
+* nuclear charges are the elements' (H 1, C 6, O 8); the random test clouds cycle through
+  (6, 1, 8, 1, 7, 1) with no random draw, so adding them changed no other array.
 
 Geometries: CO2 with O at +-2.196 Bohr (1.1621 A, gs_dft/geometries.py:29-33); ethanol from
 gs_dft/geometries.py:68-78; water clusters from the monomer gs_dft/geometries.py:18-22, each
@@ -38,6 +40,11 @@ _ETHANOL_A = np.array([
     [-0.0227, 1.1812, -0.8852],  # H
 ])
 
+_ETHANOL_Z = np.array([6.0, 6.0, 8.0, 1.0, 1.0, 1.0, 1.0, 1.0, 1.0])
+_WATER_Z = np.array([8.0, 1.0, 1.0])
+_CO2_Z = np.array([6.0, 8.0, 8.0])
+_CYCLE_Z = (6.0, 1.0, 8.0, 1.0, 7.0, 1.0)
+
 _WATER_A = np.array([
     [0.0000, 0.0000, 0.1173],    # O
     [0.0000, 0.7572, -0.4692],   # H
@@ -58,6 +65,12 @@ class SplatSystem:
     occ: np.ndarray          # (n_occ,)
     eps: float = 1e-7
     lam: float = 1e-8
+    charges: np.ndarray | None = None   # (n_atoms,) nuclear charges Z_A
+
+    def __post_init__(self):
+        if self.charges is None:
+            self.charges = np.array([_CYCLE_Z[k % len(_CYCLE_Z)]
+                                     for k in range(self.atoms.shape[0])], dtype=np.float64)
 
     @property
     def M(self) -> int:
@@ -93,7 +106,7 @@ def water_cluster(n_side: int, n_keep: int | None, rng, spacing_A: float = 3.1) 
 
 
 def splat_cloud(name: str, atoms: np.ndarray, M: int, n_occ: int, rng,
-                eps: float = 1e-7) -> SplatSystem:
+                eps: float = 1e-7, charges: np.ndarray | None = None) -> SplatSystem:
     """Draw M splats over ``atoms`` (divmod allocation) and an orthonormal C_occ."""
     n_atoms = atoms.shape[0]
     base, rem = divmod(M, n_atoms)
@@ -108,7 +121,8 @@ def splat_cloud(name: str, atoms: np.ndarray, M: int, n_occ: int, rng,
     C_occ, _ = np.linalg.qr(G)
     occ = np.full(n_occ, 2.0)
     return SplatSystem(name=name, atoms=atoms, quat=quat, log_scale=log_scale,
-                       centers=centers, C_occ=np.ascontiguousarray(C_occ), occ=occ, eps=eps)
+                       centers=centers, C_occ=np.ascontiguousarray(C_occ), occ=occ, eps=eps,
+                       charges=None if charges is None else np.asarray(charges, np.float64))
 
 
 def make_config(index: int, M: int | None = None) -> SplatSystem:
@@ -117,23 +131,26 @@ def make_config(index: int, M: int | None = None) -> SplatSystem:
     if index == 0:
         rng = np.random.default_rng(0)
         atoms = np.array([[0.0, 0.0, 0.0], [0.0, 0.0, 2.196], [0.0, 0.0, -2.196]])
-        return splat_cloud("co2", atoms, M or 126, 11, rng)
+        return splat_cloud("co2", atoms, M or 126, 11, rng, charges=_CO2_Z)
     if index == 1:
         rng = np.random.default_rng(0)
         atoms = _ETHANOL_A * BOHR_PER_ANGSTROM
-        return splat_cloud("ethanol", atoms, M or 600, 13, rng)
+        return splat_cloud("ethanol", atoms, M or 600, 13, rng, charges=_ETHANOL_Z)
     if index == 2:
         rng = np.random.default_rng(1)
         atoms = water_cluster(4, None, rng)
-        return splat_cloud("h2o_64", atoms, M or 3000, 320, rng)
+        return splat_cloud("h2o_64", atoms, M or 3000, 320, rng,
+                           charges=np.tile(_WATER_Z, atoms.shape[0] // 3))
     if index == 3:
         rng = np.random.default_rng(2)
         atoms = water_cluster(7, None, rng)
-        return splat_cloud("h2o_343", atoms, M or 20000, 1715, rng)
+        return splat_cloud("h2o_343", atoms, M or 20000, 1715, rng,
+                           charges=np.tile(_WATER_Z, atoms.shape[0] // 3))
     if index == 4:
         rng = np.random.default_rng(3)
         atoms = water_cluster(10, 914, rng)
-        return splat_cloud("h2o_914", atoms, M or 53000, 4570, rng)
+        return splat_cloud("h2o_914", atoms, M or 53000, 4570, rng,
+                           charges=np.tile(_WATER_Z, atoms.shape[0] // 3))
     raise ValueError(f"unknown config {index}")
 
 

@@ -1,4 +1,5 @@
-"""CPU oracle for the screened density-fitted Coulomb (RI-J) path — TEST INFRASTRUCTURE ONLY.
+"""CPU oracle for the screened density-fitted Coulomb (RI-J) path and the screened nuclear
+attraction on the same pair list — TEST INFRASTRUCTURE ONLY.
 
 This module is the checker, never the product: only ``tests/``, ``__graft_entry__.smoke()`` and the
 ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it. The product path
@@ -545,19 +546,137 @@ def energy_and_grad(sys_arrays, aux_q, L, pi, pj, valid, chunk=1024):
         Ah, Pa, KNa = full_pair_quantities(qs, ci, cj)
         Jc, Abar, Pbar, KNbar = _pair_vjp_integral(beta, R, KN_aux, dvec, Ah, Pa, KNa, qa)
         J[np.arange(a, min(a + chunk, n))[live]] = Jc
-        gAi, gAj, gmui, gmuj, gNi, gNj = _pair_chain(qs, ci, cj, Abar, Pbar, KNbar)
-        np.add.at(gA, ci, gAi)
-        np.add.at(gA, cj, gAj)
-        np.add.at(gmu, ci, gmui)
-        np.add.at(gmu, cj, gmuj)
-        np.add.at(gN, ci, gNi)
-        np.add.at(gN, cj, gNj)
-        s = (Jc * cw)[:, None] * occ[None, :]
-        np.add.at(gC, ci, s * C_occ[cj])
-        np.add.at(gC, cj, s * C_occ[ci])
+        _scatter_pair_grads(qs, ci, cj, cw, Jc, Abar, Pbar, KNbar, C_occ, occ, gA, gmu, gN, gC)
     g_quat, g_log = chart_vjp(quat, log_scale, gA, gN)
     return dict(E=E, gamma=gamma, d=dvec, J=J, g_quat=g_quat, g_log_scale=g_log,
                 g_centers=gmu, g_C=gC, gA=gA, gmu=gmu, gN=gN)
+
+
+def _scatter_pair_grads(qs, ci, cj, cw, Jc, Abar, Pbar, KNbar, C_occ, occ, gA, gmu, gN, gC):
+    """Chain one chunk's pair cotangents to the splats (in place): (A_hat, P, KN) -> (A, mu, N) of
+    both members, and dE/dq_a = Jc -> C_occ through q_a = w_a sum_o occ_o C_io C_jo."""
+    gAi, gAj, gmui, gmuj, gNi, gNj = _pair_chain(qs, ci, cj, Abar, Pbar, KNbar)
+    np.add.at(gA, ci, gAi)
+    np.add.at(gA, cj, gAj)
+    np.add.at(gmu, ci, gmui)
+    np.add.at(gmu, cj, gmuj)
+    np.add.at(gN, ci, gNi)
+    np.add.at(gN, cj, gNj)
+    s = (Jc * cw)[:, None] * occ[None, :]
+    np.add.at(gC, ci, s * C_occ[cj])
+    np.add.at(gC, cj, s * C_occ[ci])
+
+# ----------------------------------------------------------------------------------------------
+#  Screened nuclear attraction on the pair list  (gs_dft/screening/pairs.py:348-370, 403-440)
+# ----------------------------------------------------------------------------------------------
+
+VNE_PREF = 2.0 * PI          # (2/sqrt(pi)) pi^1.5
+
+
+def nuclear_pairs(q_splat, pi, pj, coords, charges):
+    """V_ij = -N_iN_jK sum_A Z_A (2/sqrt(pi)) sum_t w_t pi^1.5 det(B)^-1/2
+    exp(-(t^2 |d|^2 - t^4 d.adj(B).d / det B)), B = A_hat + t^2 I, d = P_ij - R_A: one
+    reciprocal of det(B) per pair and node (gs_dft/screening/pairs.py:348-370)."""
+    Ah, P, NK = full_pair_quantities(q_splat, pi, pj)
+    d = P[:, None, :] - coords[None, :, :]
+    d2 = np.sum(d * d, axis=-1)
+    acc = np.zeros(d2.shape)
+    eye = np.eye(3)
+    for t, w in zip(QUAD_T, QUAD_W):
+        t2 = t * t
+        B = Ah + t2 * eye
+        invdet = 1.0 / det3(B)
+        quad = np.einsum("pak,pkl,pal->pa", d, adj3(B), d)
+        expo = t2 * d2 - (t2 * t2) * quad * invdet[:, None]
+        acc = acc + (w * PI ** 1.5) * np.sqrt(invdet)[:, None] * np.exp(-expo)
+    acc = (2.0 / math.sqrt(PI)) * acc
+    return -np.sum(charges[None, :] * acc, axis=1) * NK
+
+
+def density_pairs(C, occ, pi, pj):
+    """P_ij = sum_o occ_o C_io C_jo on the pair list (gs_dft/screening/pairs.py:403-406)."""
+    return np.sum(occ[None, :] * C[pi] * C[pj], axis=1)
+
+
+def external_energy(sys_arrays, pi, pj, valid, coords, charges, chunk=8192):
+    """E_ext = sum_a valid_a P_a V_a over the listed pairs, chunked
+    (gs_dft/screening/pairs.py:409-440; ``valid`` is the pair weight, pairs.py:325-327)."""
+    quat, log_scale, centers, C, occ = sys_arrays
+    q = full_quantities(quat, log_scale, centers)
+    n = pi.shape[0]
+    w = np.ones(n) if valid is None else np.asarray(valid, np.float64)
+    E = 0.0
+    for a in range(0, n, chunk):
+        sl = slice(a, a + chunk)
+        Pp = w[sl] * density_pairs(C, occ, pi[sl], pj[sl])
+        E = E + float(np.sum(Pp * nuclear_pairs(q, pi[sl], pj[sl], coords, charges)))
+    return E
+
+
+def _pair_vjp_nuclear(coords, charges, A_pair, P_pair, KN_pair, qa):
+    """For each pair: V_a and the cotangents of (A_hat, P_a, KN_a) of E = sum_a q_a V_a.
+
+    With d = R_A - P, t^2|d|^2 - t^4 d.B^-1 d = t^2 d.A_hat B^-1 d, so per node and atom
+    f = w det(B)^-1/2 exp(-t^2 d.A_hat B^-1 d) and
+      df/dA_hat = f (-1/2 B^-1 - t^4 z z^T),   df/dP = 2 t^2 f A_hat z,   z = B^-1 d
+    (the reference gets the same by JAX autodiff through pairs.py:356-370)."""
+    n = A_pair.shape[0]
+    d = coords[None, :, :] - P_pair[:, None, :]                     # (B, A, 3)
+    F = np.zeros(d.shape[:2])
+    GA = np.zeros((n, 3, 3))
+    GP = np.zeros((n, 3))
+    eye = np.eye(3)
+    for t, w in zip(QUAD_T, QUAD_W):
+        t2 = t * t
+        B = A_pair + t2 * eye
+        Binv = np.linalg.inv(B)
+        z = np.einsum("bkl,bal->bak", Binv, d)
+        ex = t2 * np.einsum("bak,bkl,bal->ba", d, A_pair, z)
+        f = w * (1.0 / np.sqrt(np.linalg.det(B)))[:, None] * np.exp(-ex)
+        F += f
+        fz = charges[None, :] * f
+        GA += (-0.5 * np.sum(fz, axis=1)[:, None, None] * Binv
+               - (t2 * t2) * np.einsum("ba,bak,bal->bkl", fz, z, z))
+        GP += 2.0 * t2 * np.einsum("bkl,bal,ba->bk", A_pair, z, fz)
+    S = F @ charges
+    c = -VNE_PREF * KN_pair
+    V = c * S
+    Abar = (qa * c)[:, None, None] * GA
+    Pbar = (qa * c)[:, None] * GP
+    KNbar = qa * (-VNE_PREF) * S
+    return V, Abar, Pbar, KNbar
+
+
+def external_energy_and_grad(sys_arrays, pi, pj, valid, coords, charges, chunk=1024):
+    """E_ext, V per listed pair (0 on zero-weight entries; it is dE/dq_a) and the gradient of E_ext
+    with respect to (quat, log_scale, centers, C_occ), pair list frozen."""
+    quat, log_scale, centers, C_occ, occ = sys_arrays
+    qs = full_quantities(quat, log_scale, centers)
+    M = centers.shape[0]
+    n = pi.shape[0]
+    w = np.ones(n) if valid is None else np.asarray(valid, np.float64)
+    V = np.zeros(n)
+    gA = np.zeros((M, 3, 3))
+    gmu = np.zeros((M, 3))
+    gN = np.zeros(M)
+    gC = np.zeros_like(C_occ)
+    E = 0.0
+    for a in range(0, n, chunk):
+        sl = slice(a, a + chunk)
+        ci, cj, cw = pi[sl], pj[sl], w[sl]
+        live = cw != 0
+        if not np.any(live):
+            continue
+        ci, cj, cw = ci[live], cj[live], cw[live]
+        qa = pair_density(C_occ, occ, ci, cj, cw)
+        Ah, Pa, KNa = full_pair_quantities(qs, ci, cj)
+        Vc, Abar, Pbar, KNbar = _pair_vjp_nuclear(coords, charges, Ah, Pa, KNa, qa)
+        V[np.arange(a, min(a + chunk, n))[live]] = Vc
+        E += float(np.sum(qa * Vc))
+        _scatter_pair_grads(qs, ci, cj, cw, Vc, Abar, Pbar, KNbar, C_occ, occ, gA, gmu, gN, gC)
+    g_quat, g_log = chart_vjp(quat, log_scale, gA, gN)
+    return dict(E=E, V=V, g_quat=g_quat, g_log_scale=g_log, g_centers=gmu, g_C=gC, gA=gA,
+                gmu=gmu, gN=gN)
 
 # ----------------------------------------------------------------------------------------------
 #  Convenience: a full refresh + step for one system

@@ -15,7 +15,13 @@ Outputs (compressed .npz, a few hundred KB in all):
   * ``ref_grad.npz``    — the gradient of E_J w.r.t. (quat, log_scale, centers, C_occ) by
     Richardson-extrapolated central differences of the executed reference energy (pair list,
     aux and factor frozen, as in training);
-  * ``ref_nodes_bwd.npz`` — the reference's hand-written node reverse pass on one block.
+  * ``ref_nodes_bwd.npz`` — the reference's hand-written node reverse pass on one block;
+  * ``ref_vne.npz``     — the screened nuclear attraction: V_ij on the ordered list
+    (``screened_nuclear_pairs``), E_ext on the padded ordered and the unique lists
+    (``screened_external_energy``) for the three systems, and the gradient of E_ext by
+    Richardson-extrapolated central differences of the executed reference on a 10-splat system.
+
+``python tests/golden/make_golden.py vne`` regenerates only ``ref_vne.npz``.
 """
 from __future__ import annotations
 
@@ -138,8 +144,63 @@ def make_nodes_bwd():
     print("nodes_bwd: done")
 
 
+def make_vne(eps=1e-7):
+    spec, _, pairs, _ = _modules()
+    out = {}
+    for name, s in _cases().items():
+        sp = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+        X, Z = J(s.atoms), J(s.charges)
+        C, occ = J(s.C_occ), J(s.occ)
+        pi, pj, _ = pairs.neighbor_pairs(sp, eps=eps)
+        n = int(pi.shape[0])
+        out[f"{name}_V"] = np.asarray(pairs.screened_nuclear_pairs(sp, pi, pj, X, Z))
+        pi2, pj2, v2 = pairs.neighbor_pairs(sp, eps=eps, pad_to=n + 37)
+        out[f"{name}_E"] = float(pairs.screened_external_energy(sp, C, occ, pi2, pj2, X, Z, v2,
+                                                                chunk=256))
+        ui, uj, uw = pairs.neighbor_pairs(sp, eps=eps, unique=True)
+        out[f"{name}_E_unique"] = float(pairs.screened_external_energy(sp, C, occ, ui, uj, X, Z,
+                                                                       uw, chunk=256))
+        out[f"{name}_atoms"] = s.atoms
+        out[f"{name}_charges"] = s.charges
+        print(f"vne {name}: n={n} E_ext={out[f'{name}_E']:.15g}")
+
+    s = small_random_system(10, 3, seed=3, spread=1.0, n_atoms=3)
+    sp0 = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+    pi, pj, v = pairs.neighbor_pairs(sp0, eps=eps)
+    X, Z = J(s.atoms), J(s.charges)
+
+    def energy(quat, ls, cen, C):
+        sp = spec.Splat(quat=J(quat), log_scale=J(ls), centers=J(cen))
+        return float(pairs.screened_external_energy(sp, J(C), J(s.occ), pi, pj, X, Z, v, chunk=64))
+
+    x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy()]
+
+    def fd(k, h):
+        g = np.zeros_like(x0[k])
+        for idx in np.ndindex(x0[k].shape):
+            xp = [a.copy() for a in x0]
+            xm = [a.copy() for a in x0]
+            xp[k][idx] += h
+            xm[k][idx] -= h
+            g[idx] = (energy(*xp) - energy(*xm)) / (2 * h)
+        return g
+
+    out.update(grad_quat=s.quat, grad_log_scale=s.log_scale, grad_centers=s.centers,
+               grad_C_occ=s.C_occ, grad_occ=s.occ, grad_atoms=s.atoms, grad_charges=s.charges,
+               grad_E=energy(*x0), eps=eps)
+    for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
+        h = 1e-3
+        out["grad_" + name] = (4 * fd(k, h / 2) - fd(k, h)) / 3      # Richardson, O(h^4)
+    np.savez_compressed(os.path.join(HERE, "ref_vne.npz"), **out)
+    print("vne grad: M=10 E_ext=", out["grad_E"])
+
+
 if __name__ == "__main__":
+    if sys.argv[1:] == ["vne"]:
+        make_vne()
+        sys.exit(0)
     for name, s in _cases().items():
         make_case(name, s)
     make_grad()
     make_nodes_bwd()
+    make_vne()

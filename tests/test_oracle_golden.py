@@ -139,3 +139,37 @@ def test_pad_rule_and_stripe():
         k = b.sum()
         assert b[:k].all() and not b[k:].any()
     assert O.stripe_pairs(pi, pi, v, 5)[0] is pi      # n % G != 0 leaves the list alone
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_nuclear_pairs_and_external_energy_match_reference(case):
+    """V_ij on the ordered list and E_ext on the padded ordered and the unique lists, against the
+    executed reference (gs_dft/screening/pairs.py:348-370, 409-440)."""
+    g = load_golden(case)
+    r = load_golden("ref_vne.npz")
+    name = case[4:-4]
+    q = _q(g)
+    X, Z = r[f"{name}_atoms"], r[f"{name}_charges"]
+    V = O.nuclear_pairs(q, g["ord_pi"], g["ord_pj"], X, Z)
+    ref = r[f"{name}_V"]
+    np.testing.assert_allclose(V, ref, rtol=1e-12, atol=1e-13 * np.abs(ref).max())
+    arr = (g["quat"], g["log_scale"], g["centers"], g["C_occ"], g["occ"])
+    E = O.external_energy(arr, g["pad_pi"], g["pad_pj"], g["pad_v"], X, Z)
+    np.testing.assert_allclose(E, float(r[f"{name}_E"]), rtol=1e-12)
+    Eu = O.external_energy(arr, g["uni_pi"], g["uni_pj"], g["uni_w"], X, Z)
+    np.testing.assert_allclose(Eu, float(r[f"{name}_E_unique"]), rtol=1e-12)
+    np.testing.assert_allclose(Eu, E, rtol=1e-11)         # unique weights reproduce the ordered sum
+
+
+def test_external_gradient_matches_reference_finite_differences():
+    """The hand-derived gradient of E_ext (the reference's is JAX autodiff) against Richardson
+    central differences of the executed reference energy."""
+    r = load_golden("ref_vne.npz")
+    arr = (r["grad_quat"], r["grad_log_scale"], r["grad_centers"], r["grad_C_occ"], r["grad_occ"])
+    q = O.full_quantities(*arr[:3])
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=float(r["eps"]))
+    res = O.external_energy_and_grad(arr, pi, pj, v, r["grad_atoms"], r["grad_charges"])
+    np.testing.assert_allclose(res["E"], float(r["grad_E"]), rtol=1e-13)
+    for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
+        ref = r["grad_" + k]
+        np.testing.assert_allclose(res[k], ref, rtol=0, atol=2e-9 * np.abs(ref).max())
