@@ -8,13 +8,15 @@ the analytic gradient, as hand-written sm_100a CUDA kernels behind a C ABI
 from .basis import IsotropicSplat, Splat, init_product_aux
 from .coulomb import (RIJEngine, aux_cholesky, aux_metric, aux_quantities,
                       df_coulomb_energy_screened, df_coulomb_gamma_screened, df_coulomb_solve)
-from .ks import (CoulombKS, DFSpec, Pairlist, SplatModel, SplatState, df, pad_rule, pairlist,
-                 refresh)
-from .screening import neighbor_pairs, stripe_pairs
+from .ks import (CoulombKS, DFSpec, ExternalKS, Pairlist, SplatModel, SplatState, df, pad_rule,
+                 pairlist, refresh)
+from .screening import (density_pairs, neighbor_pairs, screened_external_energy,
+                        screened_nuclear_pairs, stripe_pairs)
 
 __all__ = [
     "Splat", "IsotropicSplat", "init_product_aux", "neighbor_pairs", "stripe_pairs",
     "aux_quantities", "aux_metric", "aux_cholesky", "df_coulomb_gamma_screened",
     "df_coulomb_solve", "df_coulomb_energy_screened", "RIJEngine", "df", "pairlist", "DFSpec",
     "Pairlist", "CoulombKS", "SplatModel", "SplatState", "refresh", "pad_rule",
+    "screened_nuclear_pairs", "density_pairs", "screened_external_energy", "ExternalKS",
 ]

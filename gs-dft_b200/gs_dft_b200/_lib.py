@@ -68,6 +68,10 @@ SIGNATURES = {
                                 _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "gsdft_splat_reduce": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p,
                                   _c_p]),
+    "gsdft_vne_workspace_size": (_sz, [_i64]),
+    "gsdft_vne": (_i32, [_c_p, _i64, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i32,
+                         _c_p, _sz, _c_p]),
+    "gsdft_density_pairs": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _i64, _c_p, _c_p]),
     "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
                                   _i64, _c_p, _c_p]),
 }

@@ -9,6 +9,12 @@ workspace), allocated once per refresh, so a step allocates nothing. A step is
 
 which is the single-device screened DF step of the reference (gs_dft/coulomb/ri.py:436-494 under
 jax.value_and_grad, gs_dft/ks/train.py:367-382) with the gradient written out.
+
+With ``atoms`` the engine also evaluates the screened nuclear attraction on the same pair list,
+E_ne = sum_a q_a V_a (gs_dft/screening/pairs.py:348-370, 409-440, as SplatKS uses it with a
+screened pair list, gs_dft/ks/energy.py:326-328): its reverse-pass sums are added to the RI-J ones
+before the shared chain, so one backward pass gives the gradient of E_J + E_ne. With ``beta=None``
+the engine carries E_ne alone.
 """
 from __future__ import annotations
 
@@ -101,21 +107,27 @@ class RIJEngine:
         pi, pj: int32 pair indices (device); w: float64 weights (0 = padding; 1 ordered; 2 unique).
         M: number of splats; n_occ: occupied orbitals.
         beta, R, KN: the aux quantities; L: lower Cholesky factor of V + lam I (row-major).
+            ``beta=None``: no RI-J term (an engine for the nuclear attraction alone).
         rank, world: this device evaluates representatives [n_rep*rank//world, n_rep*(rank+1)//world).
         merge_twins: evaluate each (i,j)/(j,i) pair of a live transposed twin once (same integral).
         inverse_solve: form [L^-1, L^-T] once (O(n_aux^3)) so each step's solve is two parallel
             mat-vecs; for engines that run many steps. Off: per-step triangular substitution.
+        atoms: optional (n_atoms, 4) float64 device tensor of nuclei (x, y, z, Z) in Bohr: adds the
+            screened nuclear attraction E_ne on the same pairs.
     """
 
-    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1, merge_twins=True,
-                 inverse_solve=True):
+    def __init__(self, pi, pj, w, M, n_occ, beta=None, R=None, KN=None, L=None, rank=0, world=1,
+                 merge_twins=True, inverse_solve=True, atoms=None):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi = pi.contiguous()
         self.pj = pj.contiguous()
         self.w = w.to(F64).contiguous()
         self.beta, self.R, self.KN, self.L = beta, R, KN, L
-        self.n_aux = int(beta.shape[0])
+        self.rij = beta is not None
+        self.n_aux = int(beta.shape[0]) if self.rij else 0
+        if not self.rij and atoms is None:
+            raise ValueError("RIJEngine needs the aux quantities (beta, R, KN), atoms, or both")
         self.plan = make_plan(self.pi, self.pj, self.w, self.M, rank, world, merge_twins)
         dev, nl, n = self.device, self.plan.n_rep, self.plan.n
         e = lambda *s: torch.empty(s, dtype=F64, device=dev)
@@ -129,10 +141,22 @@ class RIJEngine:
         self.gA6, self.gmu, self.gN = e(self.M, 6), e(self.M, 3), e(self.M)
         self.g_quat, self.g_log = e(self.M, 4), e(self.M, 3)
         self.g_C = e(self.M, max(self.n_occ, 1))
-        self.ws_bytes = max(lib.gsdft_j_forward_workspace_size(nl, self.n_aux),
-                            lib.gsdft_j_vjp_workspace_size(nl, self.n_aux),
-                            lib.gsdft_j_solve_workspace_size(self.n_aux),
-                            lib.gsdft_j_solve_inv_workspace_size(self.n_aux), 256)
+        self.atoms, self.n_atoms = None, 0
+        if atoms is not None:
+            self.atoms = atoms.to(device=dev, dtype=F64).contiguous()
+            if self.atoms.dim() != 2 or self.atoms.shape[1] != 4:
+                raise ValueError("atoms must be (n_atoms, 4): x, y, z, Z")
+            self.n_atoms = int(self.atoms.shape[0])
+            self.E_ne, self.V = e(1), e(max(n, 1))
+        sizes = [256]
+        if self.rij:
+            sizes += [lib.gsdft_j_forward_workspace_size(nl, self.n_aux),
+                      lib.gsdft_j_vjp_workspace_size(nl, self.n_aux),
+                      lib.gsdft_j_solve_workspace_size(self.n_aux),
+                      lib.gsdft_j_solve_inv_workspace_size(self.n_aux)]
+        if self.atoms is not None:
+            sizes.append(lib.gsdft_vne_workspace_size(nl))
+        self.ws_bytes = max(sizes)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
         # [L^-1, L^-T] once per refresh: the per-step solve is then two row-parallel mat-vecs
         self.Linv2 = None
@@ -143,7 +167,7 @@ class RIJEngine:
         # Optional CUDA-event brackets around the two integral kernels (recorded on the current
         # stream, the one the kernels are launched on): {"forward": [(start, end)], "vjp": [...]}.
         self.timing = False
-        self.events = {"forward": [], "vjp": []}
+        self.events = {"forward": [], "vjp": [], "vne": []}
 
     def _bracket(self, name):
         if not self.timing:
@@ -162,15 +186,35 @@ class RIJEngine:
         return sum(a.elapsed_time(b) for a, b in ev) / max(len(ev), 1)
 
     # -- stages -----------------------------------------------------------------------------------
+    def prepare(self, quat, log_scale, centers, C_occ, occ):
+        """Splat quantities and the pair records (A_hat eigenframe, P, KN, q) of this device's
+        representatives."""
+        s = stream_handle(self.device)
+        lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),
+                 ptr(self.N), s)
+        lib.call("gsdft_pair_prep", ptr(self.A9), ptr(centers), ptr(self.N), self.M, ptr(self.pi),
+                 ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_w), self.plan.n_rep,
+                 ptr(C_occ), ptr(occ), self.n_occ, ptr(self.rec), s)
+
+    def external(self, sums=False, add=False, g_E=None):
+        """This device's E_ne = sum_a q_a V_a and V per list entry (after ``prepare``); with
+        ``sums`` also the reverse-pass sums of g_E * E_ne, written or (``add``) added."""
+        end = self._bracket("vne")
+        lib.call("gsdft_vne", ptr(self.rec), self.plan.n_rep, ptr(self.atoms), self.n_atoms,
+                 ptr(g_E), ptr(self.plan.rep_pos), ptr(self.plan.rep_twin), self.plan.n,
+                 ptr(self.V), ptr(self.E_ne), ptr(self.sums) if sums else None, int(bool(add)),
+                 ptr(self.ws), self.ws_bytes, stream_handle(self.device))
+        if end is not None:
+            end.record(torch.cuda.current_stream(self.device))
+        return self.E_ne
+
     def forward_local(self, quat, log_scale, centers, C_occ, occ):
         """Splat quantities, pair prep and this device's gamma (before any allreduce)."""
         s = stream_handle(self.device)
         nl = self.plan.n_rep
-        lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),
-                 ptr(self.N), s)
-        lib.call("gsdft_pair_prep", ptr(self.A9), ptr(centers), ptr(self.N), self.M, ptr(self.pi),
-                 ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_w), nl, ptr(C_occ),
-                 ptr(occ), self.n_occ, ptr(self.rec), s)
+        self.prepare(quat, log_scale, centers, C_occ, occ)
+        if not self.rij:
+            return None
         end = self._bracket("forward")
         lib.call("gsdft_j_forward", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
                  self.n_aux, ptr(self.gamma), ptr(self.ws), self.ws_bytes, s)
@@ -189,15 +233,21 @@ class RIJEngine:
                      ptr(self.E), ptr(self.ws), self.ws_bytes, stream_handle(self.device))
         return self.E, self.d
 
-    def backward_local(self, centers, C_occ, occ, g_E=None):
-        """This device's pre-chart splat cotangents (gA6, gmu, gN), J per list entry and g_C."""
+    def backward_local(self, centers, C_occ, occ, g_E=None, g_E_ne=None):
+        """This device's pre-chart splat cotangents (gA6, gmu, gN), J = dE/dq per list entry and
+        g_C, of g_E E_J + g_E_ne E_ne (the terms the engine carries; device scalars, None = 1).
+        With atoms this also evaluates E_ne."""
         s = stream_handle(self.device)
         nl = self.plan.n_rep
-        end = self._bracket("vjp")
-        lib.call("gsdft_j_vjp", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
-                 ptr(self.d), ptr(g_E), self.n_aux, ptr(self.sums), ptr(self.ws), self.ws_bytes, s)
-        if end is not None:
-            end.record(torch.cuda.current_stream(self.device))
+        if self.rij:
+            end = self._bracket("vjp")
+            lib.call("gsdft_j_vjp", ptr(self.rec), nl, ptr(self.beta), ptr(self.R), ptr(self.KN),
+                     ptr(self.d), ptr(g_E), self.n_aux, ptr(self.sums), ptr(self.ws),
+                     self.ws_bytes, s)
+            if end is not None:
+                end.record(torch.cuda.current_stream(self.device))
+        if self.atoms is not None:
+            self.external(sums=True, add=self.rij, g_E=g_E_ne)
         lib.call("gsdft_pair_chain", ptr(self.A9), ptr(centers), ptr(self.N), self.M,
                  ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_twin),
                  ptr(self.plan.rep_w), nl, self.plan.n, ptr(self.rec), ptr(self.sums),
@@ -218,17 +268,24 @@ class RIJEngine:
         return self.g_quat, self.g_log
 
     # -- whole step -------------------------------------------------------------------------------
-    def step(self, quat, log_scale, centers, C_occ, occ, grad=True, g_E=None):
-        """Single-device J-build + gradient. Returns a dict of device tensors (views of the
-        engine's buffers: copy them before the next step if they must persist)."""
+    def step(self, quat, log_scale, centers, C_occ, occ, grad=True, g_E=None, g_E_ne=None):
+        """Single-device J-build (and E_ne with atoms) + gradient of their sum. Returns a dict of
+        device tensors (views of the engine's buffers: copy them before the next step if they
+        must persist)."""
         self.forward_local(quat, log_scale, centers, C_occ, occ)
-        self.solve()
-        out = dict(E=self.E, gamma=self.gamma, d=self.d)
+        out = {}
+        if self.rij:
+            self.solve()
+            out.update(E=self.E, gamma=self.gamma, d=self.d)
         if grad:
-            self.backward_local(centers, C_occ, occ, g_E)
+            self.backward_local(centers, C_occ, occ, g_E, g_E_ne)
             self.chart(quat, log_scale)
             out.update(J=self.J, g_quat=self.g_quat, g_log_scale=self.g_log, g_centers=self.gmu,
                        g_C=self.g_C[:, :self.n_occ], gA6=self.gA6, gN=self.gN)
+        elif self.atoms is not None:
+            self.external()
+        if self.atoms is not None:
+            out.update(E_ne=self.E_ne, V=self.V[:self.plan.n])
         return out
 
 

@@ -1,6 +1,6 @@
 """Strategy specs, refresh state and the Coulomb builder (the drop-in surface of gs_dft.ks)."""
 from .terms import (DFSpec, Pairlist, SCREEN_PAD, ScreenedProductDFCoulomb, df, pairlist)
-from .state import CoulombKS, SplatModel, SplatState, pad_rule, refresh
+from .state import CoulombKS, ExternalKS, SplatModel, SplatState, pad_rule, refresh
 
 __all__ = ["DFSpec", "Pairlist", "SCREEN_PAD", "ScreenedProductDFCoulomb", "df", "pairlist",
-           "CoulombKS", "SplatModel", "SplatState", "pad_rule", "refresh"]
+           "CoulombKS", "ExternalKS", "SplatModel", "SplatState", "pad_rule", "refresh"]

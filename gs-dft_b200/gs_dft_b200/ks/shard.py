@@ -12,6 +12,11 @@ representatives, equal to within one: every representative costs the same N_aux 
 padding costs nothing, so equal counts are equal work, and contiguity keeps each rank's per-splat
 scatter local. The reference instead deals the padded list round-robin (``stripe_pairs``) because
 its padding is appended; striped lists are accepted too (a stripe only reorders the same pairs).
+
+With ``atoms`` each rank also evaluates the screened nuclear attraction on its slice (the
+reference's ``screened_external_energy`` on the local stripe, psum'd: gs_dft/ks/shard.py:223,
+267); its partial E_ne travels in one extra slot of the packed gradient allreduce, so the step
+keeps two collectives.
 """
 from __future__ import annotations
 
@@ -31,13 +36,17 @@ class ShardedRIJ:
     """
 
     def __init__(self, pi, pj, valid, M, n_occ, beta, R, KN, L, rank: int, world: int,
-                 group=None, engine_cls=RIJEngine):
+                 group=None, engine_cls=RIJEngine, atoms=None):
         self.rank, self.world, self.group = rank, world, group
+        kw = {} if atoms is None else {"atoms": atoms}
         self.engine = engine_cls(pi.contiguous(), pj.contiguous(), pair_weight(valid).contiguous(),
-                                 M, n_occ, beta, R, KN, L, rank=rank, world=world)
+                                 M, n_occ, beta, R, KN, L, rank=rank, world=world, **kw)
         self.M, self.n_occ = int(M), int(n_occ)
-        self.packed = torch.empty(10 * self.M + self.M * max(self.n_occ, 1),
-                                  dtype=torch.float64, device=pi.device)
+        self.external = atoms is not None
+        # [gA6 (6M) | gmu (3M) | gN (M) | g_C (M n_occ) | E_ne partial (1)]
+        self.n_gc = self.M * max(self.n_occ, 1)
+        self.packed = torch.empty(10 * self.M + self.n_gc + 1, dtype=torch.float64,
+                                  device=pi.device)
 
     # The step in three parts around its two collectives, so that the compute parts can be
     # captured as CUDA graphs while the NCCL allreduces stay eager.
@@ -53,7 +62,9 @@ class ShardedRIJ:
         p[6 * M:9 * M].copy_(gmu.reshape(-1))
         p[9 * M:10 * M].copy_(gN)
         if self.n_occ:
-            p[10 * M:].copy_(gC[:, :self.n_occ].reshape(-1))
+            p[10 * M:10 * M + M * self.n_occ].copy_(gC[:, :self.n_occ].reshape(-1))
+        if self.external:
+            p[-1:].copy_(eng.E_ne)
         return E, d
 
     def _tail(self, quat, log_scale):
@@ -70,15 +81,24 @@ class ShardedRIJ:
 
     def _outputs(self, E, d, g_quat, g_log):
         M, eng = self.M, self.engine
-        return dict(E=E, gamma=eng.gamma, d=d, J_local=eng.J, g_quat=g_quat, g_log_scale=g_log,
-                    g_centers=eng.gmu, g_C=self.packed[10 * M:].view(M, -1)[:, :self.n_occ])
+        gC = self.packed[10 * M:10 * M + self.n_gc].view(M, -1)[:, :self.n_occ]
+        out = dict(E=E, gamma=eng.gamma, d=d, J_local=eng.J, g_quat=g_quat, g_log_scale=g_log,
+                   g_centers=eng.gmu, g_C=gC)
+        if self.external:
+            out["E_ne"] = self.packed[-1:]
+        return out
 
     def step(self, quat, log_scale, centers, C_occ, occ, grad=True):
         gamma = self._forward(quat, log_scale, centers, C_occ, occ)
         self._allreduce(gamma)
         if not grad:
             E, d = self.engine.solve()
-            return dict(E=E, gamma=gamma, d=d)
+            out = dict(E=E, gamma=gamma, d=d)
+            if self.external:
+                E_ne = self.engine.external().clone()
+                self._allreduce(E_ne)
+                out["E_ne"] = E_ne
+            return out
         E, d = self._middle(centers, C_occ, occ)
         self._allreduce(self.packed)
         g_quat, g_log = self._tail(quat, log_scale)

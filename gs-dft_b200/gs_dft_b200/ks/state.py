@@ -3,8 +3,10 @@
 ``SplatState`` / ``refresh`` mirror gs_dft/ks/energy.py:121-139 and :421-474 for the fields the
 screened DF Coulomb needs (pairs, aux, cholV); the pad rule mirrors gs_dft/ks/train.py:356-359.
 ``CoulombKS`` carries the ``coulomb`` / ``screen`` / ``mesh`` arguments of ``SplatKS``
-(gs_dft/ks/energy.py:166-173) and evaluates the Hartree term E_J of a model; the rest of the
-Kohn-Sham energy (kinetic, external, XC) is outside this library.
+(gs_dft/ks/energy.py:166-173) and evaluates the Hartree term E_J of a model; ``ExternalKS`` is the
+screened external term of the same ``SplatKS`` branch, E_external on the refresh state's pair list
+(gs_dft/ks/energy.py:326-328). The rest of the Kohn-Sham energy (kinetic, XC) is outside this
+library.
 """
 from __future__ import annotations
 
@@ -16,6 +18,7 @@ from ..basis.isotropic import IsotropicSplat, init_product_aux
 from ..basis.spectral import Splat
 from ..coulomb.engine import RIJEngine
 from ..coulomb.ri import aux_cholesky
+from ..screening.nuclear import _ScreenedExternalEnergy, atom_records
 from ..screening.pairs import count_significant, neighbor_pairs, pair_weight, stripe_pairs
 from .terms import DFSpec, Pairlist, ScreenedProductDFCoulomb
 
@@ -42,6 +45,7 @@ class SplatState:
     aux: IsotropicSplat | None = None
     cholV: torch.Tensor | None = None
     _engine: RIJEngine | None = field(default=None, repr=False)
+    _ext_engine: RIJEngine | None = field(default=None, repr=False)
 
     def engine_for(self, basis, C_occ) -> RIJEngine:
         """The device engine for this state's pairs/aux/factor (built once, reused per step)."""
@@ -52,6 +56,16 @@ class SplatState:
                                      pair_weight(valid).contiguous(), basis.n_basis,
                                      int(C_occ.shape[1]), beta, R.contiguous(), KN, self.cholV)
         return self._engine
+
+    def external_engine_for(self, basis, C_occ, atoms) -> RIJEngine:
+        """The device engine of the screened external term on this state's pairs (built once)."""
+        if self._ext_engine is None:
+            pi, pj, valid = self.pairs
+            self._ext_engine = RIJEngine(pi.to(torch.int32).contiguous(),
+                                         pj.to(torch.int32).contiguous(),
+                                         pair_weight(valid).contiguous(), basis.n_basis,
+                                         int(C_occ.shape[1]), atoms=atoms)
+        return self._ext_engine
 
 
 def refresh(ks, basis: Splat, *, pad_to: int | None = None,
@@ -98,3 +112,24 @@ class CoulombKS:
             raise ValueError("coulomb=df() needs the refresh state: see refresh(ks, basis).")
         e_j, _ = self.coulomb.energy(model.basis, model.C, None, model.occupations, state)
         return e_j
+
+
+class ExternalKS:
+    """The screened external term of ``SplatKS(..., screen=pairlist())``:
+    ``ext(model, state) -> E_external = sum_ij P_ij V_ij`` over the refresh state's pair list
+    (gs_dft/ks/energy.py:326-328 with gs_dft/screening/pairs.py:409-440), differentiable in the
+    model's splats and C. The coefficients are used as given: pass orthonormalised orbitals, as the
+    reference does (its C_orth)."""
+
+    def __init__(self, atom_coords, atom_charges):
+        self.atom_coords = atom_coords
+        self.atom_charges = atom_charges
+
+    def __call__(self, model: SplatModel, state: SplatState):
+        if state is None or state.pairs is None:
+            raise ValueError("the screened external term needs the refresh state's pair list")
+        basis = model.basis
+        atoms = atom_records(self.atom_coords, self.atom_charges, basis.centers.device)
+        eng = state.external_engine_for(basis, model.C, atoms)
+        return _ScreenedExternalEnergy.apply(basis.quat, basis.log_scale, basis.centers, model.C,
+                                             model.occupations, eng)

@@ -265,6 +265,28 @@ int gsdft_density_grad(const int32_t* order_i, const int64_t* seg_i, const int32
                        const double* jw, int64_t n_rep, int64_t M, const double* C_occ,
                        const double* occ, int64_t n_occ, double* g_C, gsdft_stream_t stream);
 
+/* Screened nuclear attraction on the pair representatives: V_a = -2 pi KN_a sum_A Z_A sum_t w_t
+ * det(A_hat + t^2 I)^-1/2 exp(-t^2 d.A_hat (A_hat + t^2 I)^-1 d), d = R_A - P_a, and
+ * E_ne = sum_a q_a V_a (q from rec, so pair weights and twin merging apply). Replaces
+ * _full_nuclear_pairs / screened_nuclear_pairs / screened_external_energy
+ * (gs_dft/screening/pairs.py:348-370, 378-380, 409-440). atoms (n_atoms, 4) row-major = (x, y, z, Z),
+ * 32-byte aligned; E a device scalar (always written). V (optional): each representative's V at
+ * rep_pos[a] and, when rep_twin[a] >= 0, at rep_twin[a] of a list of length n (zero elsewhere), or at
+ * a when rep_pos is NULL. sums (optional): the reverse-pass sums of g_E * E_ne (g_E a device scalar,
+ * NULL = 1) in gsdft_j_vjp's layout and scale, written (add = 0) or added (add = 1: onto gsdft_j_vjp's,
+ * so one gsdft_pair_chain carries E_J + E_ne and its J is dE/dq including V). Deterministic. */
+size_t gsdft_vne_workspace_size(int64_t n_rep);
+int gsdft_vne(const double* rec, int64_t n_rep, const double* atoms, int64_t n_atoms,
+              const double* g_E, const int32_t* rep_pos, const int32_t* rep_twin, int64_t n,
+              double* V, double* E, double* sums, int add, void* ws, size_t ws_bytes,
+              gsdft_stream_t stream);
+
+/* P_a = sum_o occ_o C_occ[pi_a, o] C_occ[pj_a, o] for every listed pair (no weights), the density
+ * matrix entries on the pair list without forming P. Replaces density_pairs
+ * (gs_dft/screening/pairs.py:403-406). */
+int gsdft_density_pairs(const int32_t* pi, const int32_t* pj, int64_t n, const double* C_occ,
+                        const double* occ, int64_t n_occ, double* P, gsdft_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

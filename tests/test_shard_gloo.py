@@ -29,7 +29,7 @@ def _full(g6):
 class OracleEngine:
     """CPU stand-in for RIJEngine with the same stage methods, computed by the oracle."""
 
-    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1):
+    def __init__(self, pi, pj, w, M, n_occ, beta, R, KN, L, rank=0, world=1, atoms=None):
         # this rank's contiguous share of the live entries (the sum over pairs is order-free)
         live = np.nonzero(w.numpy() != 0)[0]
         r0, r1 = len(live) * rank // world, len(live) * (rank + 1) // world
@@ -39,6 +39,7 @@ class OracleEngine:
         self.aq = (beta.numpy(), R.numpy(), KN.numpy())
         self.L = L.numpy()
         self.J = torch.zeros(max(len(self.pi), 1), dtype=torch.float64)
+        self.atoms = None if atoms is None else atoms.numpy()
 
     def forward_local(self, quat, ls, cen, C, occ):
         q = O.full_quantities(quat.numpy(), ls.numpy(), cen.numpy())
@@ -50,7 +51,7 @@ class OracleEngine:
 
     def solve(self):
         E, d = O.df_coulomb_solve(self.gamma.numpy(), self.L)
-        self.E, self.d = torch.tensor([E]), torch.from_numpy(d)
+        self.E, self.d = torch.tensor([E], dtype=torch.float64), torch.from_numpy(d)
         return self.E, self.d
 
     def backward_local(self, cen, C, occ, g_E=None):
@@ -61,6 +62,11 @@ class OracleEngine:
         Ah, Pa, KNa = O.full_pair_quantities(self.qs, ci, cj)
         J, Abar, Pbar, KNbar = O._pair_vjp_integral(*self.aq[:2], self.aq[2], self.d.numpy(), Ah,
                                                     Pa, KNa, qa)
+        if self.atoms is not None:
+            V, Ab2, Pb2, Kb2 = O._pair_vjp_nuclear(self.atoms[:, :3], self.atoms[:, 3], Ah, Pa,
+                                                   KNa, qa)
+            J, Abar, Pbar, KNbar = J + V, Abar + Ab2, Pbar + Pb2, KNbar + Kb2
+            self.E_ne = torch.tensor([float(np.sum(qa * V))], dtype=torch.float64)
         gAi, gAj, gmui, gmuj, gNi, gNj = O._pair_chain(self.qs, ci, cj, Abar, Pbar, KNbar)
         gA, gmu, gN = np.zeros((self.M, 3, 3)), np.zeros((self.M, 3)), np.zeros(self.M)
         np.add.at(gA, ci, gAi)
@@ -94,7 +100,7 @@ def _problem():
     return s, pi, pj, v, aq, L
 
 
-def _run(rank, world, port, out):
+def _run(rank, world, port, out, with_atoms=False):
     import torch.distributed as dist
     from gs_dft_b200.ks.shard import ShardedRIJ
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -102,11 +108,12 @@ def _run(rank, world, port, out):
         dist.init_process_group("gloo", rank=rank, world_size=world)
     s, pi, pj, v, aq, L = _problem()
     T = torch.from_numpy
+    atoms = T(np.concatenate([s.atoms, s.charges[:, None]], 1)) if with_atoms else None
     sh = ShardedRIJ(T(pi), T(pj), T(v), s.M, s.n_occ, T(aq[0]), T(aq[1]), T(aq[2]), T(L), rank,
-                    world, engine_cls=OracleEngine)
+                    world, engine_cls=OracleEngine, atoms=atoms)
     o = sh.step(T(s.quat), T(s.log_scale), T(s.centers), T(s.C_occ), T(s.occ))
-    res = {k: o[k].numpy().copy() for k in ("E", "gamma", "g_quat", "g_log_scale", "g_centers",
-                                               "g_C")}
+    keys = ("E", "gamma", "g_quat", "g_log_scale", "g_centers", "g_C") + (("E_ne",) if with_atoms else ())
+    res = {k: o[k].numpy().copy() for k in keys}
     if world > 1:
         dist.destroy_process_group()
     np.savez(out.format(rank=rank, world=world), **res)
@@ -118,13 +125,26 @@ def _free_port():
         return sk.getsockname()[1]
 
 
-def test_two_rank_gloo_equals_single_rank(tmp_path):
+@pytest.mark.parametrize("with_atoms", [False, True])
+def test_two_rank_gloo_equals_single_rank(tmp_path, with_atoms):
     import torch.multiprocessing as mp
     out = str(tmp_path / "r{rank}_w{world}.npz")
-    _run(0, 1, _free_port(), out)
-    mp.start_processes(_run, args=(2, _free_port(), out), nprocs=2, start_method="spawn")
+    _run(0, 1, _free_port(), out, with_atoms)
+    mp.start_processes(_run, args=(2, _free_port(), out, with_atoms), nprocs=2,
+                       start_method="spawn")
     one = np.load(out.format(rank=0, world=1))
+    keys = ("E", "gamma", "g_quat", "g_log_scale", "g_centers", "g_C") + (("E_ne",) if with_atoms else ())
     for r in range(2):
         two = np.load(out.format(rank=r, world=2))
-        for k in ("E", "gamma", "g_quat", "g_log_scale", "g_centers", "g_C"):
+        for k in keys:
             np.testing.assert_allclose(two[k], one[k], rtol=1e-12, atol=1e-12 * np.abs(one[k]).max())
+    if with_atoms:
+        # the whole-system E_ne and gradient of E_J + E_ne against the oracle's separate terms
+        s, pi, pj, v, aq, L = _problem()
+        arr = (s.quat, s.log_scale, s.centers, s.C_occ, s.occ)
+        rj = O.energy_and_grad(arr, aq, L, pi, pj, v)
+        rn = O.external_energy_and_grad(arr, pi, pj, v, s.atoms, s.charges)
+        np.testing.assert_allclose(float(one["E_ne"][0]), rn["E"], rtol=1e-12)
+        for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
+            want = rj[k] + rn[k]
+            np.testing.assert_allclose(one[k], want, rtol=1e-10, atol=1e-12 * np.abs(want).max())
