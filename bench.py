@@ -37,6 +37,10 @@ FP64_DATASHEET = 37e12
 # workload has a capture; other configs and N > 1 report null.
 NCU_TRAFFIC_CFG1_N1 = {"j_vjp_kernel": 22.364160e6 + 65.776128e6, "j_forward_kernel": 21.477120e6}
 L2_FLUSH_BYTES = 256 << 20
+# FP64 work per (pair, atom) unit of the screened nuclear attraction kernel with its reverse sums,
+# counted from gsdft_vne's operations (FMA = 2): 20 nodes x 50, y and m in two node passes 48, the
+# per-atom epilogue 41 (the per-pair node constants, amortised over the atoms, are not counted).
+FLOP_VNE = 1089
 
 
 def parse():
@@ -302,6 +306,10 @@ def main():
                           barrier)
 
     peak = dfma_peak(torch, lib, ptr, stream_handle)
+    vne = None
+    if world == 1:
+        vne = measure_vne(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush,
+                          peak, args)
     del graph                 # release every CUDA graph before the process group goes away
     torch.cuda.synchronize()
     if world > 1:
@@ -358,9 +366,46 @@ def main():
     }
     if e2e is not None:
         line["e2e"] = e2e
+    if vne is not None:
+        line["next_rows"] = {"vne": vne}
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def measure_vne(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush, peak, args):
+    """The screened nuclear attraction on the same pair list (not part of the metric): value and
+    reverse-pass sums in one gsdft_vne call, device-timed with CUDA events on the launching stream,
+    L2 flushed between launches outside the events."""
+    from gs_dft_b200.coulomb.engine import RIJEngine
+    from gs_dft_b200.screening import atom_records, pair_weight
+    atoms = atom_records(sy.atoms, sy.charges, quat.device)
+    eng = RIJEngine(pi, pj, pair_weight(valid).contiguous(), sy.M, sy.n_occ, atoms=atoms)
+    eng.prepare(quat, log_scale, centers, C, occ)
+    for _ in range(3):
+        eng.external(sums=True)
+    torch.cuda.synchronize()
+    K = max(5, min(args.steps, 30))
+    total = 0.0
+    for k in range(K):
+        flush.fill_(float(k))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        eng.external(sums=True)
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    ms = total / K
+    units = eng.plan.n_rep * eng.n_atoms
+    flops = FLOP_VNE * units / (ms * 1e-3)
+    return {"what": "screened V_ne on the pair list, value + reverse-pass sums (gsdft_vne: "
+                    "vne_kernel + vne_sum), not part of the metric",
+            "ms": ms, "launches_timed": K, "atoms": eng.n_atoms,
+            "evaluated_pairs": eng.plan.n_rep, "units": "(pair, atom)",
+            "units_per_s": units / (ms * 1e-3), "flop_per_unit": FLOP_VNE,
+            "achieved_tflops": flops / 1e12, "frac_of_measured_fp64_peak": flops / peak,
+            "E_ne": float(eng.E_ne[0])}
 
 
 def _launches_per_step(lib, step, torch):
