@@ -419,9 +419,11 @@ def energy(sys_arrays, aux_q, L, pi, pj, valid, chunk=2048):
 # ----------------------------------------------------------------------------------------------
 
 
-def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa):
+def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa, W=None):
     """For each pair: J_a = sum_P (P|a) d_P and the cotangents of (A_hat, P_a, KN_a) of
     E = sum_P d_P sum_a (P|a) q_a, without the 1/(lambda_i - lambda_j) terms of an eigh VJP.
+    With ``W`` (N_aux, B) the cotangents are those of E = sum_{P,a} W[P,a] (P|a) instead
+    (dvec and qa unused; J returned as zeros).
 
     Per node, f = w det(G)^-1/2 exp(-t^2 beta d^T A_hat G^-1 d) with G = (beta+t^2) A_hat + t^2 beta I:
       df/dA_hat = f (-1/2 (beta+t^2) G^-1 - t^4 beta^2 z z^T),  z = G^-1 d
@@ -447,16 +449,21 @@ def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa):
         Dk += (f * s)[..., None] * invG
         Zkl += (f * t2 * t2 * b * b)[..., None, None] * z[..., :, None] * z[..., None, :]
         Vk += (f * t2 * b)[..., None] * Lam[None] * z
-    c = dvec[:, None] * KN_aux[:, None] * (KN_pair * PREF)[None, :]   # d_P KN_P KN_a pref
-    J = np.sum(c * coul, axis=0)
-    cq = c * qa[None, :]
+    if W is not None:
+        cq = W * KN_aux[:, None] * (KN_pair * PREF)[None, :]          # W_Pa KN_P KN_a pref
+        J = np.zeros(KN_pair.shape[0])
+        KNbar = np.sum(W * KN_aux[:, None] * PREF * coul, axis=0)
+    else:
+        c = dvec[:, None] * KN_aux[:, None] * (KN_pair * PREF)[None, :]   # d_P KN_P KN_a pref
+        J = np.sum(c * coul, axis=0)
+        cq = c * qa[None, :]
+        KNbar = qa * np.sum(dvec[:, None] * KN_aux[:, None] * PREF * coul, axis=0)
     Mk = -0.5 * np.sum(cq[..., None] * Dk, axis=0)                     # (B,3) diagonal part
     Mkl = -np.sum(cq[..., None, None] * Zkl, axis=0)                   # (B,3,3)
     Mkl[:, [0, 1, 2], [0, 1, 2]] += Mk
     Abar = np.einsum("bik,bkl,bjl->bij", U, Mkl, U)
     Pbar_eig = 2.0 * np.sum(cq[..., None] * Vk, axis=0)                # (B,3) eigenframe
     Pbar = np.einsum("bik,bk->bi", U, Pbar_eig)
-    KNbar = qa * np.sum(dvec[:, None] * KN_aux[:, None] * PREF * coul, axis=0)
     return J, Abar, Pbar, KNbar
 
 
@@ -565,6 +572,78 @@ def _scatter_pair_grads(qs, ci, cj, cw, Jc, Abar, Pbar, KNbar, C_occ, occ, gA, g
     s = (Jc * cw)[:, None] * occ[None, :]
     np.add.at(gC, ci, s * C_occ[cj])
     np.add.at(gC, cj, s * C_occ[ci])
+
+# ----------------------------------------------------------------------------------------------
+#  Screened RI-K  (gs_dft/coulomb/ri.py:497-544)
+# ----------------------------------------------------------------------------------------------
+
+
+def _exchange_D(q_splat, C, aux_q, pi, pj, valid, chunk=1024):
+    """D[P,o,o'] = sum_{live (i,k)} (P|ik) C_io C_ko' over the listed pairs (``valid`` a 0/1 mask,
+    as the reference's ``cv & ov`` requires) (gs_dft/coulomb/ri.py:496-526)."""
+    beta, R, KN = aux_q
+    n = pi.shape[0]
+    live_all = np.ones(n, bool) if valid is None else (np.asarray(valid) != 0)
+    D = np.zeros((beta.shape[0], C.shape[1], C.shape[1]))
+    for a in range(0, n, chunk):
+        sl = slice(a, a + chunk)
+        live = live_all[sl]
+        if not np.any(live):
+            continue
+        ci, cj = pi[sl][live], pj[sl][live]
+        blk = full_isobra_block(beta, R, KN, *full_pair_quantities(q_splat, ci, cj))
+        D += np.einsum("Ap,po,pq->Aoq", blk, C[ci], C[cj])
+    return D
+
+
+def exchange_energy_screened(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024):
+    """E_K = -tr((V + lam I)^-1 M), M_PQ = sum_{o,o'} D[P,o,o'] D[Q,o,o']
+    (gs_dft/coulomb/ri.py:529-544; ``sys_arrays`` = (quat, log_scale, centers, C_occ, occ), occ
+    unused as in the reference). Returns (E_K, D)."""
+    quat, log_scale, centers, C = sys_arrays[:4]
+    q = full_quantities(quat, log_scale, centers)
+    D = _exchange_D(q, C, aux_q, pi, pj, valid, chunk)
+    Vs = aux_metric(*aux_q)
+    Vs[np.diag_indices_from(Vs)] += lam
+    Mm = np.einsum("Aoq,Boq->AB", D, D)
+    return -float(np.trace(np.linalg.solve(Vs, Mm))), D
+
+
+def exchange_energy_and_grad(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024):
+    """E_K and its gradient with respect to (quat, log_scale, centers, C_occ), aux and pairs frozen.
+    With Y = (V + lam I)^-1 D: dE/dD = -2 Y, dE/d(P|a) = -2 C_i^T Y_P C_k, and dE/dC from D's
+    bilinear dependence on C_i, C_k."""
+    quat, log_scale, centers, C = sys_arrays[:4]
+    qs = full_quantities(quat, log_scale, centers)
+    E, D = exchange_energy_screened(sys_arrays, aux_q, lam, pi, pj, valid, chunk)
+    beta, R, KN_aux = aux_q
+    Vs = aux_metric(*aux_q)
+    Vs[np.diag_indices_from(Vs)] += lam
+    nA, no = D.shape[0], D.shape[1]
+    Ybar = -2.0 * np.linalg.solve(Vs, D.reshape(nA, no * no)).reshape(nA, no, no)
+    M = centers.shape[0]
+    gA, gmu, gN = np.zeros((M, 3, 3)), np.zeros((M, 3)), np.zeros(M)
+    gC = np.zeros_like(C)
+    n = pi.shape[0]
+    live_all = np.ones(n, bool) if valid is None else (np.asarray(valid) != 0)
+    for a in range(0, n, chunk):
+        sl = slice(a, a + chunk)
+        live = live_all[sl]
+        if not np.any(live):
+            continue
+        ci, cj = pi[sl][live], pj[sl][live]
+        Ah, Pa, KNa = full_pair_quantities(qs, ci, cj)
+        blk = full_isobra_block(beta, R, KN_aux, Ah, Pa, KNa)               # (N_aux, c)
+        W = np.einsum("po,Aoq,pq->Ap", C[ci], Ybar, C[cj])                  # dE/d(P|a)
+        _, Abar, Pbar, KNbar = _pair_vjp_integral(beta, R, KN_aux, None, Ah, Pa, KNa, None, W=W)
+        _scatter_pair_grads(qs, ci, cj, np.ones(ci.shape[0]), np.zeros(ci.shape[0]), Abar, Pbar,
+                            KNbar, C, np.zeros(C.shape[1]), gA, gmu, gN, gC)
+        T = np.einsum("Ap,Aoq->poq", blk, Ybar)                             # dE/dX[a,o,o']
+        np.add.at(gC, ci, np.einsum("poq,pq->po", T, C[cj]))
+        np.add.at(gC, cj, np.einsum("poq,po->pq", T, C[ci]))
+    g_quat, g_log = chart_vjp(quat, log_scale, gA, gN)
+    return dict(E=E, D=D, g_quat=g_quat, g_log_scale=g_log, g_centers=gmu, g_C=gC, gA=gA,
+                gmu=gmu, gN=gN)
 
 # ----------------------------------------------------------------------------------------------
 #  Screened nuclear attraction on the pair list  (gs_dft/screening/pairs.py:348-370, 403-440)

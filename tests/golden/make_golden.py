@@ -21,7 +21,11 @@ Outputs (compressed .npz, a few hundred KB in all):
     (``screened_external_energy``) for the three systems, and the gradient of E_ext by
     Richardson-extrapolated central differences of the executed reference on a 10-splat system.
 
-``python tests/golden/make_golden.py vne`` regenerates only ``ref_vne.npz``.
+  * ``ref_k.npz``       — screened RI-K: E_K (``df_exchange_energy_screened``) on the padded ordered
+    list of the three systems, and its gradient by Richardson central differences of the executed
+    reference on the 10-splat system.
+
+``python tests/golden/make_golden.py vne`` (or ``k``) regenerates only that file.
 """
 from __future__ import annotations
 
@@ -195,12 +199,60 @@ def make_vne(eps=1e-7):
     print("vne grad: M=10 E_ext=", out["grad_E"])
 
 
+def make_k(eps=1e-7, lam=1e-8):
+    spec, iso, pairs, ri = _modules()
+    out = {}
+    for name, s in _cases().items():
+        sp = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+        pi, pj, _ = pairs.neighbor_pairs(sp, eps=eps)
+        n = int(pi.shape[0])
+        pi2, pj2, v2 = pairs.neighbor_pairs(sp, eps=eps, pad_to=n + 37)
+        aux = iso.init_product_aux(sp)
+        out[f"{name}_E_K"] = float(ri.df_exchange_energy_screened(sp, J(s.C_occ), aux, pi2, pj2,
+                                                                   lam=lam, chunk=512, valid=v2))
+        print(f"k {name}: E_K={out[f'{name}_E_K']:.15g}")
+
+    s = small_random_system(10, 3, seed=3, spread=1.0, n_atoms=3)
+    sp0 = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+    pi, pj, v = pairs.neighbor_pairs(sp0, eps=eps)
+    aux = iso.init_product_aux(sp0)
+
+    def energy(quat, ls, cen, C):
+        sp = spec.Splat(quat=J(quat), log_scale=J(ls), centers=J(cen))
+        return float(ri.df_exchange_energy_screened(sp, J(C), aux, pi, pj, lam=lam, chunk=64,
+                                                    valid=v))
+
+    x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy()]
+
+    def fd(k, h):
+        g = np.zeros_like(x0[k])
+        for idx in np.ndindex(x0[k].shape):
+            xp = [a.copy() for a in x0]
+            xm = [a.copy() for a in x0]
+            xp[k][idx] += h
+            xm[k][idx] -= h
+            g[idx] = (energy(*xp) - energy(*xm)) / (2 * h)
+        return g
+
+    out.update(grad_quat=s.quat, grad_log_scale=s.log_scale, grad_centers=s.centers,
+               grad_C_occ=s.C_occ, grad_occ=s.occ, grad_E_K=energy(*x0), eps=eps, lam=lam)
+    for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
+        h = 1e-3
+        out["grad_" + name] = (4 * fd(k, h / 2) - fd(k, h)) / 3      # Richardson, O(h^4)
+    np.savez_compressed(os.path.join(HERE, "ref_k.npz"), **out)
+    print("k grad: M=10 E_K=", out["grad_E_K"])
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["vne"]:
         make_vne()
+        sys.exit(0)
+    if sys.argv[1:] == ["k"]:
+        make_k()
         sys.exit(0)
     for name, s in _cases().items():
         make_case(name, s)
     make_grad()
     make_nodes_bwd()
     make_vne()
+    make_k()
