@@ -38,20 +38,25 @@ __global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const doubl
   if (P >= n) return;
   double b = beta[P];
   double g = gE ? gE[0] : 1.0;
+  double dP = d ? d[P] : 1.0;
   double* o = out + P * kAuxRec;
   o[0] = b;
   o[1] = -kLog2e * b;
   o[2] = R[3 * P];
   o[3] = R[3 * P + 1];
   o[4] = R[3 * P + 2];
-  o[5] = (g * d[P]) * KN[P];
+  o[5] = (g * dP) * KN[P];
   o[6] = b * b;
   o[7] = 0.0;
 }
 
+// kW: the per-(P,a) weight of the reverse pass is W[a * ldw + P] x (the aux record's dbar KN)
+// (E = sum_{P,a} W[a][P] (P|a), as the RI-K gradient needs); without it the weight is dbar_P KN_P.
+template <bool kW>
 __global__ void GSDFT_VJP_BOUNDS
     j_vjp_kernel(const double* __restrict__ rec, int64_t n_live, const double* __restrict__ auxr,
-                 int64_t n_aux, int64_t per_split, double* __restrict__ out) {
+                 int64_t n_aux, int64_t per_split, double* __restrict__ out,
+                 const double* __restrict__ Wt, int64_t ldw) {
   __shared__ __align__(128) double tile[2][kVjpTile * kAuxRec];
   __shared__ __align__(8) uint64_t bar[2];
   extern __shared__ __align__(16) double etab[];  // GSDFT_NQUAD x 2^kVjpBits weighted table
@@ -101,7 +106,9 @@ __global__ void GSDFT_VJP_BOUNDS
     // a warp with no live pair (the tail of the last pair tile) only takes part in the barriers
     for (int k = 0; warp_active && k < cnt; ++k) {
       const double* ar = tl + k * kAuxRec;
-      const double b = ar[0], cP = ar[1], dk = ar[5], b2 = ar[6];
+      const double b = ar[0], cP = ar[1], b2 = ar[6];
+      double dk = ar[5];
+      if constexpr (kW) dk *= Wt[aa * ldw + (P0 + (int64_t)t * kVjpTile + k)];
       const double d0 = ar[2] - Pc[0], d1 = ar[3] - Pc[1], d2 = ar[4] - Pc[2];
       double y[3], m[3];
 #pragma unroll
@@ -449,12 +456,14 @@ static int vjp_num_sms() {
 
 // Aux splits: pair tiles x S CTAs filling whole waves of resident CTAs (S <= 8, since the partial
 // sums take S x n_live x 13 doubles).
+template <bool kW>
 static int vjp_splits(int64_t n_live, int64_t n_aux) {
   static int per_sm = 0;
   if (!per_sm) {
-    cudaFuncSetAttribute(j_vjp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(j_vjp_kernel<kW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kVjpDynSmem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, j_vjp_kernel, kVjpThreads, kVjpDynSmem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, j_vjp_kernel<kW>, kVjpThreads,
+                                                  kVjpDynSmem);
     if (per_sm <= 0) per_sm = 1;
   }
   int64_t tiles = (n_live + kVjpThreads - 1) / kVjpThreads;
@@ -476,22 +485,22 @@ int device_status_vjp(int* out, int clear) {
 
 using namespace gsdft;
 
-extern "C" size_t gsdft_j_vjp_workspace_size(int64_t n_live, int64_t n_aux) {
-  int S = vjp_splits(n_live, n_aux);
+namespace gsdft {
+template <bool kW>
+static size_t vjp_workspace_size(int64_t n_live, int64_t n_aux) {
+  int S = vjp_splits<kW>(n_live, n_aux);
   Sizer z;
   z.take<double>((size_t)n_aux * kAuxRec);
   if (S > 1) z.take<double>((size_t)S * n_live * GSDFT_VJP_FIELDS);
   return z.off + 256;
 }
 
-extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta, const double* R,
-                           const double* KN, const double* d, const double* g_E, int64_t n_aux,
-                           double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
-  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31), "bad sizes");
-  if (n_live == 0) return GSDFT_OK;
-  GSDFT_REQUIRE(rec && beta && R && KN && d && sums, "null pointer");
-  cudaStream_t st = (cudaStream_t)stream;
-  int S = vjp_splits(n_live, n_aux);
+template <bool kW>
+static int vjp_run(const double* rec, int64_t n_live, const double* beta, const double* R,
+                   const double* KN, const double* d, const double* g_E, const double* Wt,
+                   int64_t ldw, int64_t n_aux, double* sums, void* ws, size_t ws_bytes,
+                   cudaStream_t st) {
+  int S = vjp_splits<kW>(n_live, n_aux);
   Carver c(ws, ws_bytes);
   double* auxr = c.take<double>((size_t)n_aux * kAuxRec);
   double* part = S > 1 ? c.take<double>((size_t)S * n_live * GSDFT_VJP_FIELDS) : sums;
@@ -500,7 +509,8 @@ extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta
   GSDFT_LAUNCHED("aux_vjp_pack");
   int64_t per_split = (n_aux + S - 1) / S;
   dim3 grid((unsigned)((n_live + kVjpThreads - 1) / kVjpThreads), (unsigned)S);
-  j_vjp_kernel<<<grid, kVjpThreads, kVjpDynSmem, st>>>(rec, n_live, auxr, n_aux, per_split, part);
+  j_vjp_kernel<kW><<<grid, kVjpThreads, kVjpDynSmem, st>>>(rec, n_live, auxr, n_aux, per_split,
+                                                            part, Wt, ldw);
   GSDFT_LAUNCHED("j_vjp");
   if (S > 1) {
     sum_vjp_splits_kernel<<<grid_1d(n_live * GSDFT_VJP_FIELDS, 256), 256, 0, st>>>(part, S, n_live,
@@ -508,6 +518,37 @@ extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta
     GSDFT_LAUNCHED("sum_vjp_splits");
   }
   return GSDFT_OK;
+}
+}  // namespace gsdft
+
+extern "C" size_t gsdft_j_vjp_workspace_size(int64_t n_live, int64_t n_aux) {
+  return vjp_workspace_size<false>(n_live, n_aux);
+}
+
+extern "C" int gsdft_j_vjp(const double* rec, int64_t n_live, const double* beta, const double* R,
+                           const double* KN, const double* d, const double* g_E, int64_t n_aux,
+                           double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31), "bad sizes");
+  if (n_live == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(rec && beta && R && KN && d && sums, "null pointer");
+  return vjp_run<false>(rec, n_live, beta, R, KN, d, g_E, nullptr, 0, n_aux, sums, ws, ws_bytes,
+                        (cudaStream_t)stream);
+}
+
+extern "C" size_t gsdft_j_vjp_weighted_workspace_size(int64_t n_live, int64_t n_aux) {
+  return vjp_workspace_size<true>(n_live, n_aux);
+}
+
+extern "C" int gsdft_j_vjp_weighted(const double* rec, int64_t n_live, const double* beta,
+                                    const double* R, const double* KN, const double* Wt,
+                                    int64_t ldw, int64_t n_aux, double* sums, void* ws,
+                                    size_t ws_bytes, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31) && ldw >= n_aux,
+                "bad sizes");
+  if (n_live == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(rec && beta && R && KN && Wt && sums, "null pointer");
+  return vjp_run<true>(rec, n_live, beta, R, KN, nullptr, nullptr, Wt, ldw, n_aux, sums, ws,
+                       ws_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,

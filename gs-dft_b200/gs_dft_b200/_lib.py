@@ -72,6 +72,16 @@ SIGNATURES = {
     "gsdft_vne": (_i32, [_c_p, _i64, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i32,
                          _c_p, _sz, _c_p]),
     "gsdft_density_pairs": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _i64, _c_p, _c_p]),
+    "gsdft_j_vjp_weighted_workspace_size": (_sz, [_i64, _i64]),
+    "gsdft_j_vjp_weighted": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _sz,
+                                    _c_p]),
+    "gsdft_k_workspace_size": (_sz, [_i64, _i64, _i64]),
+    "gsdft_k_forward": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p,
+                               _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_k_backward": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p,
+                                _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64,
+                                _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_k_unit_q": (_i32, [_c_p, _i64, _c_p, _c_p]),
     "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
                                   _i64, _c_p, _c_p]),
 }

@@ -46,6 +46,7 @@ class SplatState:
     cholV: torch.Tensor | None = None
     _engine: RIJEngine | None = field(default=None, repr=False)
     _ext_engine: RIJEngine | None = field(default=None, repr=False)
+    _k_engine: object | None = field(default=None, repr=False)
 
     def engine_for(self, basis, C_occ) -> RIJEngine:
         """The device engine for this state's pairs/aux/factor (built once, reused per step)."""
@@ -56,6 +57,16 @@ class SplatState:
                                      pair_weight(valid).contiguous(), basis.n_basis,
                                      int(C_occ.shape[1]), beta, R.contiguous(), KN, self.cholV)
         return self._engine
+
+    def k_engine_for(self, basis, C_occ):
+        """The device engine of the screened RI-K term on this state's pairs/aux/factor."""
+        if self._k_engine is None:
+            from ..coulomb.exchange import RIKEngine
+            pi, pj, valid = self.pairs
+            beta, R, KN = self.aux.quantities()
+            self._k_engine = RIKEngine(pi, pj, valid, basis.n_basis, int(C_occ.shape[1]), beta,
+                                       R, KN, self.cholV)
+        return self._k_engine
 
     def external_engine_for(self, basis, C_occ, atoms) -> RIJEngine:
         """The device engine of the screened external term on this state's pairs (built once)."""
@@ -93,14 +104,15 @@ class CoulombKS:
     ``ks(model, state) -> E_J`` (differentiable in the model's splats and C)."""
 
     def __init__(self, *, coulomb: DFSpec | None = None, screen: Pairlist | None = None,
-                 n_devices: int = 1):
+                 n_devices: int = 1, hf_coeff: float = 0.0):
         coulomb = coulomb or DFSpec()
         if not isinstance(coulomb, DFSpec):
             raise TypeError(f"coulomb must come from df(), got {coulomb!r}")
         if screen is None:
             raise ValueError("the B200 RI-J path is the screened path: pass screen=pairlist(...)")
         self.screen = screen
-        self.coulomb = ScreenedProductDFCoulomb.from_spec(coulomb, skip_pad=screen.skip_pad)
+        self.coulomb = ScreenedProductDFCoulomb.from_spec(coulomb, skip_pad=screen.skip_pad,
+                                                          hf_coeff=hf_coeff)
         self.n_devices = int(n_devices)
 
     def initial_pad(self, basis: Splat) -> int:
@@ -112,6 +124,13 @@ class CoulombKS:
             raise ValueError("coulomb=df() needs the refresh state: see refresh(ks, basis).")
         e_j, _ = self.coulomb.energy(model.basis, model.C, None, model.occupations, state)
         return e_j
+
+    def energy(self, model: SplatModel, state: SplatState):
+        """(E_J, E_K) as ``ScreenedProductDFCoulomb.energy`` returns them (E_K = 0 unless the
+        builder was given ``hf_coeff != 0``)."""
+        if state is None or state.pairs is None or state.aux is None:
+            raise ValueError("coulomb=df() needs the refresh state: see refresh(ks, basis).")
+        return self.coulomb.energy(model.basis, model.C, None, model.occupations, state)
 
 
 class ExternalKS:

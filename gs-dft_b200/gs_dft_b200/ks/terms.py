@@ -48,29 +48,34 @@ def pairlist(eps: float = 1e-7, *, pad: float = SCREEN_PAD, unique: bool = False
 
 
 class ScreenedProductDFCoulomb:
-    """Frozen pair-product RI-J over the significant pairs only.
+    """Frozen pair-product RI-J (+ RI-K for hybrids) over the significant pairs only.
 
-    ``energy(basis, C_orth, P, occ, state) -> (E_J, E_K)`` like the reference. Exact exchange
-    (RI-K, for hybrids) is not on the B200 path: ``hf_coeff != 0`` raises.
+    ``energy(basis, C_orth, P, occ, state) -> (E_J, E_K)`` like the reference
+    (gs_dft/ks/terms.py:236-256): E_K from ``df_exchange_energy_screened`` on the same pairs and
+    aux (the reference's aux_K is the same product basis, gs_dft/ks/energy.py:468) when
+    ``hf_coeff != 0``, else 0. Range-separated exchange (``energy_lr``) is not on the B200 path.
     """
 
     def __init__(self, hf_coeff: float = 0.0, lam: float = 1e-8, chunk: int = 2048,
                  scales: tuple = (1.0,), diagonal: bool = True, skip_pad: bool = False):
-        if hf_coeff != 0.0:
-            raise NotImplementedError("screened RI-K (hybrid exchange) is not on the B200 path")
-        self.hf_coeff = 0.0
+        self.hf_coeff = float(hf_coeff)
         self.lam, self.chunk = float(lam), int(chunk)
         self.scales, self.diagonal = tuple(scales), bool(diagonal)
         self.skip_pad = bool(skip_pad)
 
     @classmethod
-    def from_spec(cls, spec: DFSpec, skip_pad: bool = False):
-        return cls(lam=spec.lam, chunk=spec.chunk, scales=spec.scales, diagonal=spec.diagonal,
-                   skip_pad=skip_pad)
+    def from_spec(cls, spec: DFSpec, skip_pad: bool = False, hf_coeff: float = 0.0):
+        return cls(hf_coeff=hf_coeff, lam=spec.lam, chunk=spec.chunk, scales=spec.scales,
+                   diagonal=spec.diagonal, skip_pad=skip_pad)
 
     def energy(self, basis, C_orth, P, occ, state):
         from ..coulomb.ri import _ScreenedDFEnergy
         eng = state.engine_for(basis, C_orth)
         e_j = _ScreenedDFEnergy.apply(basis.quat, basis.log_scale, basis.centers, C_orth,
                                       occ, eng)
-        return e_j, torch.zeros((), dtype=e_j.dtype, device=e_j.device)
+        if self.hf_coeff == 0.0:
+            return e_j, torch.zeros((), dtype=e_j.dtype, device=e_j.device)
+        from ..coulomb.exchange import _ScreenedDFExchange
+        keng = state.k_engine_for(basis, C_orth)
+        e_k = _ScreenedDFExchange.apply(basis.quat, basis.log_scale, basis.centers, C_orth, keng)
+        return e_j, e_k

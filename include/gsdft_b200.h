@@ -287,6 +287,43 @@ int gsdft_vne(const double* rec, int64_t n_rep, const double* atoms, int64_t n_a
 int gsdft_density_pairs(const int32_t* pi, const int32_t* pj, int64_t n, const double* C_occ,
                         const double* occ, int64_t n_occ, double* P, gsdft_stream_t stream);
 
+/* The reverse pass of E = sum_{P,a} W[a][P] (P|a): gsdft_j_vjp with a per-(aux, pair) weight matrix
+ * Wt (n_rep rows of leading dimension ldw >= n_aux) instead of dbar_P q_a; the sums then go to
+ * gsdft_pair_chain with records whose q is 1 (gsdft_k_unit_q). Used by the RI-K gradient (the
+ * reference differentiates gs_dft/coulomb/ri.py:497-544 with JAX autodiff). */
+size_t gsdft_j_vjp_weighted_workspace_size(int64_t n_rep, int64_t n_aux);
+int gsdft_j_vjp_weighted(const double* rec, int64_t n_rep, const double* beta, const double* R,
+                         const double* KN, const double* Wt, int64_t ldw, int64_t n_aux,
+                         double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream);
+
+/* Screened RI-K over the pair representatives: D[P,o,o'] = sum_{live (i,k)} (P|ik) C_io C_ko',
+ * E_K = -tr((V + lam I)^-1 D D^T) = -|L^-1 D|^2 (replaces _exchange_M_streamed_screened and
+ * df_exchange_energy_screened, gs_dft/coulomb/ri.py:497-544, for omega = None). The pair list must
+ * be an ordered 0/1 list (the reference masks with valid & occupied); a merged transposed twin adds
+ * C_ko C_io'. Writes Z = L^-1 D (n_aux x n_occ^2, row-major; kept for the backward) and E (device
+ * scalar). The workspace (gsdft_k_workspace_size: 8 n_rep (n_aux + 2 n_occ^2) bytes and more) holds
+ * the integral block and the products between forward and backward: pass the same, untouched
+ * workspace to gsdft_k_backward. */
+size_t gsdft_k_workspace_size(int64_t n_rep, int64_t n_aux, int64_t n_occ);
+int gsdft_k_forward(const double* rec, const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
+                    const int32_t* rep_twin, int64_t n_rep, const double* beta, const double* R,
+                    const double* KN, int64_t n_aux, const double* L, const double* C_occ,
+                    int64_t n_occ, double* Z, double* E, void* ws, size_t ws_bytes,
+                    gsdft_stream_t stream);
+/* Gradient of g_E * E_K (g_E a device scalar, NULL = 1): the reverse-pass sums (for gsdft_pair_chain
+ * with gsdft_k_unit_q records) and g_C (M x n_occ, written). Groupings and partners from
+ * gsdft_pair_groups. Deterministic. */
+int gsdft_k_backward(const double* rec, const int32_t* pi, const int32_t* pj,
+                     const int32_t* rep_pos, const int32_t* rep_twin, int64_t n_rep,
+                     const double* beta, const double* R, const double* KN, int64_t n_aux,
+                     const double* L, const double* C_occ, int64_t n_occ, const double* Z,
+                     const double* g_E, const int32_t* order_i, const int64_t* seg_i,
+                     const int32_t* partner_i, const int32_t* order_j, const int64_t* seg_j,
+                     const int32_t* partner_j, int64_t M, double* sums, double* g_C, void* ws,
+                     size_t ws_bytes, gsdft_stream_t stream);
+/* rec_out = rec with q = 1 (Q = 1, QK = KN pref), for the chain of a weighted reverse pass. */
+int gsdft_k_unit_q(const double* rec, int64_t n_rep, double* rec_out, gsdft_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
