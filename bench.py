@@ -306,10 +306,16 @@ def main():
                           barrier)
 
     peak = dfma_peak(torch, lib, ptr, stream_handle)
-    vne = None
+    next_rows = None
     if world == 1:
-        vne = measure_vne(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush,
-                          peak, args)
+        # rows beyond the metric, measured after it; a failure here is recorded, never fatal
+        next_rows = {}
+        for name, fn in (("vne", measure_vne), ("k", measure_k)):
+            try:
+                next_rows[name] = fn(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C,
+                                     occ, flush, peak, args, aux=aux, L=L)
+            except Exception as exc:          # noqa: BLE001 - reported in the JSON line
+                next_rows[name] = {"error": f"{type(exc).__name__}: {exc}"}
     del graph                 # release every CUDA graph before the process group goes away
     torch.cuda.synchronize()
     if world > 1:
@@ -366,14 +372,15 @@ def main():
     }
     if e2e is not None:
         line["e2e"] = e2e
-    if vne is not None:
-        line["next_rows"] = {"vne": vne}
+    if next_rows:
+        line["next_rows"] = next_rows
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
 
 
-def measure_vne(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush, peak, args):
+def measure_vne(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush, peak, args,
+                **_):
     """The screened nuclear attraction on the same pair list (not part of the metric): value and
     reverse-pass sums in one gsdft_vne call, device-timed with CUDA events on the launching stream,
     L2 flushed between launches outside the events."""
@@ -406,6 +413,41 @@ def measure_vne(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, f
             "units_per_s": units / (ms * 1e-3), "flop_per_unit": FLOP_VNE,
             "achieved_tflops": flops / 1e12, "frac_of_measured_fp64_peak": flops / peak,
             "E_ne": float(eng.E_ne[0])}
+
+
+def measure_k(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush, peak, args,
+              aux=None, L=None):
+    """Screened RI-K on the same pair list and aux (not part of the metric): E_K and its full
+    gradient per step (RIKEngine.step), device-timed with CUDA events, L2 flushed between steps."""
+    beta, R, KN = aux.quantities()
+    eng = g.RIKEngine(pi, pj, valid, sy.M, sy.n_occ, beta, R, KN, L)
+    for _ in range(2):
+        eng.step(quat, log_scale, centers, C)
+    torch.cuda.synchronize()
+    K = max(3, min(args.steps, 10))
+    total = 0.0
+    for k in range(K):
+        flush.fill_(float(k))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        eng.step(quat, log_scale, centers, C)
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    ms = total / K
+    n_aux, n_rep, K2 = eng.n_aux, eng.plan.n_rep, sy.n_occ * sy.n_occ
+    integrals = n_aux * n_rep
+    # integral block (forward integrand) + weighted reverse pass + the three n_aux x n_rep x K2 GEMMs
+    flop = integrals * (FLOP_FWD + FLOP_VJP) + 3 * 2.0 * integrals * K2
+    return {"what": "screened RI-K on the pair list: E_K + full gradient per step (integral "
+                    "block, orbital products, cuBLAS DGEMM x 3 + trsm, weighted reverse pass, "
+                    "chain), not part of the metric",
+            "ms_per_step": ms, "steps_timed": K, "evaluated_pairs": n_rep, "n_aux": n_aux,
+            "n_occ": sy.n_occ, "integrals_per_s": integrals / (ms * 1e-3),
+            "flop_per_step": flop, "achieved_tflops": flop / (ms * 1e-3) / 1e12,
+            "frac_of_measured_fp64_peak": flop / (ms * 1e-3) / peak,
+            "E_K": float(eng.E[0]), "workspace_bytes": eng.ws_bytes}
 
 
 def _launches_per_step(lib, step, torch):
