@@ -574,6 +574,55 @@ def _scatter_pair_grads(qs, ci, cj, cw, Jc, Abar, Pbar, KNbar, C_occ, occ, gA, g
     np.add.at(gC, cj, s * C_occ[ci])
 
 # ----------------------------------------------------------------------------------------------
+#  Screened exact (pair|pair) Coulomb  (gs_dft/coulomb/stream.py:249-320)
+# ----------------------------------------------------------------------------------------------
+
+
+def eri_block_schur(q_splat, bi, bj, ki, kj):
+    """(a|b) for bra pairs (bi, bj) x ket pairs (ki, kj) through the Schur complement of the 6x6
+    precision G = [[X, -t^2 I], [-t^2 I, Y]], X = A_a + t^2 I, Y = A_b + t^2 I, S = Y - t^4 X^-1:
+    det G = det X det S, v^T G^-1 v = v_a.u + w.S^-1 w, u = X^-1 v_a, w = t^2 u + v_b
+    (gs_dft/coulomb/stream.py:249-283)."""
+    Aa, Pa, KNa = full_pair_quantities(q_splat, bi, bj)
+    Ab, Pb, KNb = full_pair_quantities(q_splat, ki, kj)
+    va = matvec3(Aa, Pa)
+    vb = matvec3(Ab, Pb)
+    cv = np.sum(Pa * va, -1)[:, None] + np.sum(Pb * vb, -1)[None, :]
+    eye = np.eye(3)
+    coul = np.zeros((Aa.shape[0], Ab.shape[0]))
+    for t, wq in zip(QUAD_T, QUAD_W):
+        t2 = t * t
+        X = Aa + t2 * eye
+        Xinv = adj3(X) / det3(X)[:, None, None]
+        u = matvec3(Xinv, va)
+        vau = np.sum(va * u, -1)
+        Y = Ab + t2 * eye
+        S = Y[None, :] - (t2 * t2) * Xinv[:, None]
+        w = t2 * u[:, None, :] + vb[None, :, :]
+        z = solve3(S, w)
+        quad = cv - (vau[:, None] + np.sum(w * z, -1))
+        detG = det3(X)[:, None] * det3(S)
+        coul = coul + wq * (2.0 / math.sqrt(PI)) * (PI ** 3 / np.sqrt(detG) * np.exp(-quad))
+    return (KNa[:, None] * KNb[None, :]) * coul
+
+
+def screened_coulomb_energy_exact(sys_arrays, pi, pj, valid, bra_chunk=128):
+    """Exact E_J = 1/2 sum_{a,b} P_a P_b (a|b) over the listed pairs, P_a = valid_a sum_o occ_o
+    C_io C_jo (gs_dft/coulomb/stream.py:294-320). Returns (E, Jvec) with Jvec_a = sum_b (a|b) P_b."""
+    quat, log_scale, centers, C, occ = sys_arrays
+    q = full_quantities(quat, log_scale, centers)
+    n = pi.shape[0]
+    w = np.ones(n) if valid is None else np.asarray(valid, np.float64)
+    Pw = w * np.sum(occ[None, :] * C[pi] * C[pj], axis=1)
+    live = Pw != 0
+    ki, kj, Pk = pi[live], pj[live], Pw[live]
+    jv = np.zeros(n)
+    for a in range(0, n, bra_chunk):
+        sl = slice(a, a + bra_chunk)
+        jv[sl] = eri_block_schur(q, pi[sl], pj[sl], ki, kj) @ Pk
+    return 0.5 * float(np.sum(jv * Pw)), jv
+
+# ----------------------------------------------------------------------------------------------
 #  Screened RI-K  (gs_dft/coulomb/ri.py:497-544)
 # ----------------------------------------------------------------------------------------------
 

@@ -25,7 +25,12 @@ Outputs (compressed .npz, a few hundred KB in all):
     list of the three systems, and its gradient by Richardson central differences of the executed
     reference on the 10-splat system.
 
-``python tests/golden/make_golden.py vne`` (or ``k``) regenerates only that file.
+  * ``ref_exact.npz``   — the screened exact Hartree energy (``screened_coulomb_energy``, the
+    Schur (pair|pair) kernel) on the padded ordered lists of the two random systems, the unique
+    list of the 48-splat one, and the first 2000 ordered pairs of CO2 (the full CO2 list takes the
+    NumPy stand-in half an hour).
+
+``python tests/golden/make_golden.py vne`` (or ``k``, ``exact``) regenerates only that file.
 """
 from __future__ import annotations
 
@@ -243,7 +248,34 @@ def make_k(eps=1e-7, lam=1e-8):
     print("k grad: M=10 E_K=", out["grad_E_K"])
 
 
+def make_exact(eps=1e-7):
+    spec, _, pairs, _ = _modules()
+    cs = jaxshim.load("gs_dft.coulomb.stream")
+    out = {}
+    for name, s in _cases().items():
+        sp = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+        C, occ = J(s.C_occ), J(s.occ)
+        pi, pj, _ = pairs.neighbor_pairs(sp, eps=eps)
+        n = int(pi.shape[0])
+        if name == "co2":
+            pi, pj, v = pi[:2000], pj[:2000], None
+            out["co2_sub_pi"], out["co2_sub_pj"] = np.asarray(pi), np.asarray(pj)
+        else:
+            pi, pj, v = pairs.neighbor_pairs(sp, eps=eps, pad_to=n + 37)
+        out[f"{name}_E"] = float(cs.screened_coulomb_energy(sp, C, occ, pi, pj, valid=v,
+                                                            bra_chunk=128))
+        print(f"exact {name}: E_J={out[f'{name}_E']:.15g}", flush=True)
+        if name == "rand48":
+            ui, uj, uw = pairs.neighbor_pairs(sp, eps=eps, unique=True)
+            out["rand48_E_unique"] = float(cs.screened_coulomb_energy(sp, C, occ, ui, uj,
+                                                                      valid=uw, bra_chunk=128))
+    np.savez_compressed(os.path.join(HERE, "ref_exact.npz"), **out)
+
+
 if __name__ == "__main__":
+    if sys.argv[1:] == ["exact"]:
+        make_exact()
+        sys.exit(0)
     if sys.argv[1:] == ["vne"]:
         make_vne()
         sys.exit(0)
@@ -256,3 +288,4 @@ if __name__ == "__main__":
     make_nodes_bwd()
     make_vne()
     make_k()
+    make_exact()

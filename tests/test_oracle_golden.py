@@ -203,3 +203,21 @@ def test_exchange_gradient_matches_reference_finite_differences():
     for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
         ref = r["grad_" + k]
         np.testing.assert_allclose(res[k], ref, rtol=0, atol=5e-9 * np.abs(ref).max())
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_exact_coulomb_energy_matches_reference(case):
+    """Screened exact E_J (Schur (pair|pair) kernel) against the executed reference
+    (gs_dft/coulomb/stream.py:249-320); CO2 on its first 2000 ordered pairs."""
+    g = load_golden(case)
+    r = load_golden("ref_exact.npz")
+    name = case[4:-4]
+    arr = (g["quat"], g["log_scale"], g["centers"], g["C_occ"], g["occ"])
+    if name == "co2":
+        E, _ = O.screened_coulomb_energy_exact(arr, r["co2_sub_pi"], r["co2_sub_pj"], None)
+    else:
+        E, _ = O.screened_coulomb_energy_exact(arr, g["pad_pi"], g["pad_pj"], g["pad_v"])
+    np.testing.assert_allclose(E, float(r[f"{name}_E"]), rtol=1e-12)
+    if name == "rand48":
+        Eu, _ = O.screened_coulomb_energy_exact(arr, g["uni_pi"], g["uni_pj"], g["uni_w"])
+        np.testing.assert_allclose(Eu, float(r["rand48_E_unique"]), rtol=1e-12)
