@@ -310,7 +310,7 @@ def main():
     if world == 1:
         # rows beyond the metric, measured after it; a failure here is recorded, never fatal
         next_rows = {}
-        for name, fn in (("vne", measure_vne), ("k", measure_k)):
+        for name, fn in (("vne", measure_vne), ("k", measure_k), ("exact_j", measure_exact)):
             try:
                 next_rows[name] = fn(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C,
                                      occ, flush, peak, args, aux=aux, L=L)
@@ -448,6 +448,34 @@ def measure_k(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flu
             "flop_per_step": flop, "achieved_tflops": flop / (ms * 1e-3) / 1e12,
             "frac_of_measured_fp64_peak": flop / (ms * 1e-3) / peak,
             "E_K": float(eng.E[0]), "workspace_bytes": eng.ws_bytes}
+
+
+def measure_exact(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush, peak,
+                  args, **_):
+    """The screened exact Hartree energy (value; O(n_rep^2) pair-pair integrals) on the same pair
+    list, one warm-up and two timed evaluations with CUDA events (not part of the metric)."""
+    s = g.Splat(quat, log_scale, centers)
+    E = g.screened_coulomb_energy(s, C, occ, pi, pj, valid=valid)
+    torch.cuda.synchronize()
+    total, K = 0.0, 2
+    for k in range(K):
+        flush.fill_(float(k))
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        E = g.screened_coulomb_energy(s, C, occ, pi, pj, valid=valid)
+        b.record()
+        b.synchronize()
+        total += a.elapsed_time(b)
+    ms = total / K
+    from gs_dft_b200.coulomb.engine import make_plan
+    n_rep = make_plan(pi.to(torch.int32).contiguous(), pj.to(torch.int32).contiguous(),
+                      valid.to(torch.float64).contiguous(), sy.M).n_rep_total
+    pp = float(n_rep) * n_rep
+    return {"what": "screened exact E_J (Schur-equivalent 20-node (pair|pair) kernel, value; "
+                    "plan, pair prep and gsdft_exact_j per call), not part of the metric",
+            "ms": ms, "evaluations_timed": K, "evaluated_pairs": n_rep,
+            "pair_pairs_per_s": pp / (ms * 1e-3), "E_J_exact": float(E)}
 
 
 def _launches_per_step(lib, step, torch):

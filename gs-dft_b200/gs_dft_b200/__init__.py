@@ -8,9 +8,9 @@ the analytic gradient, as hand-written sm_100a CUDA kernels behind a C ABI
 from .basis import IsotropicSplat, Splat, init_product_aux
 from .coulomb import (RIJEngine, RIKEngine, aux_cholesky, aux_metric, aux_quantities,
                       df_coulomb_energy_screened, df_coulomb_gamma_screened, df_coulomb_solve,
-                      df_exchange_energy_screened)
-from .ks import (CoulombKS, DFSpec, ExternalKS, Pairlist, SplatModel, SplatState, df, pad_rule,
-                 pairlist, refresh)
+                      df_exchange_energy_screened, screened_coulomb_energy)
+from .ks import (CoulombKS, DFSpec, ExternalKS, Pairlist, ScreenedExactCoulomb, SplatModel,
+                 SplatState, df, pad_rule, pairlist, refresh)
 from .screening import (density_pairs, neighbor_pairs, screened_external_energy,
                         screened_nuclear_pairs, stripe_pairs)
 
@@ -20,5 +20,5 @@ __all__ = [
     "df_coulomb_solve", "df_coulomb_energy_screened", "RIJEngine", "df", "pairlist", "DFSpec",
     "Pairlist", "CoulombKS", "SplatModel", "SplatState", "refresh", "pad_rule",
     "screened_nuclear_pairs", "density_pairs", "screened_external_energy", "ExternalKS",
-    "RIKEngine", "df_exchange_energy_screened",
+    "RIKEngine", "df_exchange_energy_screened", "screened_coulomb_energy", "ScreenedExactCoulomb",
 ]

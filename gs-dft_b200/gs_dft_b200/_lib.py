@@ -82,6 +82,8 @@ SIGNATURES = {
                                 _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64,
                                 _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_k_unit_q": (_i32, [_c_p, _i64, _c_p, _c_p]),
+    "gsdft_exact_j_workspace_size": (_sz, [_i64]),
+    "gsdft_exact_j": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
                                   _i64, _c_p, _c_p]),
 }

@@ -79,3 +79,23 @@ class ScreenedProductDFCoulomb:
         keng = state.k_engine_for(basis, C_orth)
         e_k = _ScreenedDFExchange.apply(basis.quat, basis.log_scale, basis.centers, C_orth, keng)
         return e_j, e_k
+
+
+class ScreenedExactCoulomb:
+    """Exact streamed ERI over the significant pairs (DF-free), PBE-class only: the reference's
+    ``ScreenedExactCoulomb`` (gs_dft/ks/terms.py:195-205). ``energy(basis, C_orth, P, occ, state)
+    -> (E_J, 0)``; the value only (its gradient is not on the B200 path), and hybrids are rejected
+    as in the reference (there is no screened exact K)."""
+
+    def __init__(self, chunk: int = 128, hf_coeff: float = 0.0):
+        if hf_coeff != 0.0:
+            raise ValueError("ScreenedExactCoulomb is PBE-class only (no screened exact K)")
+        self.chunk = int(chunk)
+        self.hf_coeff = 0.0
+
+    def energy(self, basis, C_orth, P, occ, state):
+        from ..coulomb.stream import screened_coulomb_energy
+        pi, pj, valid = state.pairs
+        e_j = screened_coulomb_energy(basis, C_orth, occ, pi, pj, valid=valid,
+                                      bra_chunk=self.chunk)
+        return e_j, torch.zeros((), dtype=e_j.dtype, device=e_j.device)

@@ -324,6 +324,15 @@ int gsdft_k_backward(const double* rec, const int32_t* pi, const int32_t* pj,
 /* rec_out = rec with q = 1 (Q = 1, QK = KN pref), for the chain of a weighted reverse pass. */
 int gsdft_k_unit_q(const double* rec, int64_t n_rep, double* rec_out, gsdft_stream_t stream);
 
+/* Screened exact Hartree energy E_J = 1/2 sum_{a,b} q_a q_b (a|b) over the pair representatives
+ * (q from rec: pair weights, densities and merged twins included), (a|b) the exact 6-D Coulomb
+ * integral of two product Gaussians on the reference's 20-node rule. Replaces
+ * screened_coulomb_energy with full_eri_block_schur (gs_dft/coulomb/stream.py:249-320); value only.
+ * Writes J (n_rep: J_a = sum_b q_b (a|b)) and E (device scalar). O(n_rep^2). Deterministic. */
+size_t gsdft_exact_j_workspace_size(int64_t n_rep);
+int gsdft_exact_j(const double* rec, int64_t n_rep, double* J, double* E, void* ws, size_t ws_bytes,
+                  gsdft_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
