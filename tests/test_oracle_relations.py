@@ -1,0 +1,84 @@
+"""Relations the reference's own tests assert for this path, checked on the CPU oracle (they pin it
+beyond the golden vectors): the DF energy is a lower bound of the exact Hartree energy and
+approaches it as the aux set grows (tests/unit/test_coulomb_df.py:54-63,
+tests/unit/test_aux_mult.py:28-49), the closed-form 3x3 algebra agrees with LAPACK
+(tests/unit/test_linalg3.py:14-44), solving with the metric's Cholesky factor agrees with a general
+solve (tests/unit/test_refresh_cholv.py:24-41), and the small-argument branch of F0 joins the closed
+form (tests/unit/test_coulomb_stream.py:115-134)."""
+import numpy as np
+import pytest
+
+import gsdft_oracle as O
+
+
+def _system():
+    from gs_dft_b200.systems import small_random_system
+    s = small_random_system(24, 4, seed=0)
+    arr = (s.quat, s.log_scale, s.centers, s.C_occ, s.occ)
+    q = O.full_quantities(s.quat, s.log_scale, s.centers)
+    M = s.M
+    pi = np.repeat(np.arange(M), M).astype(np.int32)     # every ordered pair: no screening
+    pj = np.tile(np.arange(M), M).astype(np.int32)
+    return s, arr, q, pi, pj
+
+
+@pytest.fixture(scope="module")
+def exact_and_df():
+    s, arr, q, pi, pj = _system()
+    E_exact, _ = O.screened_coulomb_energy_exact(arr, pi, pj, None)
+    out = {}
+    for scales in ((1.0,), (1.0, 2.0), (0.5, 1.0, 2.0)):
+        la, R = O.init_product_aux(q, scales=scales)
+        aq = O.aux_quantities(la, R)
+        L = O.aux_cholesky(O.aux_metric(*aq), s.lam)
+        E_df, _, _ = O.energy(arr, aq, L, pi, pj, np.ones(pi.size))
+        out[scales] = (E_df, aq[0].shape[0])
+    return s.M, E_exact, out
+
+
+def test_df_energy_is_a_lower_bound(exact_and_df):
+    M, E_exact, out = exact_and_df
+    for scales, (E_df, _) in out.items():
+        assert E_df <= E_exact * (1 + 1e-12), (scales, E_df, E_exact)
+
+
+def test_bigger_aux_moves_df_toward_exact(exact_and_df):
+    """Nested aux sets (scales (1), (1, 2), (0.5, 1, 2)): n_aux = mult x M and the DF gap shrinks."""
+    M, E_exact, out = exact_and_df
+    gaps = []
+    for scales in ((1.0,), (1.0, 2.0), (0.5, 1.0, 2.0)):
+        E_df, n_aux = out[scales]
+        assert n_aux == len(scales) * M
+        gaps.append(E_exact - E_df)
+    assert gaps[0] >= gaps[1] >= gaps[2] >= -1e-12 * abs(E_exact), gaps
+
+
+def test_closed_form_3x3_matches_lapack():
+    rng = np.random.default_rng(0)
+    B = rng.standard_normal((64, 3, 3))
+    A = np.einsum("nkl,nml->nkm", B, B) + 0.5 * np.eye(3)     # SPD like A_i + A_j + t^2 I
+    b = rng.standard_normal((64, 3))
+    assert np.max(np.abs(O.det3(A) - np.linalg.det(A))) < 1e-12
+    inv = O.adj3(A) / O.det3(A)[:, None, None]
+    assert np.max(np.abs(inv - np.linalg.inv(A))) < 1e-12
+    assert np.max(np.abs(O.solve3(A, b) - np.linalg.solve(A, b[..., None])[..., 0])) < 1e-12
+
+
+def test_cholesky_solve_matches_general_solve():
+    s, arr, q, pi, pj = _system()
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    V = O.aux_metric(*aq)
+    L = O.aux_cholesky(V, s.lam)
+    gamma = O.df_coulomb_gamma_screened(q, s.C_occ, s.occ, aq, pi, pj, np.ones(pi.size))
+    E_chol, d_chol = O.df_coulomb_solve(gamma, L)
+    Vs = V + s.lam * np.eye(V.shape[0])
+    d_solve = np.linalg.solve(Vs, gamma)
+    assert abs(E_chol - 0.5 * float(gamma @ d_solve)) < 1e-10 * abs(E_chol)
+
+
+def test_boys_small_argument_branch_joins_closed_form():
+    T = np.array([1e-8 * (1 - 1e-6), 1e-8 * (1 + 1e-6)])
+    F = O.boys0(T)
+    closed = 0.5 * np.sqrt(np.pi / T) * np.vectorize(__import__("math").erf)(np.sqrt(T))
+    np.testing.assert_allclose(F, closed, rtol=1e-14)
