@@ -9,6 +9,7 @@ from dataclasses import dataclass
 
 import torch
 
+from .. import _check
 from ..coulomb.engine import splat_quantities
 
 
@@ -20,6 +21,12 @@ class Splat:
     quat: torch.Tensor
     log_scale: torch.Tensor
     centers: torch.Tensor
+
+    def __post_init__(self):
+        M = int(self.centers.shape[0]) if isinstance(self.centers, torch.Tensor) else -1
+        for t, name, k in ((self.quat, "quat", 4), (self.log_scale, "log_scale", 3),
+                           (self.centers, "centers", 3)):
+            _check.f64(t, name, (M, k), contiguous=False)
 
     @property
     def n_basis(self) -> int:

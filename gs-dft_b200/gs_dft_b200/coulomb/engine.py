@@ -23,6 +23,7 @@ from dataclasses import dataclass
 
 import torch
 
+from .. import _check
 from .._lib import (REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, lib, ptr,
                     stream_handle)
 
@@ -62,6 +63,8 @@ class PairPlan:
 
 
 def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: bool = True):
+    _check.pair_indices(pi, pj, M)
+    _check.f64(w, "pair weights", (int(pi.shape[0]),))
     dev = pi.device
     n = int(pi.shape[0])
     pos = torch.empty(max(n, 1), dtype=torch.int32, device=dev)
@@ -88,6 +91,20 @@ def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: boo
              ptr(oj), ptr(sj), ptr(qj), ptr(gws), gb, stream_handle(dev))
     return PairPlan(n=n, n_rep_total=n_rep, r0=r0, r1=r1, rep_pos=pos, rep_w=rw, rep_twin=tw,
                     order_i=oi, seg_i=si, partner_i=qi, order_j=oj, seg_j=sj, partner_j=qj)
+
+
+def check_step_inputs(M, n_occ, quat, log_scale, centers, C_occ=None, occ=None):
+    """The per-step parameters as the kernels read them: contiguous float64 CUDA tensors of the
+    engine's sizes (metadata only)."""
+    args = [(quat, "quat", (M, 4)), (log_scale, "log_scale", (M, 3)), (centers, "centers", (M, 3))]
+    if n_occ > 0:
+        args.append((C_occ, "C_occ", (M, n_occ)))
+        if occ is not None:
+            args.append((occ, "occ", (n_occ,)))
+    for t, name, shape in args:          # dtype, shape and layout of all first, then the device
+        _check.tensor(t, name, torch.float64, shape, cuda=False)
+    for t, name, _ in args:
+        _check.tensor(t, name, torch.float64, None, contiguous=False)
 
 
 def splat_quantities(quat, log_scale):
@@ -120,9 +137,15 @@ class RIJEngine:
                  merge_twins=True, inverse_solve=True, atoms=None):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
-        self.pi = pi.contiguous()
-        self.pj = pj.contiguous()
+        self.pi = pi.to(torch.int32).contiguous()
+        self.pj = pj.to(torch.int32).contiguous()
         self.w = w.to(F64).contiguous()
+        if beta is not None:
+            n_aux = int(beta.shape[0])
+            beta, KN = _check.f64(beta, "beta", (n_aux,)), _check.f64(KN, "KN", (n_aux,))
+            R = _check.f64(R.contiguous(), "R", (n_aux, 3))
+            if L is not None:
+                _check.f64(L, "L", (n_aux, n_aux))
         self.beta, self.R, self.KN, self.L = beta, R, KN, L
         self.rij = beta is not None
         self.n_aux = int(beta.shape[0]) if self.rij else 0
@@ -189,6 +212,7 @@ class RIJEngine:
     def prepare(self, quat, log_scale, centers, C_occ, occ):
         """Splat quantities and the pair records (A_hat eigenframe, P, KN, q) of this device's
         representatives."""
+        check_step_inputs(self.M, self.n_occ, quat, log_scale, centers, C_occ, occ)
         s = stream_handle(self.device)
         lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),
                  ptr(self.N), s)

@@ -20,7 +20,8 @@ from __future__ import annotations
 import torch
 
 from .._lib import REC_FIELDS, SIDE_FIELDS, VJP_FIELDS, lib, ptr, stream_handle
-from .engine import make_plan
+from .. import _check
+from .engine import check_step_inputs, make_plan
 
 F64 = torch.float64
 MAX_WORKSPACE_BYTES = 64 << 30
@@ -47,8 +48,11 @@ class RIKEngine:
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi, self.pj = pi.to(torch.int32).contiguous(), pj.to(torch.int32).contiguous()
-        self.beta, self.R, self.KN, self.L = beta, R.contiguous(), KN, L
         self.n_aux = int(beta.shape[0])
+        self.beta = _check.f64(beta, "beta", (self.n_aux,))
+        self.R = _check.f64(R.contiguous(), "R", (self.n_aux, 3))
+        self.KN = _check.f64(KN, "KN", (self.n_aux,))
+        self.L = _check.f64(L, "L", (self.n_aux, self.n_aux))
         self.plan = make_plan(self.pi, self.pj, w, self.M, 0, 1, merge_twins)
         dev, nl, n = self.device, self.plan.n_rep, self.plan.n
         self.ws_bytes = int(lib.gsdft_k_workspace_size(nl, self.n_aux, self.n_occ))
@@ -70,6 +74,7 @@ class RIKEngine:
 
     def forward(self, quat, log_scale, centers, C):
         """E_K (device scalar); keeps what the backward needs in the engine's workspace."""
+        check_step_inputs(self.M, self.n_occ, quat, log_scale, centers, C)
         s = stream_handle(self.device)
         nl = self.plan.n_rep
         lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),

@@ -16,6 +16,7 @@ import ctypes
 
 import torch
 
+from .. import _check
 from .._lib import lib, ptr, stream_handle
 
 from .engine import RIJEngine
@@ -88,7 +89,8 @@ def df_coulomb_gamma_screened(splats, C_occ, occ, aux, pi, pj, chunk=2048, valid
     """gamma_P = sum_a (P|a) q_a over the listed pairs (q_a = valid_a sum_o occ_o C_io C_jo)."""
     eng = _engine(splats, C_occ, aux, pi, pj, valid, L=None)
     g = eng.forward_local(splats.quat.detach().contiguous(), splats.log_scale.detach().contiguous(),
-                          splats.centers.detach().contiguous(), C_occ.detach().contiguous(),
+                          splats.centers.detach().contiguous(),
+                          C_occ.detach().to(F64).contiguous(),
                           occ.detach().to(F64).contiguous())
     return g.clone()
 
@@ -98,9 +100,11 @@ def df_coulomb_solve(gamma, aux, lam=1e-8, cholV=None):
     triangular solves, otherwise the metric is built and factored first."""
     L = cholV if cholV is not None else aux_cholesky(aux, lam)
     n = int(gamma.shape[0])
+    _check.f64(L, "cholV", (n, n))
+    gamma = _check.f64(gamma.detach().to(F64).contiguous(), "gamma", (n,))
     d = torch.empty_like(gamma)
     E = torch.empty(1, dtype=F64, device=gamma.device)
-    lib.call("gsdft_j_solve", ptr(L), ptr(gamma.contiguous()), n, ptr(d), ptr(E), None, 0,
+    lib.call("gsdft_j_solve", ptr(L), ptr(gamma), n, ptr(d), ptr(E), None, 0,
              stream_handle(gamma.device))
     return E[0]
 
@@ -111,7 +115,7 @@ class _ScreenedDFEnergy(torch.autograd.Function):
     @staticmethod
     def forward(ctx, quat, log_scale, centers, C_occ, occ, eng):
         q, ls, c = quat.detach().contiguous(), log_scale.detach().contiguous(), centers.detach().contiguous()
-        C, oc = C_occ.detach().contiguous(), occ.detach().to(F64).contiguous()
+        C, oc = C_occ.detach().to(F64).contiguous(), occ.detach().to(F64).contiguous()
         eng.forward_local(q, ls, c, C, oc)
         E, _ = eng.solve()
         ctx.eng = eng
