@@ -10,6 +10,7 @@ from dataclasses import dataclass
 
 import torch
 
+from .. import _check
 from .._lib import lib, ptr, stream_handle
 from .spectral import Splat, full_quantities
 
@@ -22,6 +23,11 @@ class IsotropicSplat:
 
     log_alpha: torch.Tensor
     centers: torch.Tensor
+
+    def __post_init__(self):
+        n = int(self.log_alpha.shape[0]) if isinstance(self.log_alpha, torch.Tensor) else -1
+        self.log_alpha = _check.f64(self.log_alpha, "log_alpha", (n,), contiguous=False).contiguous()
+        self.centers = _check.f64(self.centers, "aux centers", (n, 3), contiguous=False).contiguous()
 
     @property
     def n_basis(self) -> int:
@@ -60,6 +66,7 @@ def init_product_aux(basis: Splat, pi=None, pj=None, valid=None, *, scales=(1.0,
     else:
         pi = pi.to(torch.int32).contiguous()
         pj = pj.to(torch.int32).contiguous()
+        _check.pair_indices(pi, pj, M)
         n = int(pi.shape[0])
         w = (torch.ones(n, dtype=F64, device=dev) if valid is None
              else valid.to(F64).contiguous())

@@ -85,7 +85,8 @@ def stripe_pairs(pi, pj, valid, G: int):
     if G <= 1 or n % G:
         return pi, pj, valid
     w = pair_weight(valid).contiguous()
+    pi, pj = pi.to(torch.int32).contiguous(), pj.to(torch.int32).contiguous()
     pio, pjo, wo = torch.empty_like(pi), torch.empty_like(pj), torch.empty_like(w)
-    lib.call("gsdft_stripe_pairs", ptr(pi.contiguous()), ptr(pj.contiguous()), ptr(w), n, int(G),
+    lib.call("gsdft_stripe_pairs", ptr(pi), ptr(pj), ptr(w), n, int(G),
              ptr(pio), ptr(pjo), ptr(wo), stream_handle(pi.device))
     return pio, pjo, (wo if valid.dtype == torch.float64 else wo != 0)
