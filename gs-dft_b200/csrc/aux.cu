@@ -116,12 +116,15 @@ __global__ void half_dot_kernel(const double* __restrict__ g, const double* __re
 // for the forward sweep, warps over rows and lanes over the block's columns for the backward
 // sweep), then the 32x32 diagonal triangle is solved inside one warp. The solution lives in shared
 // memory; every reduction has a fixed order.
-// --- per-step solve through inverse factors -------------------------------------------------------
-// With X = L^-1 and XT = L^-T (row-major, computed once per refresh), d = XT (X gamma) and
-// E = 1/2 |X gamma|^2 = 1/2 gamma.(L L^T)^-1 gamma are two triangular mat-vecs: every row is
-// independent, so they spread over the SMs instead of walking a dependent chain of substitution
-// steps. One warp per row; each lane keeps four partial sums; the warp's shuffle tree fixes the
-// summation order (bitwise reproducible).
+// --- per-step solve through the inverse factor ----------------------------------------------------
+// With X = L^-1 (computed once per refresh), d = X^T (X gamma) and E = 1/2 |X gamma|^2 =
+// 1/2 gamma.(L L^T)^-1 gamma are two triangular mat-vecs: every row is independent, so they spread
+// over the SMs instead of walking a dependent chain of substitution steps, and the two of them
+// stream the factor's n^2 doubles once. Both read ONE packed n x n matrix: its lower triangle (with
+// the diagonal) is L^-1 and its strict upper triangle is L^-T's, i.e. the mirror of the strict lower
+// one, so row i holds L^-1's row i in [0, i] and L^-T's row i in [i, n) (the diagonal is shared).
+// One warp per row; each lane keeps four partial sums; the warp's shuffle tree fixes the summation
+// order (bitwise reproducible).
 constexpr int kTriWarps = 4;
 
 __global__ void identity_kernel(double* X, int64_t n) {
@@ -129,9 +132,13 @@ __global__ void identity_kernel(double* X, int64_t n) {
   if (k < n * n) X[k] = (k / n == k % n) ? 1.0 : 0.0;
 }
 
-// XT[j][i] = X[i][j] through a 32x33 shared tile (coalesced both ways).
-__global__ void transpose_kernel(const double* __restrict__ X, int64_t n, double* __restrict__ XT) {
+// In place, X[c][r] = X[r][c] for r > c: the strict lower triangle mirrored into the strict upper
+// one, through 32 x 33 shared tiles (coalesced both ways). A block reads one lower (or diagonal)
+// tile and writes its mirror tile, which no other block reads; a diagonal tile is read whole before
+// its upper half is written.
+__global__ void mirror_lower_kernel(double* X, int64_t n) {
   __shared__ double t[32][33];
+  if (blockIdx.x > blockIdx.y) return;  // strictly upper tiles are written by their mirror's block
   const int64_t r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
   for (int k = threadIdx.y; k < 32; k += blockDim.y) {
     const int64_t r = r0 + k, c = c0 + threadIdx.x;
@@ -139,8 +146,8 @@ __global__ void transpose_kernel(const double* __restrict__ X, int64_t n, double
   }
   __syncthreads();
   for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t r = c0 + k, c = r0 + threadIdx.x;
-    if (r < n && c < n) XT[r * n + c] = t[threadIdx.x][k];
+    const int64_t r = c0 + k, c = r0 + threadIdx.x;  // destination (r, c) = mirror of (c, r)
+    if (r < n && c < n && r < c) X[r * n + c] = t[threadIdx.x][k];
   }
 }
 
@@ -337,30 +344,30 @@ extern "C" int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux
   return GSDFT_OK;
 }
 
-extern "C" int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv2,
+extern "C" int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv,
                                      gsdft_stream_t stream) {
-  GSDFT_REQUIRE(n_aux > 0 && n_aux <= GSDFT_SOLVE_INV_MAX, "n_aux out of range");
-  GSDFT_REQUIRE(L && Linv2, "null pointer");
+  GSDFT_REQUIRE(n_aux > 0 && n_aux <= GSDFT_SOLVE_INV_MAX, "n_aux out of range (1..%d)",
+                GSDFT_SOLVE_INV_MAX);
+  GSDFT_REQUIRE(L && Linv, "null pointer");
+  GSDFT_REQUIRE(L != Linv, "Linv must not alias L");
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t n = n_aux;
-  double* X = Linv2;
-  double* XT = Linv2 + n * n;
-  identity_kernel<<<grid_1d(n * n, 256), 256, 0, st>>>(X, n);
+  identity_kernel<<<grid_1d(n * n, 256), 256, 0, st>>>(Linv, n);
   GSDFT_LAUNCHED("identity");
   Handles* h = nullptr;
   int rc = get_handles(&h);
   if (rc) return rc;
   cublasSetStream(h->blas, st);
   // Column-major, the row-major lower L is U = L^T (upper) and the row-major X is X^T. U Y = I gives
-  // Y = L^-T, i.e. X = L^-1 row-major.
+  // Y = L^-T, i.e. X = L^-1 row-major (lower triangular; its strict upper triangle stays zero).
   const double one = 1.0;
   if (cublasDtrsm(h->blas, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N,
-                  CUBLAS_DIAG_NON_UNIT, (int)n, (int)n, &one, L, (int)n, X, (int)n) !=
+                  CUBLAS_DIAG_NON_UNIT, (int)n, (int)n, &one, L, (int)n, Linv, (int)n) !=
       CUBLAS_STATUS_SUCCESS)
     return fail(GSDFT_ERR_LINALG, "cublasDtrsm failed");
   const dim3 tg((unsigned)((n + 31) / 32), (unsigned)((n + 31) / 32));
-  transpose_kernel<<<tg, dim3(32, 8), 0, st>>>(X, n, XT);
-  GSDFT_LAUNCHED("transpose");
+  mirror_lower_kernel<<<tg, dim3(32, 8), 0, st>>>(Linv, n);
+  GSDFT_LAUNCHED("mirror_lower");
   return GSDFT_OK;
 }
 
@@ -368,19 +375,19 @@ extern "C" size_t gsdft_j_solve_inv_workspace_size(int64_t n_aux) {
   return ((size_t)imax64(n_aux, 1) * sizeof(double) + 255) & ~(size_t)255;
 }
 
-extern "C" int gsdft_j_solve_inv(const double* Linv2, const double* gamma, int64_t n_aux, double* d,
+extern "C" int gsdft_j_solve_inv(const double* Linv, const double* gamma, int64_t n_aux, double* d,
                                  double* E, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
   GSDFT_REQUIRE(n_aux > 0 && n_aux <= GSDFT_SOLVE_INV_MAX, "n_aux out of range");
-  GSDFT_REQUIRE(Linv2 && gamma && d && E && ws, "null pointer");
+  GSDFT_REQUIRE(Linv && gamma && d && E && ws, "null pointer");
   GSDFT_REQUIRE(ws_bytes >= gsdft_j_solve_inv_workspace_size(n_aux), "workspace too small");
   GSDFT_REQUIRE(d != gamma, "d must not alias gamma");
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t n = n_aux;
   double* y = static_cast<double*>(ws);
   const unsigned grid = (unsigned)((n + kTriWarps - 1) / kTriWarps);
-  tri_rows_kernel<true><<<grid, kTriWarps * 32, 0, st>>>(Linv2, gamma, n, y, nullptr);
+  tri_rows_kernel<true><<<grid, kTriWarps * 32, 0, st>>>(Linv, gamma, n, y, nullptr);
   GSDFT_LAUNCHED("tri_rows");
-  tri_rows_kernel<false><<<grid, kTriWarps * 32, 0, st>>>(Linv2 + n * n, y, n, d, E);
+  tri_rows_kernel<false><<<grid, kTriWarps * 32, 0, st>>>(Linv, y, n, d, E);
   GSDFT_LAUNCHED("tri_rows");
   return GSDFT_OK;
 }

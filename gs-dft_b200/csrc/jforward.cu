@@ -170,11 +170,15 @@ constexpr int kFwNP = GSDFT_FW_NP;  // pairs evaluated together per thread (inde
 constexpr int kFwBits = GSDFT_FW_EXP2_BITS;  // 2^kFwBits-entry weighted exp2 table per node
 constexpr size_t kFwDynSmem = sizeof(double) * GSDFT_NQUAD * (1 << kFwBits);
 
+// Node evaluations of the forward kernel since the last reset: (aux, pair) units times the nodes
+// each evaluated (20 without screening). Read by gsdft_node_evals.
+static __device__ unsigned long long g_fw_node_evals;
+
 __global__ void GSDFT_FW_BOUNDS
     j_forward_kernel(const double* __restrict__ rec, int64_t n_live,
                      const double* __restrict__ beta, const double* __restrict__ R,
                      const double* __restrict__ KN, int64_t n_aux, int64_t per_split,
-                     double* __restrict__ partial) {
+                     double skip2, double* __restrict__ partial) {
   __shared__ __align__(128) double tile[2][kFwTile * GSDFT_REC_FIELDS];
   __shared__ __align__(8) uint64_t bar[2];
   extern __shared__ __align__(16) double etab[];  // GSDFT_NQUAD x 2^kFwBits weighted table
@@ -211,6 +215,7 @@ __global__ void GSDFT_FW_BOUNDS
   }
 
   double acc = 0.0;
+  unsigned long long evals = 0;  // node evaluations per real (aux, pair), warp-uniform
   bool ok = true;
   for (int t = 0; t < ntiles && ok; ++t) {
     // block-uniform: a thread whose bounded wait ran out takes the whole block out of the loop
@@ -220,7 +225,7 @@ __global__ void GSDFT_FW_BOUNDS
     const int cnt = (int)imin64(kFwTile, a1 - (a0 + (int64_t)t * kFwTile));
     // a warp with no aux (the tail of the last aux tile) only takes part in the barriers
     for (int k = 0; warp_active && k < cnt; k += kFwNP) {
-      double m[kFwNP][3], g[kFwNP][3], h[kFwNP][3], qk[kFwNP], coul[kFwNP];
+      double m[kFwNP][3], g[kFwNP][3], h[kFwNP][3], qk[kFwNP], coul[kFwNP], e0[kFwNP];
 #pragma unroll
       for (int p = 0; p < kFwNP; ++p) {
         const int kk = k + p < cnt ? k + p : k;  // a duplicate of pair k stands in, weight 0
@@ -239,10 +244,13 @@ __global__ void GSDFT_FW_BOUNDS
         }
         qk[p] = k + p < cnt ? rr[GSDFT_REC_QK] : 0.0;
         coul[p] = 0.0;
+        e0[p] = 0.0;
       }
+      int nodes = GSDFT_NQUAD;
 #pragma unroll
       for (int n = 0; n < GSDFT_NQUAD; ++n) {
         const double t2 = kQuadT2[n];
+        bool far = true;
 #pragma unroll
         for (int p = 0; p < kFwNP; ++p) {
           const double G0 = fma(t2, h[p][0], g[p][0]);
@@ -253,10 +261,19 @@ __global__ void GSDFT_FW_BOUNDS
           const double num = fma(m[p][0], p12, G0 * fma(m[p][1], G2, m[p][2] * G1));
           const double y = rsqrt_pos(prod);
           const double inv = y * y;
-          const double ew = wexp2<kFwBits>(num * inv, t2, etab + (n << kFwBits));
+          const double x = num * inv;  // node exponent / t^2, log2 units
+          const double ew = wexp2<kFwBits>(x, t2, etab + (n << kFwBits));
           coul[p] = fma(y, ew, coul[p]);
+          if (n == 0) e0[p] = x * t2;
+          far = far && fma(x, t2, -e0[p]) < -skip2;
+        }
+        // node screening (warp-uniform): every later node is below the last bit of every lane's sum
+        if (n >= kNodeSkipFirst && n + 1 < GSDFT_NQUAD && __all_sync(0xffffffffu, far)) {
+          nodes = n + 1;
+          break;
         }
       }
+      evals += (unsigned long long)nodes * (unsigned long long)imin64(kFwNP, cnt - k);
 #pragma unroll
       for (int p = 0; p < kFwNP; ++p) acc = fma(qk[p], coul[p], acc);
     }
@@ -264,6 +281,8 @@ __global__ void GSDFT_FW_BOUNDS
     if (threadIdx.x == 0 && t + 2 < ntiles) issue(t + 2);
   }
   if (has_aux) partial[blockIdx.y * n_aux + P] = ok ? acc * KN[P] : __longlong_as_double(-1LL);
+  const unsigned lanes = __popc(__ballot_sync(0xffffffffu, has_aux));
+  if ((threadIdx.x & 31) == 0 && lanes) atomicAdd(&g_fw_node_evals, evals * lanes);
 }
 
 // gamma_P = sum_s partial[s][P], fixed order.
@@ -326,6 +345,14 @@ int device_status_forward(int* out, int clear) {
   return GSDFT_OK;
 }
 int device_status_vjp(int* out, int clear);
+int node_evals_forward(unsigned long long* out, int clear) {
+  GSDFT_CUDA(cudaMemcpyFromSymbol(out, g_fw_node_evals, sizeof(unsigned long long)));
+  if (clear) {
+    unsigned long long z = 0;
+    GSDFT_CUDA(cudaMemcpyToSymbol(g_fw_node_evals, &z, sizeof(z)));
+  }
+  return GSDFT_OK;
+}
 }  // namespace gsdft
 
 extern "C" int gsdft_device_status(int* status_host, int clear) {
@@ -388,7 +415,7 @@ extern "C" int gsdft_j_forward(const double* rec, int64_t n_live, const double* 
   per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
   dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
   j_forward_kernel<<<grid, kFwThreads, kFwDynSmem, st>>>(rec, n_live, beta, R, KN, n_aux,
-                                                         per_split, partial);
+                                                         per_split, node_skip_threshold(), partial);
   GSDFT_LAUNCHED("j_forward");
   sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(partial, S, n_aux, gamma);
   GSDFT_LAUNCHED("sum_splits");
@@ -462,7 +489,7 @@ extern "C" int gsdft_j_forward_noalloc(const double* rec, int64_t n_rep, const d
   per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
   dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
   j_forward_kernel<<<grid, kFwThreads, kFwDynSmem, st>>>(rec, n_rep, beta, R, KN, n_aux, per_split,
-                                                         scratch);
+                                                         node_skip_threshold(), scratch);
   GSDFT_LAUNCHED("j_forward_noalloc");
   sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(scratch, (int)S, n_aux, gamma);
   GSDFT_LAUNCHED("sum_splits_noalloc");

@@ -52,10 +52,14 @@ __global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const doubl
 
 // kW: the per-(P,a) weight of the reverse pass is W[a * ldw + P] x (the aux record's dbar KN)
 // (E = sum_{P,a} W[a][P] (P|a), as the RI-K gradient needs); without it the weight is dbar_P KN_P.
+// Node evaluations of the reverse kernel since the last reset ((aux, pair) units times the nodes
+// each evaluated). Read by gsdft_node_evals.
+static __device__ unsigned long long g_vjp_node_evals;
+
 template <bool kW>
 __global__ void GSDFT_VJP_BOUNDS
     j_vjp_kernel(const double* __restrict__ rec, int64_t n_live, const double* __restrict__ auxr,
-                 int64_t n_aux, int64_t per_split, double* __restrict__ out,
+                 int64_t n_aux, int64_t per_split, double skip2, double* __restrict__ out,
                  const double* __restrict__ Wt, int64_t ldw) {
   __shared__ __align__(128) double tile[2][kVjpTile * kAuxRec];
   __shared__ __align__(8) uint64_t bar[2];
@@ -97,6 +101,7 @@ __global__ void GSDFT_VJP_BOUNDS
   }
 
   double SJ = 0.0, SD[3] = {0, 0, 0}, SV[3] = {0, 0, 0}, SZ[6] = {0, 0, 0, 0, 0, 0};
+  unsigned long long evals = 0;  // node evaluations per (aux, pair), warp-uniform
   bool ok = true;
   for (int t = 0; t < ntiles; ++t) {
     ok = __syncthreads_and(mbar_wait(&bar[t & 1], (t >> 1) & 1));
@@ -117,6 +122,8 @@ __global__ void GSDFT_VJP_BOUNDS
         m[c] = (cP * L[c]) * (y[c] * y[c]);
       }
       double cf = 0.0, B[3] = {0, 0, 0}, C[3] = {0, 0, 0}, Z[6] = {0, 0, 0, 0, 0, 0};
+      double e0 = 0.0;
+      int nodes = GSDFT_NQUAD;
 #pragma unroll
       for (int n = 0; n < GSDFT_NQUAD; ++n) {
         const double t2 = kQuadT2[n], t4 = kQuadT4[n];
@@ -130,7 +137,9 @@ __global__ void GSDFT_VJP_BOUNDS
         const double num = fma(m[0], p12, fma(m[1], p02, m[2] * p01));
         const double yy = rsqrt_pos(prod);
         const double inv = yy * yy;
-                const double f = yy * wexp2<kVjpBits>(num * inv, t2, etab + (n << kVjpBits));
+        const double x = num * inv;  // node exponent / t^2, log2 units
+        const double f = yy * wexp2<kVjpBits>(x, t2, etab + (n << kVjpBits));
+        if (n == 0) e0 = x * t2;
         cf += f;
         const double iG0 = p12 * inv, iG1 = p02 * inv, iG2 = p01 * inv;
         const double g0 = f * iG0, g1 = f * iG1, g2 = f * iG2;
@@ -147,7 +156,14 @@ __global__ void GSDFT_VJP_BOUNDS
         Z[3] = fma(h0, iG1, Z[3]);
         Z[4] = fma(h0, iG2, Z[4]);
         Z[5] = fma(h1, iG2, Z[5]);
+        // node screening (warp-uniform): every later node is below the last bit of every lane's sums
+        if (n >= kNodeSkipFirst && n + 1 < GSDFT_NQUAD &&
+            __all_sync(0xffffffffu, fma(x, t2, -e0) < -skip2)) {
+          nodes = n + 1;
+          break;
+        }
       }
+      evals += (unsigned long long)nodes;
       SJ = fma(dk, cf, SJ);
       const double dkb = dk * b, dkb2 = dk * b2;
 #pragma unroll
@@ -177,6 +193,8 @@ __global__ void GSDFT_VJP_BOUNDS
 #pragma unroll
     for (int c = 0; c < 6; ++c) o[GSDFT_VJP_SZ00 + c] = ok ? SZ[c] : bad;
   }
+  const unsigned lanes = __popc(__ballot_sync(0xffffffffu, live));
+  if ((threadIdx.x & 31) == 0 && lanes) atomicAdd(&g_vjp_node_evals, evals * lanes);
 }
 
 __global__ void sum_vjp_splits_kernel(const double* __restrict__ part, int S, int64_t n,
@@ -472,6 +490,15 @@ static int vjp_splits(int64_t n_live, int64_t n_aux) {
   return best_splits(tiles, cap, max_s);
 }
 
+int node_evals_vjp(unsigned long long* out, int clear) {
+  GSDFT_CUDA(cudaMemcpyFromSymbol(out, g_vjp_node_evals, sizeof(unsigned long long)));
+  if (clear) {
+    unsigned long long z = 0;
+    GSDFT_CUDA(cudaMemcpyToSymbol(g_vjp_node_evals, &z, sizeof(z)));
+  }
+  return GSDFT_OK;
+}
+
 int device_status_vjp(int* out, int clear) {
   GSDFT_CUDA(cudaMemcpyFromSymbol(out, g_device_status, sizeof(int)));
   if (clear) {
@@ -510,7 +537,7 @@ static int vjp_run(const double* rec, int64_t n_live, const double* beta, const 
   int64_t per_split = (n_aux + S - 1) / S;
   dim3 grid((unsigned)((n_live + kVjpThreads - 1) / kVjpThreads), (unsigned)S);
   j_vjp_kernel<kW><<<grid, kVjpThreads, kVjpDynSmem, st>>>(rec, n_live, auxr, n_aux, per_split,
-                                                            part, Wt, ldw);
+                                                            node_skip_threshold(), part, Wt, ldw);
   GSDFT_LAUNCHED("j_vjp");
   if (S > 1) {
     sum_vjp_splits_kernel<<<grid_1d(n_live * GSDFT_VJP_FIELDS, 256), 256, 0, st>>>(part, S, n_live,

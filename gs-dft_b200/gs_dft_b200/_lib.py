@@ -16,7 +16,7 @@ ERR_ARG, ERR_CUDA, ERR_OVERFLOW, ERR_LINALG = 1, 2, 3, 4
 REC_FIELDS = 18
 VJP_FIELDS = 13
 SIDE_FIELDS = 20
-SOLVE_INV_MAX = 16384   # GSDFT_SOLVE_INV_MAX
+SOLVE_INV_MAX = 65536   # GSDFT_SOLVE_INV_MAX
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -32,6 +32,10 @@ SIGNATURES = {
     "gsdft_device_status": (_i32, [ctypes.POINTER(ctypes.c_int), _i32]),
     "gsdft_kernel_launches": (_i64, []),
     "gsdft_dfma_probe": (_i32, [_c_p, _i64, _i32, _i32, _c_p]),
+    "gsdft_set_node_screening": (_i32, [_i32]),
+    "gsdft_node_screening": (_i32, []),
+    "gsdft_node_evals": (_i32, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                _i32]),
     "gsdft_splat_quantities": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p]),
     "gsdft_chart_vjp": (_i32, [_c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p]),
     "gsdft_pairs_workspace_size": (_sz, [_i64, _i64]),

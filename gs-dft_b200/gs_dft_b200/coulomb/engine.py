@@ -127,8 +127,9 @@ class RIJEngine:
             ``beta=None``: no RI-J term (an engine for the nuclear attraction alone).
         rank, world: this device evaluates representatives [n_rep*rank//world, n_rep*(rank+1)//world).
         merge_twins: evaluate each (i,j)/(j,i) pair of a live transposed twin once (same integral).
-        inverse_solve: form [L^-1, L^-T] once (O(n_aux^3)) so each step's solve is two parallel
-            mat-vecs; for engines that run many steps. Off: per-step triangular substitution.
+        inverse_solve: form the packed inverse factor once (O(n_aux^3), n_aux <= 65536) so each
+            step's solve is two parallel mat-vecs; for engines that run many steps. Off: per-step
+            triangular substitution (cuBLAS Dtrsv).
         atoms: optional (n_atoms, 4) float64 device tensor of nuclei (x, y, z, Z) in Bohr: adds the
             screened nuclear attraction E_ne on the same pairs.
     """
@@ -181,11 +182,12 @@ class RIJEngine:
             sizes.append(lib.gsdft_vne_workspace_size(nl))
         self.ws_bytes = max(sizes)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
-        # [L^-1, L^-T] once per refresh: the per-step solve is then two row-parallel mat-vecs
-        self.Linv2 = None
+        # the packed inverse factor [L^-1 lower | L^-T strict upper] once per refresh: the per-step
+        # solve is then two row-parallel mat-vecs over one n_aux^2 matrix
+        self.Linv = None
         if inverse_solve and L is not None and self.n_aux <= SOLVE_INV_MAX:
-            self.Linv2 = e(2, self.n_aux, self.n_aux)
-            lib.call("gsdft_j_solve_inverse", ptr(self.L), self.n_aux, ptr(self.Linv2),
+            self.Linv = e(self.n_aux, self.n_aux)
+            lib.call("gsdft_j_solve_inverse", ptr(self.L), self.n_aux, ptr(self.Linv),
                      stream_handle(dev))
         # Optional CUDA-event brackets around the two integral kernels (recorded on the current
         # stream, the one the kernels are launched on): {"forward": [(start, end)], "vjp": [...]}.
@@ -248,8 +250,8 @@ class RIJEngine:
 
     def solve(self):
         """d = (L L^T)^-1 gamma, E = 1/2 gamma.d (replicated tail)."""
-        if self.Linv2 is not None:
-            lib.call("gsdft_j_solve_inv", ptr(self.Linv2), ptr(self.gamma), self.n_aux,
+        if self.Linv is not None:
+            lib.call("gsdft_j_solve_inv", ptr(self.Linv), ptr(self.gamma), self.n_aux,
                      ptr(self.d), ptr(self.E), ptr(self.ws), self.ws_bytes,
                      stream_handle(self.device))
         else:
@@ -331,10 +333,13 @@ class StepGraph:
             torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         self.graph = torch.cuda.CUDAGraph()
+        n0 = lib.gsdft_kernel_launches()
         with torch.cuda.graph(self.graph):
             self.out = step_fn()
+        # the library's own kernels in the graph (each replay launches exactly these)
+        self.launches = int(lib.gsdft_kernel_launches() - n0)
 
-    def replay(self):
+    def replay(self, phases=None):
         self.graph.replay()
         return self.out
 

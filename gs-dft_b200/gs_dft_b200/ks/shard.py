@@ -104,37 +104,56 @@ class ShardedRIJ:
         g_quat, g_log = self._tail(quat, log_scale)
         return self._outputs(E, d, g_quat, g_log)
 
-    def capture(self, quat, log_scale, centers, C_occ, occ):
+    def capture(self, quat, log_scale, centers, C_occ, occ, warmup: int = 2):
         """The step as CUDA graphs: one graph on a single device; on several, three graphs (the
         compute before, between and after the two allreduces) with the NCCL allreduces issued
-        eagerly in between — collectives are never captured. Inputs are read at the given tensors'
-        addresses: copy new parameters into them before ``replay()``."""
+        eagerly in between — collectives are never captured. ``warmup`` eager steps run first.
+        Inputs are read at the given tensors' addresses: copy new parameters into them before
+        ``replay()``."""
         from ..coulomb.engine import StepGraph
         if self.world == 1:
-            return StepGraph(lambda: self.step(quat, log_scale, centers, C_occ, occ))
-        return _SegmentedStep(self, quat, log_scale, centers, C_occ, occ)
+            return StepGraph(lambda: self.step(quat, log_scale, centers, C_occ, occ),
+                             warmup=warmup)
+        return _SegmentedStep(self, quat, log_scale, centers, C_occ, occ, warmup)
+
+    def phase_events(self):
+        """Six timing events for ``_SegmentedStep.replay(phases)``: recorded on the current stream
+        before the forward, after it, after the gamma allreduce, after the middle segment, after
+        the gradient allreduce and after the chart (five phases)."""
+        import torch
+        return [torch.cuda.Event(enable_timing=True) for _ in range(6)]
 
 
 class _SegmentedStep:
     """Three captured compute segments with eager NCCL allreduces between them."""
 
-    def __init__(self, sh, quat, log_scale, centers, C_occ, occ):
+    def __init__(self, sh, quat, log_scale, centers, C_occ, occ, warmup=2):
         import torch
         from ..coulomb.engine import StepGraph
         # eager warm-up of the whole step (collectives included) on the current stream
-        for _ in range(2):
+        for _ in range(max(warmup, 1)):
             sh.step(quat, log_scale, centers, C_occ, occ)
         torch.cuda.synchronize()
         self.sh = sh
         self.gA = StepGraph(lambda: sh._forward(quat, log_scale, centers, C_occ, occ), warmup=0)
         self.gB = StepGraph(lambda: sh._middle(centers, C_occ, occ), warmup=0)
         self.gC = StepGraph(lambda: sh._tail(quat, log_scale), warmup=0)
+        self.launches = self.gA.launches + self.gB.launches + self.gC.launches
 
-    def replay(self):
+    def replay(self, phases=None):
+        """One step; with ``phases`` (six events from ``phase_events``) each segment and each
+        allreduce is bracketed on the current stream."""
         sh = self.sh
+        rec = (lambda k: phases[k].record()) if phases is not None else (lambda k: None)
+        rec(0)
         gamma = self.gA.replay()
+        rec(1)
         sh._allreduce(gamma)
+        rec(2)
         E, d = self.gB.replay()
+        rec(3)
         sh._allreduce(sh.packed)
+        rec(4)
         g_quat, g_log = self.gC.replay()
+        rec(5)
         return sh._outputs(E, d, g_quat, g_log)

@@ -90,6 +90,22 @@ int64_t gsdft_kernel_launches(void);
  * reference counterpart. */
 int gsdft_dfma_probe(double* out, int64_t iters, int blocks, int threads, gsdft_stream_t stream);
 
+/* Node screening of the integral kernels' 20-node Laplace sums (gsdft_j_forward, its no-allocation
+ * variant, gsdft_j_vjp, gsdft_j_vjp_weighted): along the nodes the exponent of an (aux, pair) term
+ * never decreases and its prefactor never increases, so once a warp's every term has an exponent
+ * 2^-87 below its first node's, the remaining nodes are below the last bit of the sums and the warp
+ * stops. On by default; enabled = 0 evaluates all 20 nodes everywhere (the reference's sum, term by
+ * term). A process-wide setting read at each launch (a CUDA graph keeps the value it was captured
+ * with). No reference counterpart: the reference always sums 20 nodes (gs_dft/coulomb/ri.py:175-185). */
+int gsdft_set_node_screening(int enabled);
+int gsdft_node_screening(void);
+
+/* Node evaluations ((aux, pair) units times the nodes each evaluated, 20 without screening) of the
+ * forward and reverse integral kernels on the current device since the last clear; clear != 0 resets
+ * them. Synchronises the device. For work accounting (the roofline's evaluated FLOP count). No
+ * reference counterpart. */
+int gsdft_node_evals(uint64_t* forward_host, uint64_t* reverse_host, int clear);
+
 /* ---- splat chart ------------------------------------------------------------------------------ */
 
 /* A = R(q) diag(exp l) R(q)^T, N = (8 exp(sum l) / pi^3)^(1/4).
@@ -218,17 +234,19 @@ size_t gsdft_j_solve_workspace_size(int64_t n_aux);
 int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d, double* E,
                   void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
-/* The same solve through inverse factors, for repeated steps on one factor. gsdft_j_solve_inverse
- * (once per refresh) writes Linv2 (2, n_aux, n_aux) = [L^-1, L^-T], row-major, from the lower
- * factor L (n_aux <= GSDFT_SOLVE_INV_MAX). gsdft_j_solve_inv then gives d = L^-T (L^-1 gamma) and
- * E = 1/2 |L^-1 gamma|^2 (= 1/2 gamma.d) as two row-parallel triangular mat-vecs, with no
- * sequential substitution. Same outputs as gsdft_j_solve to rounding (the factor's condition
- * number times the unit roundoff). Replaces, per step, cho_solve in df_coulomb_solve
- * (gs_dft/coulomb/ri.py:472-482). */
-#define GSDFT_SOLVE_INV_MAX 16384
-int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv2, gsdft_stream_t stream);
+/* The same solve through the inverse factor, for repeated steps on one factor.
+ * gsdft_j_solve_inverse (once per refresh) writes Linv (n_aux, n_aux), row-major and packed: its
+ * lower triangle with the diagonal is L^-1 and its strict upper triangle is that of L^-T (the
+ * mirror of the strict lower one), from the lower factor L (n_aux <= GSDFT_SOLVE_INV_MAX; one n_aux^2
+ * buffer, 22.5 GB at n_aux = 53,000). gsdft_j_solve_inv then gives d = L^-T (L^-1 gamma) and
+ * E = 1/2 |L^-1 gamma|^2 (= 1/2 gamma.d) as two row-parallel triangular mat-vecs that read the
+ * packed matrix once, with no sequential substitution and no library call. Same outputs as
+ * gsdft_j_solve to rounding (the factor's condition number times the unit roundoff). Replaces, per
+ * step, cho_solve in df_coulomb_solve (gs_dft/coulomb/ri.py:472-482). */
+#define GSDFT_SOLVE_INV_MAX 65536
+int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv, gsdft_stream_t stream);
 size_t gsdft_j_solve_inv_workspace_size(int64_t n_aux);
-int gsdft_j_solve_inv(const double* Linv2, const double* gamma, int64_t n_aux, double* d, double* E,
+int gsdft_j_solve_inv(const double* Linv, const double* gamma, int64_t n_aux, double* d, double* E,
                       void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
 /* Reverse pass over (representative x aux): with dbar = g_E * d (g_E device scalar, NULL = 1), the

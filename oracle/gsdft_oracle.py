@@ -849,6 +849,10 @@ def c_lib():
         lib.orc_set_threads(len(os.sched_getaffinity(0)))
         lib.orc_gamma.argtypes = [P, ctypes.c_int64, P, P, P, ctypes.c_int64, P]
         lib.orc_vjp.argtypes = [P, ctypes.c_int64, P, P, P, ctypes.c_int64, P]
+        I64, F64 = ctypes.c_int64, ctypes.c_double
+        lib.orc_pairs_count.argtypes = [P, P, P, I64, F64, ctypes.c_int, F64, F64, P, P]
+        lib.orc_pairs_fill.argtypes = [P, P, P, I64, F64, ctypes.c_int, F64, P, P, P, P]
+        lib.orc_metric.argtypes = [P, P, P, I64, P]
         t = np.ascontiguousarray(QUAD_T)
         w = np.ascontiguousarray(QUAD_W)
         lib.orc_set_nodes(t.ctypes.data, w.ctypes.data)
@@ -925,3 +929,42 @@ def energy_and_grad_c(sys_arrays, aux_q, L, pi, pj, valid, want_grad=True):
     out.update(J=J, g_quat=g_quat, g_log_scale=g_log, g_centers=gmu, g_C=gC, gA=gA, gmu=gmu,
                gN=gN)
     return out
+
+
+def neighbor_pairs_c(q, eps, unique=False, band=1e-12):
+    """The unpadded significant list of neighbor_pairs (pad_to=None) with the O(M^2) overlap sweep
+    in C/OpenMP (gsdft_oracle_c.c::orc_pairs_*), for the large configurations. Same decisions as
+    _significant_flat: |S| of the (min, max) orientation against eps, rows lexsorted.
+    Returns (pi, pj, valid, n_sig, n_guard): n_guard counts candidates within relative ``band`` of
+    eps (decisions that a last-bit change in the chart or the exponential could flip)."""
+    lib = c_lib()
+    A, mu, N = q
+    M = int(mu.shape[0])
+    A9 = np.ascontiguousarray(A.reshape(M, 9), dtype=np.float64)
+    mu = np.ascontiguousarray(mu, dtype=np.float64)
+    N = np.ascontiguousarray(N, dtype=np.float64)
+    counts = np.zeros(M, np.int64)
+    near = np.zeros(M, np.int64)
+    pi15 = PI ** 1.5
+    lib.orc_pairs_count(A9.ctypes.data, mu.ctypes.data, N.ctypes.data, M, float(eps), int(unique),
+                        pi15, float(band), counts.ctypes.data, near.ctypes.data)
+    offsets = np.zeros(M, np.int64)
+    np.cumsum(counts[:-1], out=offsets[1:])
+    n_sig = int(counts.sum())
+    pi = np.empty(n_sig, np.int32)
+    pj = np.empty(n_sig, np.int32)
+    absS = np.empty(n_sig, np.float64)
+    lib.orc_pairs_fill(A9.ctypes.data, mu.ctypes.data, N.ctypes.data, M, float(eps), int(unique),
+                       pi15, offsets.ctypes.data, pi.ctypes.data, pj.ctypes.data, absS.ctypes.data)
+    return pi, pj, pair_weights(pi, pj, unique), n_sig, int(near.sum())
+
+
+def aux_metric_c(beta, R, KN):
+    """aux_metric with the n^2 loop in C/OpenMP (C libm erf): the CPU baseline's refresh at the
+    large configurations."""
+    lib = c_lib()
+    beta, R, KN = (np.ascontiguousarray(a, dtype=np.float64) for a in (beta, R, KN))
+    n = int(beta.shape[0])
+    V = np.empty((n, n))
+    lib.orc_metric(beta.ctypes.data, R.ctypes.data, KN.ctypes.data, n, V.ctypes.data)
+    return V

@@ -128,3 +128,105 @@ void orc_vjp(const double* pr, int64_t n_pairs, const double* beta, const double
     for (int c = 0; c < 6; ++c) o[7 + c] = SZ[c];
   }
 }
+
+/* ---- significant-pair list (gs_dft/screening/pairs.py:50-118, 225-315, 342-345) ---------------------
+ * The same screening as gsdft_oracle.py::_significant_flat, in C for the large configurations: |S| of
+ * the (min, max) orientation, S = N_i N_j exp(-d.A_i A_hat^-1 A_j d) pi^1.5 / sqrt(det A_hat), with
+ * the 3x3 algebra of gs_dft/integrals/linalg3.py:17-51 in the oracle's operation order (built with
+ * FMA contraction off, so each operation rounds once as NumPy's does). A9 (M,9) row-major, mu (M,3),
+ * N (M) come from the NumPy oracle's chart. Rows are independent (OpenMP over i). */
+static double det3c(const double* A) {
+  return A[0] * (A[4] * A[8] - A[5] * A[7]) - A[1] * (A[3] * A[8] - A[5] * A[6]) +
+         A[2] * (A[3] * A[7] - A[4] * A[6]);
+}
+
+static void solve3c(const double* A, const double* b, double* x) {
+  double c[9];
+  c[0] = A[4] * A[8] - A[5] * A[7];
+  c[1] = A[2] * A[7] - A[1] * A[8];
+  c[2] = A[1] * A[5] - A[2] * A[4];
+  c[3] = A[5] * A[6] - A[3] * A[8];
+  c[4] = A[0] * A[8] - A[2] * A[6];
+  c[5] = A[2] * A[3] - A[0] * A[5];
+  c[6] = A[3] * A[7] - A[4] * A[6];
+  c[7] = A[1] * A[6] - A[0] * A[7];
+  c[8] = A[0] * A[4] - A[1] * A[3];
+  const double det = det3c(A);
+  for (int k = 0; k < 3; ++k) x[k] = (c[3 * k] * b[0] + c[3 * k + 1] * b[1] + c[3 * k + 2] * b[2]) / det;
+}
+
+static double abs_overlap(const double* A9, const double* mu, const double* N, int64_t i, int64_t j,
+                          double pi15) {
+  const int64_t lo = i < j ? i : j, hi = i < j ? j : i;
+  const double *Ai = A9 + 9 * lo, *Aj = A9 + 9 * hi, *mi = mu + 3 * lo, *mj = mu + 3 * hi;
+  double Ah[9], d[3], Ajd[3], s[3], x[3];
+  for (int k = 0; k < 9; ++k) Ah[k] = Ai[k] + Aj[k];
+  for (int k = 0; k < 3; ++k) d[k] = mi[k] - mj[k];
+  for (int k = 0; k < 3; ++k) Ajd[k] = Aj[3 * k] * d[0] + Aj[3 * k + 1] * d[1] + Aj[3 * k + 2] * d[2];
+  solve3c(Ah, Ajd, s);
+  for (int k = 0; k < 3; ++k) x[k] = Ai[3 * k] * s[0] + Ai[3 * k + 1] * s[1] + Ai[3 * k + 2] * s[2];
+  const double quad = d[0] * x[0] + d[1] * x[1] + d[2] * x[2];
+  const double NK = N[lo] * N[hi] * exp(-quad);
+  return fabs(NK * pi15 / sqrt(det3c(Ah)));
+}
+
+/* counts[i] = number of j (j >= i when unique) with |S_ij| > eps; near[i] = number of those within
+ * relative `band` of eps either side (the guard band: decisions a last-bit change could flip). */
+void orc_pairs_count(const double* A9, const double* mu, const double* N, int64_t M, double eps,
+                     int unique, double pi15, double band, int64_t* counts, int64_t* near) {
+#pragma omp parallel for schedule(dynamic, 8)
+  for (int64_t i = 0; i < M; ++i) {
+    int64_t c = 0, nb = 0;
+    for (int64_t j = unique ? i : 0; j < M; ++j) {
+      const double s = abs_overlap(A9, mu, N, i, j, pi15);
+      c += s > eps;
+      nb += fabs(s / eps - 1.0) < band;
+    }
+    counts[i] = c;
+    near[i] = nb;
+  }
+}
+
+/* The lexsorted significant list: row i's entries start at offsets[i] (exclusive prefix of counts). */
+void orc_pairs_fill(const double* A9, const double* mu, const double* N, int64_t M, double eps,
+                    int unique, double pi15, const int64_t* offsets, int32_t* pi, int32_t* pj,
+                    double* absS) {
+#pragma omp parallel for schedule(dynamic, 8)
+  for (int64_t i = 0; i < M; ++i) {
+    int64_t o = offsets[i];
+    for (int64_t j = unique ? i : 0; j < M; ++j) {
+      const double s = abs_overlap(A9, mu, N, i, j, pi15);
+      if (s > eps) {
+        pi[o] = (int32_t)i;
+        pj[o] = (int32_t)j;
+        absS[o] = s;
+        ++o;
+      }
+    }
+  }
+}
+
+/* ---- aux metric (gs_dft/coulomb/ri.py:63-76, 267-275) -----------------------------------------------
+ * V_PQ = KN_P KN_Q 2 pi^2.5 / (b_P b_Q sqrt(b_P + b_Q)) F0(b_P b_Q / (b_P + b_Q) |R_P - R_Q|^2),
+ * F0(T) = 1/2 sqrt(pi/T) erf(sqrt T) (Taylor below 1e-8), as gsdft_oracle.py::coulomb_block; C libm's
+ * erf, so entries may differ from the NumPy oracle's in the last bits. For the CPU baseline's refresh
+ * at sizes where the NumPy temporaries (n^2 x 3 doubles) are too large. */
+static double boys0c(double T) {
+  if (T < 1e-8) return 1.0 - T / 3.0 + T * T / 10.0 - T * T * T / 42.0;
+  return 0.5 * sqrt(3.141592653589793 / T) * erf(sqrt(T));
+}
+
+void orc_metric(const double* beta, const double* R, const double* KN, int64_t n, double* V) {
+  const double c = 2.0 * pow(3.141592653589793, 2.5);
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int64_t p = 0; p < n; ++p) {
+    for (int64_t q = 0; q < n; ++q) {
+      const double g1 = beta[p], g2 = beta[q];
+      const double gab = g1 * g2, gsum = g1 + g2;
+      const double dx = R[3 * p] - R[3 * q], dy = R[3 * p + 1] - R[3 * q + 1],
+                   dz = R[3 * p + 2] - R[3 * q + 2];
+      const double T = gab / gsum * (dx * dx + dy * dy + dz * dz);
+      V[p * n + q] = (KN[p] * KN[q]) * (c / (gab * sqrt(gsum)) * boys0c(T));
+    }
+  }
+}

@@ -148,7 +148,7 @@ def test_gamma_energy_vs_reference(g, case):
 
 @pytest.mark.parametrize("cfg,M", [(1, None), (2, 1500)])
 def test_inverse_factor_solve(g, cfg, M):
-    """gsdft_j_solve_inv (two triangular mat-vecs on [L^-1, L^-T]) against cho_solve on the same
+    """gsdft_j_solve_inv (two triangular mat-vecs on the packed [L^-1 | L^-T]) against cho_solve on the same
     factor (copied to the host), against the substitution path, and bitwise across calls;
     oversize n is rejected. The factor is the device's own: cond(V + lam I) reaches ~1e9 here, so
     last-ulp differences between two metrics move d far more than the solve method does (the
@@ -167,15 +167,19 @@ def test_inverse_factor_solve(g, cfg, M):
     gam_h = V @ rng.standard_normal(n) + np.abs(rng.standard_normal(n))
     E_ref, d_ref = O.df_coulomb_solve(gam_h, Lo)
     gam = dev(gam_h)
-    Linv2 = torch.empty((2, n, n), dtype=torch.float64, device="cuda")
+    Linv = torch.empty((n, n), dtype=torch.float64, device="cuda")
     st = stream_handle(gam.device)
-    lib.call("gsdft_j_solve_inverse", ptr(L), n, ptr(Linv2), st)
+    lib.call("gsdft_j_solve_inverse", ptr(L), n, ptr(Linv), st)
+    # packed: lower triangle = L^-1, strict upper = its mirror (L^-T)
+    Lih = host(Linv)
+    np.testing.assert_array_equal(np.triu(Lih, 1), np.tril(Lih, -1).T)
+    close(np.tril(Lih) @ Lo, np.eye(n), rtol=0, atol_rel=1e-6)
     wb = lib.gsdft_j_solve_inv_workspace_size(n)
     ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
     outs = []
     for _ in range(2):
         d_, E_ = torch.empty(n, dtype=torch.float64, device="cuda"), torch.empty(1, dtype=torch.float64, device="cuda")
-        lib.call("gsdft_j_solve_inv", ptr(Linv2), ptr(gam), n, ptr(d_), ptr(E_), ptr(ws), wb, st)
+        lib.call("gsdft_j_solve_inv", ptr(Linv), ptr(gam), n, ptr(d_), ptr(E_), ptr(ws), wb, st)
         outs.append((host(d_), float(E_)))
     close(outs[0][0], d_ref)
     close(outs[0][1], E_ref)
@@ -185,7 +189,7 @@ def test_inverse_factor_solve(g, cfg, M):
     close(outs[0][0], host(d2))
     close(outs[0][1], float(E2))
     with pytest.raises(g._lib.GsdftError):
-        lib.call("gsdft_j_solve_inverse", ptr(L), 16385, ptr(Linv2), st)
+        lib.call("gsdft_j_solve_inverse", ptr(L), g._lib.SOLVE_INV_MAX + 1, ptr(Linv), st)
 
 
 def _oracle_grad(d, pi, pj, v):
