@@ -118,7 +118,7 @@ __global__ void chart_vjp_kernel(const double* __restrict__ quat,
 using namespace gsdft;
 
 extern "C" const char* gsdft_last_error_string(void) { return g_err; }
-extern "C" int gsdft_version(void) { return 1; }
+extern "C" int gsdft_version(void) { return GSDFT_ABI_VERSION; }
 
 extern "C" int gsdft_splat_quantities(const double* quat, const double* log_scale, int64_t M,
                                       double* A9, double* N, gsdft_stream_t stream) {

@@ -333,8 +333,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // evaluates ~10 of the 20 nodes, at configuration 4 ~7; at a compact molecule all 20.
 // gsdft_set_node_screening(0) turns it off (every node evaluated, as the reference does).
 // ------------------------------------------------------------------------------------------------
+// The warp checks after node kNodeSkipFirst and then every kNodeSkipEvery nodes: a check is a vote
+// and a branch, which also ends the compiler's interleaving of consecutive nodes, so checking
+// every node costs ~10% where nothing can be skipped (compact molecules).
+#ifndef GSDFT_SKIP_FIRST
+#define GSDFT_SKIP_FIRST 5
+#endif
+#ifndef GSDFT_SKIP_EVERY
+#define GSDFT_SKIP_EVERY 2
+#endif
 constexpr double kNodeSkipLog2 = 87.0;  // 2^-87 = e^-60.3
-constexpr int kNodeSkipFirst = 3;       // nodes 0..3 are always evaluated
+constexpr int kNodeSkipFirst = GSDFT_SKIP_FIRST;  // nodes 0..kNodeSkipFirst are always evaluated
+constexpr int kNodeSkipEvery = GSDFT_SKIP_EVERY;
+__host__ __device__ constexpr bool node_check(int n) {
+  return n >= kNodeSkipFirst && (n - kNodeSkipFirst) % kNodeSkipEvery == 0 && n + 1 < 20;
+}
 // Host: the skip threshold the launches pass (kNodeSkipLog2, or +inf when screening is off).
 double node_skip_threshold();
 

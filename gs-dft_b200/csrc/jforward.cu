@@ -250,7 +250,7 @@ __global__ void GSDFT_FW_BOUNDS
 #pragma unroll
       for (int n = 0; n < GSDFT_NQUAD; ++n) {
         const double t2 = kQuadT2[n];
-        bool far = true;
+        bool far = node_check(n);  // tested at the check nodes only (the exponent is monotone)
 #pragma unroll
         for (int p = 0; p < kFwNP; ++p) {
           const double G0 = fma(t2, h[p][0], g[p][0]);
@@ -265,10 +265,10 @@ __global__ void GSDFT_FW_BOUNDS
           const double ew = wexp2<kFwBits>(x, t2, etab + (n << kFwBits));
           coul[p] = fma(y, ew, coul[p]);
           if (n == 0) e0[p] = x * t2;
-          far = far && fma(x, t2, -e0[p]) < -skip2;
+          if (node_check(n)) far = far && fma(x, t2, -e0[p]) < -skip2;
         }
         // node screening (warp-uniform): every later node is below the last bit of every lane's sum
-        if (n >= kNodeSkipFirst && n + 1 < GSDFT_NQUAD && __all_sync(0xffffffffu, far)) {
+        if (node_check(n) && __all_sync(0xffffffffu, far)) {
           nodes = n + 1;
           break;
         }

@@ -157,8 +157,7 @@ __global__ void GSDFT_VJP_BOUNDS
         Z[4] = fma(h0, iG2, Z[4]);
         Z[5] = fma(h1, iG2, Z[5]);
         // node screening (warp-uniform): every later node is below the last bit of every lane's sums
-        if (n >= kNodeSkipFirst && n + 1 < GSDFT_NQUAD &&
-            __all_sync(0xffffffffu, fma(x, t2, -e0) < -skip2)) {
+        if (node_check(n) && __all_sync(0xffffffffu, fma(x, t2, -e0) < -skip2)) {
           nodes = n + 1;
           break;
         }

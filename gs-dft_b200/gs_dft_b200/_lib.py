@@ -17,6 +17,7 @@ REC_FIELDS = 18
 VJP_FIELDS = 13
 SIDE_FIELDS = 20
 SOLVE_INV_MAX = 65536   # GSDFT_SOLVE_INV_MAX
+ABI_VERSION = 2         # GSDFT_ABI_VERSION
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -116,6 +117,11 @@ class _Lib:
                 f = getattr(h, name)
                 f.restype = res
                 f.argtypes = args
+            if h.gsdft_version() != ABI_VERSION:
+                raise RuntimeError(
+                    f"{LIB_PATH} implements ABI version {h.gsdft_version()}, this package needs "
+                    f"{ABI_VERSION}: the library is stale, rebuild it with "
+                    f"`python -m gs_dft_b200._build`")
             self._h = h
         return self._h
 

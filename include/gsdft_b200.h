@@ -72,6 +72,10 @@ enum {
 
 #define GSDFT_SIDE_FIELDS 20 /* per live pair: i-side (gA6, gmu3, gN) then j-side */
 
+/* Version of this ABI (entry points, argument meaning, record layouts); gsdft_version() returns it.
+ * A host binding checks it at load time so that a library built from older sources is refused. */
+#define GSDFT_ABI_VERSION 2
+
 const char* gsdft_last_error_string(void);
 int gsdft_version(void);
 

@@ -5,8 +5,9 @@
    golden systems.
 2. Node screening: the integral kernels stop a warp's 20-node Laplace sum once every one of its
    (aux, pair) terms has an exponent more than 2^-kNodeSkipLog2 below its first node's
-   (``csrc/common.cuh``). Emulated here per (aux, pair) — which stops no later than a warp, so it
-   truncates at least as much — with the kernels' constants, on (aux, pair) samples of the water
+   (``csrc/common.cuh``), checked after the same nodes. Emulated here per (aux, pair) — which stops
+   no later than a warp, so it truncates at least as much — with the kernels' constants, on (aux,
+   pair) samples of the water
    clusters: every node sum the kernels accumulate (the value and the reverse pass's weighted sums)
    is unchanged to below one rounding.
 """
@@ -21,10 +22,12 @@ from conftest import ROOT, load_golden
 
 
 def _kernel_constants():
+    """(threshold in log2 units, first checked node, check cadence) as the kernels are built."""
     src = open(os.path.join(ROOT, "gs-dft_b200", "csrc", "common.cuh")).read()
     thr = float(re.search(r"kNodeSkipLog2\s*=\s*([0-9.]+)", src).group(1))
-    first = int(re.search(r"kNodeSkipFirst\s*=\s*(\d+)", src).group(1))
-    return thr, first
+    first = int(re.search(r"#define GSDFT_SKIP_FIRST (\d+)", src).group(1))
+    every = int(re.search(r"#define GSDFT_SKIP_EVERY (\d+)", src).group(1))
+    return thr, first, every
 
 
 @pytest.mark.parametrize("case", ["ref_rand24.npz", "ref_rand48.npz", "ref_co2.npz"])
@@ -79,7 +82,9 @@ def _node_terms(beta, R, lam, U, P):
 @pytest.mark.parametrize("cfg", [2, 3])
 def test_node_screening_changes_no_sum(cfg):
     from gs_dft_b200.systems import make_config
-    thr, first = _kernel_constants()
+    thr, first, every = _kernel_constants()
+    checked = np.zeros(O.QUAD_T.size, bool)
+    checked[first:O.QUAD_T.size - 1:every] = True
     s = make_config(cfg)
     q = O.full_quantities(s.quat, s.log_scale, s.centers)
     la, R = O.init_product_aux(q)
@@ -99,9 +104,9 @@ def test_node_screening_changes_no_sum(cfg):
     for chunk in range(4):
         aux = rng.choice(M, 96, replace=False)
         ex, terms = _node_terms(beta[aux], R[aux], lam, U, P)
-        # the first node n >= first at which the exponent is thr below node 0's: nodes after it drop
+        # the first checked node at which the exponent is thr below node 0's: nodes after it drop
         far = (ex - ex[0]) < -thr
-        far[:first] = False
+        far[~checked] = False
         stop = np.where(far.any(0), far.argmax(0) + 1, ex.shape[0])       # nodes evaluated
         keep = np.arange(ex.shape[0])[:, None, None] < stop[None]
         full = terms.sum(0)
