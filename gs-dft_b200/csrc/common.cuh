@@ -97,6 +97,10 @@ inline int best_splits(int64_t base, int64_t cap, int64_t max_s) {
   return 1;
 }
 
+// Streaming multiprocessors of the device current at the first call (148 on B200); a thread-safe
+// static, queried once per process.
+int device_sms();
+
 inline int grid_1d(int64_t n, int block) {
   int64_t g = (n + block - 1) / block;
   if (g < 1) g = 1;
@@ -236,7 +240,11 @@ __device__ __forceinline__ void load_wexp2_tables(double* dst) {
 // number of correct bits of the seed.
 __device__ __forceinline__ double rsqrt_pos(double p) {
   double y0;
+#if GSDFT_RSQRT_SEED_F32
+  y0 = (double)rsqrtf(__double2float_rn(p));
+#else
   asm("rsqrt.approx.ftz.f64 %0, %1;" : "=d"(y0) : "d"(p));
+#endif
   double t = p * y0;
   double e = fma(-t, y0, 1.0);
   double c = fma(0.375, e, 0.5);

@@ -145,15 +145,12 @@ __global__ void __launch_bounds__(256)
 }
 
 static int exact_splits(int64_t n) {
-  static int sms = 0, per_sm = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, exact_j_kernel, kXThreads, kXDynSmem);
-    if (per_sm <= 0) per_sm = 1;
-  }
+  static const int per_sm = [] {
+    int v = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, exact_j_kernel, kXThreads, kXDynSmem);
+    return v > 0 ? v : 1;
+  }();
+  const int sms = device_sms();
   const int64_t tiles = (n + kXThreads - 1) / kXThreads;
   const int64_t max_s = imin64(64, imax64(1, n / kXTile));
   return best_splits(tiles, (int64_t)sms * per_sm, max_s);

@@ -303,30 +303,18 @@ __global__ void sum_splits_kernel(const double* __restrict__ partial, int S, int
   out[P] = (a0 + a1) + (a2 + a3);
 }
 
-static int num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  return sms;
-}
-
 // Pair splits of the forward grid: aux tiles x S CTAs filling whole waves of resident CTAs, with at
-// least two pair tiles per split.
+// least two pair tiles per split. The occupancy query runs once (a thread-safe static).
 static int forward_splits(int64_t n_live, int64_t n_aux) {
-  static int per_sm = 0;
-  if (!per_sm) {
+  static const int per_sm = [] {
+    int v = 0;
     cudaFuncSetAttribute(j_forward_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kFwDynSmem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, j_forward_kernel, kFwThreads,
-                                                  kFwDynSmem);
-    if (per_sm <= 0) per_sm = 1;
-  }
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, j_forward_kernel, kFwThreads, kFwDynSmem);
+    return v > 0 ? v : 1;
+  }();
   int64_t aux_tiles = (n_aux + kFwThreads - 1) / kFwThreads;
-  int64_t cap = (int64_t)num_sms() * per_sm;
+  int64_t cap = (int64_t)device_sms() * per_sm;
   int64_t max_s = imin64(4096, imax64(1, n_live / (2 * kFwTile)));
   return best_splits(aux_tiles, cap, max_s);
 }

@@ -460,31 +460,21 @@ __global__ void __launch_bounds__(kDgWarps * 32)
   }
 }
 
-static int vjp_num_sms() {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (sms <= 0) sms = 148;
-  }
-  return sms;
-}
-
 // Aux splits: pair tiles x S CTAs filling whole waves of resident CTAs (S <= 8, since the partial
-// sums take S x n_live x 13 doubles).
+// sums take S x n_live x 13 doubles). The occupancy query runs once per template (a thread-safe
+// static).
 template <bool kW>
 static int vjp_splits(int64_t n_live, int64_t n_aux) {
-  static int per_sm = 0;
-  if (!per_sm) {
+  static const int per_sm = [] {
+    int v = 0;
     cudaFuncSetAttribute(j_vjp_kernel<kW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kVjpDynSmem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, j_vjp_kernel<kW>, kVjpThreads,
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, j_vjp_kernel<kW>, kVjpThreads,
                                                   kVjpDynSmem);
-    if (per_sm <= 0) per_sm = 1;
-  }
+    return v > 0 ? v : 1;
+  }();
   int64_t tiles = (n_live + kVjpThreads - 1) / kVjpThreads;
-  int64_t cap = (int64_t)vjp_num_sms() * per_sm;
+  int64_t cap = (int64_t)device_sms() * per_sm;
   int64_t max_s = imin64(8, imax64(1, n_aux / kVjpTile));
   return best_splits(tiles, cap, max_s);
 }

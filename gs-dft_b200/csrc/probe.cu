@@ -10,6 +10,16 @@ static std::atomic<int> g_node_screening{1};
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+int device_sms() {
+  static const int sms = [] {
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v > 0 ? v : 148;
+  }();
+  return sms;
+}
+
 double node_skip_threshold() {
   return g_node_screening.load(std::memory_order_relaxed) ? kNodeSkipLog2 : (double)INFINITY;
 }

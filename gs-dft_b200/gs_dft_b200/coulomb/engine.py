@@ -193,6 +193,9 @@ class RIJEngine:
         # stream, the one the kernels are launched on): {"forward": [(start, end)], "vjp": [...]}.
         self.timing = False
         self.events = {"forward": [], "vjp": [], "vne": []}
+        # token of the forward whose pair records, gamma and d the buffers hold (a backward after
+        # another forward on this engine must re-run its own forward first)
+        self.last_forward = None
 
     def _bracket(self, name):
         if not self.timing:
@@ -239,6 +242,7 @@ class RIJEngine:
         s = stream_handle(self.device)
         nl = self.plan.n_rep
         self.prepare(quat, log_scale, centers, C_occ, occ)
+        self.last_forward = object()
         if not self.rij:
             return None
         end = self._bracket("forward")

@@ -109,6 +109,9 @@ class RIKEngine:
                  ptr(self.gN), s)
         lib.call("gsdft_chart_vjp", ptr(quat), ptr(log_scale), ptr(self.gA6), ptr(self.gN),
                  self.M, ptr(self.g_quat), ptr(self.g_log), s)
+        # gsdft_k_backward overwrote the workspace's integral block with its weights: a further
+        # backward must re-run the forward first
+        self.last_forward = None
         return self.g_quat, self.g_log, self.gmu, self.g_C
 
     def step(self, quat, log_scale, centers, C, grad=True, g_E=None):

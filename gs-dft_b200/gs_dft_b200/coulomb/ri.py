@@ -118,7 +118,7 @@ class _ScreenedDFEnergy(torch.autograd.Function):
         C, oc = C_occ.detach().to(F64).contiguous(), occ.detach().to(F64).contiguous()
         eng.forward_local(q, ls, c, C, oc)
         E, _ = eng.solve()
-        ctx.eng = eng
+        ctx.eng, ctx.token = eng, eng.last_forward
         ctx.save_for_backward(q, ls, c, C, oc)
         return E[0].clone()
 
@@ -127,6 +127,10 @@ class _ScreenedDFEnergy(torch.autograd.Function):
         q, ls, c, C, oc = ctx.saved_tensors
         eng = ctx.eng
         gE = gE.detach().to(F64).reshape(1).contiguous()
+        if eng.last_forward is not ctx.token:   # another forward used the engine since
+            eng.forward_local(q, ls, c, C, oc)
+            eng.solve()
+            ctx.token = eng.last_forward
         eng.backward_local(c, C, oc, g_E=gE)
         g_quat, g_log = eng.chart(q, ls)
         g_C = eng.g_C[:, :eng.n_occ].clone()

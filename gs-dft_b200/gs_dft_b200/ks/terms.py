@@ -95,6 +95,12 @@ class ScreenedExactCoulomb:
 
     def energy(self, basis, C_orth, P, occ, state):
         from ..coulomb.stream import screened_coulomb_energy
+        if torch.is_grad_enabled() and any(
+                t.requires_grad for t in (basis.quat, basis.log_scale, basis.centers, C_orth)):
+            raise NotImplementedError(
+                "ScreenedExactCoulomb on the B200 path gives the value of E_J only; its gradient "
+                "is not built. Evaluate it under torch.no_grad() (or on detached inputs), or train "
+                "with the density-fitted Coulomb (df()).")
         pi, pj, valid = state.pairs
         e_j = screened_coulomb_energy(basis, C_orth, occ, pi, pj, valid=valid,
                                       bra_chunk=self.chunk)

@@ -7,8 +7,16 @@
  *
  * Conventions (every entry point):
  *   - all pointers are DEVICE pointers unless the name ends in _host; FP64 arrays are row-major;
- *   - buffers are owned and allocated by the caller; no entry point allocates device memory. Scratch
- *     comes from an explicit workspace whose size the matching *_workspace_size() returns;
+ *   - buffers are owned and allocated by the caller, and scratch comes from an explicit workspace
+ *     whose size the matching *_workspace_size() returns. No entry point allocates device memory for
+ *     its data, with one exception: the entry points that call cuBLAS / cuSOLVER
+ *     (gsdft_aux_cholesky_workspace_size, gsdft_aux_cholesky, gsdft_j_solve, gsdft_j_solve_inverse,
+ *     gsdft_k_forward, gsdft_k_backward) create that library's handle for the current device on
+ *     their first call there, and handle creation allocates. Make that first call on each device
+ *     before any stream capture, and from a context that may allocate (outside a framework's
+ *     preallocated pool); later calls allocate nothing. The per-step path of the RI-J engine
+ *     (gsdft_pair_prep, gsdft_j_forward, gsdft_j_solve_inv, gsdft_j_vjp and the chain) calls no
+ *     library;
  *   - work is enqueued on `stream` (the last argument). Only gsdft_pairs_count / gsdft_pairs_build /
  *     gsdft_pair_plan / gsdft_aux_cholesky synchronise the stream, to read back integers (pair counts,
  *     the factorisation status), exactly where the reference syncs to the host

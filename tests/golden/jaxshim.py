@@ -22,6 +22,7 @@ differences of the executed reference energy.
 from __future__ import annotations
 
 import importlib
+import os
 import math
 import sys
 import types
@@ -29,7 +30,7 @@ import types
 import numpy as np
 from scipy.special import erf
 
-REFERENCE_ROOT = "/root/reference"
+REFERENCE_ROOT = os.environ.get("GSDFT_REFERENCE_ROOT", "/root/reference")
 
 
 class JArr(np.ndarray):

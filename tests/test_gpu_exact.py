@@ -69,3 +69,18 @@ def test_exact_unique_list_and_twin_merge(g):
     st = g.SplatState(pairs=(pi, pj, v))
     e_j, e_k = ks_term.energy(s, C, None, occ, st)
     assert float(e_j) == float(Em) and float(e_k) == 0.0
+
+
+def test_screened_exact_term_refuses_a_gradient(g):
+    """The exact E_J has no reverse pass on this path: with inputs that require grad the term
+    raises instead of returning an energy whose gradient would silently be missing."""
+    d = load_golden("ref_rand24.npz")
+    s = g.Splat(dev(d["quat"]), dev(d["log_scale"]), dev(d["centers"]).requires_grad_(True))
+    st = g.SplatState(pairs=(dev(d["pad_pi"], torch.int32), dev(d["pad_pj"], torch.int32),
+                             dev(d["pad_v"], torch.bool)))
+    C, occ = dev(d["C_occ"]), dev(d["occ"])
+    with pytest.raises(NotImplementedError):
+        g.ScreenedExactCoulomb().energy(s, C, None, occ, st)
+    with torch.no_grad():
+        e_j, _ = g.ScreenedExactCoulomb().energy(s, C, None, occ, st)
+    assert np.isfinite(float(e_j))

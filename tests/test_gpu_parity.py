@@ -410,3 +410,36 @@ def test_graph_replay_matches_eager_step(g):
     for k in eager2:
         np.testing.assert_array_equal(host(out[k]), eager2[k])
     assert not np.array_equal(eager2["E"], eager["E"])
+
+
+def test_two_forwards_then_backward_of_the_first(g):
+    """The engine a refresh state caches serves every forward: a backward after a second forward
+    at other orbitals re-runs its own forward first, so E(C1) and E(C2) in one loss get their own
+    gradients (checked against the oracle)."""
+    d = load_golden("ref_rand48.npz")
+    pi, pj, v = d["pad_pi"], d["pad_pj"], d["pad_v"]
+    s = splats(g, d)
+    ks = g.CoulombKS(coulomb=g.df(), screen=g.pairlist(eps=float(d["eps"])))
+    st = g.refresh(ks, s, pad_to=int(pi.size))
+    C1 = d["C_occ"]
+    C2 = np.linalg.qr(C1 + 0.05 * np.random.default_rng(1).standard_normal(C1.shape))[0]
+    Ct1, Ct2 = dev(C1).requires_grad_(True), dev(C2).requires_grad_(True)
+    occ = dev(d["occ"])
+    E1 = ks(g.SplatModel(basis=s, C=Ct1, occupations=occ), st)
+    E2 = ks(g.SplatModel(basis=s, C=Ct2, occupations=occ), st)
+    E1.backward()                 # the engine's buffers hold E2's forward at this point
+    q = O.full_quantities(d["quat"], d["log_scale"], d["centers"])
+    opi, opj, ov, _ = O.neighbor_pairs(q, eps=float(d["eps"]), pad_to=int(pi.size))
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    Lo = O.aux_cholesky(O.aux_metric(*aq), float(d["lam"]))
+    for Ch, Et, Ctg in ((C1, E1, Ct1), (C2, E2, Ct2)):
+        ref = O.energy_and_grad((d["quat"], d["log_scale"], d["centers"], Ch, d["occ"]), aq, Lo,
+                                opi, opj, ov)
+        close(float(Et), ref["E"])
+        if Ctg is Ct1:
+            close(host(Ctg.grad), ref["g_C"])
+    E2.backward()
+    ref2 = O.energy_and_grad((d["quat"], d["log_scale"], d["centers"], C2, d["occ"]), aq, Lo,
+                             opi, opj, ov)
+    close(host(Ct2.grad), ref2["g_C"])
