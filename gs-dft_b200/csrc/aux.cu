@@ -1,12 +1,7 @@
 // Product auxiliary basis, its Coulomb metric, the metric's Cholesky factor and the per-step solve.
 // Reference: gs_dft/basis/isotropic.py:22-39,81-116 (aux); gs_dft/coulomb/ri.py:63-123,267-275
-// (metric), :243-264 (factor), :472-482 (solve).
-#include <cublas_v2.h>
-#include <cusolverDn.h>
-
-#include <mutex>
-#include <unordered_map>
-
+// (metric), :243-264 (factor), :472-482 (solve). The factorisations themselves (Cholesky, the
+// factor's inverse, blocked substitution) are the DMMA routines of dense.cu.
 #include "common.cuh"
 
 namespace gsdft {
@@ -83,18 +78,6 @@ __global__ void aux_metric_kernel(const double* __restrict__ beta, const double*
   }
 }
 
-__global__ void shift_diag_kernel(double* V, int64_t n, double lam) {
-  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (i < n) V[i * n + i] += lam;
-}
-
-// Zero the strict upper triangle of a row-major matrix.
-__global__ void zero_upper_kernel(double* V, int64_t n) {
-  int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (q >= n) return;
-  for (int64_t p = blockIdx.y; p < q; p += gridDim.y) V[p * n + q] = 0.0;
-}
-
 // E = 1/2 gamma . d, one block, fixed-order tree: deterministic.
 __global__ void half_dot_kernel(const double* __restrict__ g, const double* __restrict__ d,
                                 int64_t n, double* E) {
@@ -126,11 +109,6 @@ __global__ void half_dot_kernel(const double* __restrict__ g, const double* __re
 // One warp per row; each lane keeps four partial sums; the warp's shuffle tree fixes the summation
 // order (bitwise reproducible).
 constexpr int kTriWarps = 4;
-
-__global__ void identity_kernel(double* X, int64_t n) {
-  const int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (k < n * n) X[k] = (k / n == k % n) ? 1.0 : 0.0;
-}
 
 // In place, X[c][r] = X[r][c] for r > c: the strict lower triangle mirrored into the strict upper
 // one, through 32 x 33 shared tiles (coalesced both ways). A block reads one lower (or diagonal)
@@ -199,31 +177,9 @@ __global__ void __launch_bounds__(kTriWarps * 32)
   }
 }
 
-// Library handles, one per device, created on first use.
-struct Handles {
-  cusolverDnHandle_t solver = nullptr;
-  cublasHandle_t blas = nullptr;
-};
-
-static std::mutex g_mu;
-static std::unordered_map<int, Handles> g_handles;
-
-static int get_handles(Handles** out) {
-  int dev = 0;
-  GSDFT_CUDA(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lk(g_mu);
-  Handles& h = g_handles[dev];
-  if (!h.solver) {
-    if (cusolverDnCreate(&h.solver) != CUSOLVER_STATUS_SUCCESS)
-      return fail(GSDFT_ERR_LINALG, "cusolverDnCreate failed");
-  }
-  if (!h.blas) {
-    if (cublasCreate(&h.blas) != CUBLAS_STATUS_SUCCESS)
-      return fail(GSDFT_ERR_LINALG, "cublasCreate failed");
-  }
-  *out = &h;
-  return GSDFT_OK;
-}
+int potrf_dmma(double* V, int64_t n, double lam, double* Dinv, int* info_dev, cudaStream_t st);
+int trtri_dmma(const double* L, int64_t n, double* X, cudaStream_t st);
+int trsv_llt(const double* L, int64_t n, double* d, cudaStream_t st);
 
 }  // namespace gsdft
 
@@ -269,13 +225,11 @@ extern "C" int gsdft_aux_metric(const double* beta, const double* R, const doubl
 }
 
 extern "C" size_t gsdft_aux_cholesky_workspace_size(int64_t n_aux) {
-  Handles* h = nullptr;
-  if (get_handles(&h)) return 0;
-  int lwork = 0;
-  if (cusolverDnDpotrf_bufferSize(h->solver, CUBLAS_FILL_MODE_UPPER, (int)n_aux, nullptr,
-                                  (int)n_aux, &lwork) != CUSOLVER_STATUS_SUCCESS)
-    return 0;
-  return align_up((size_t)lwork * sizeof(double), 256) + 256 + 256;
+  (void)n_aux;
+  Sizer z;
+  z.take<double>(64 * 64);  // inverse of the current diagonal block
+  z.take<int>(1);           // first non-positive pivot
+  return z.off + 256;
 }
 
 extern "C" int gsdft_aux_cholesky(double* V, int64_t n_aux, double lam, void* ws, size_t ws_bytes,
@@ -283,34 +237,19 @@ extern "C" int gsdft_aux_cholesky(double* V, int64_t n_aux, double lam, void* ws
   GSDFT_REQUIRE(n_aux > 0 && n_aux < (int64_t(1) << 31), "n_aux out of range");
   GSDFT_REQUIRE(V, "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
-  Handles* h = nullptr;
-  int rc = get_handles(&h);
-  if (rc) return rc;
-  int lwork = 0;
-  if (cusolverDnDpotrf_bufferSize(h->solver, CUBLAS_FILL_MODE_UPPER, (int)n_aux, V, (int)n_aux,
-                                  &lwork) != CUSOLVER_STATUS_SUCCESS)
-    return fail(GSDFT_ERR_LINALG, "potrf_bufferSize failed");
   Carver c(ws, ws_bytes);
-  double* work = c.take<double>((size_t)lwork);
+  double* Dinv = c.take<double>(64 * 64);
   int* info = c.take<int>(1);
   if (!c.ok) return fail(GSDFT_ERR_ARG, "cholesky workspace too small (%zu < %zu)", ws_bytes, c.off);
-  shift_diag_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(V, n_aux, lam);
-  GSDFT_LAUNCHED("shift_diag");
-  cusolverDnSetStream(h->solver, st);
-  // Row-major V is symmetric, so it is its own column-major view; the column-major UPPER factor U
-  // (V = U^T U) read back row-major is the lower factor L = U^T.
-  if (cusolverDnDpotrf(h->solver, CUBLAS_FILL_MODE_UPPER, (int)n_aux, V, (int)n_aux, work, lwork,
-                       info) != CUSOLVER_STATUS_SUCCESS)
-    return fail(GSDFT_ERR_LINALG, "cusolverDnDpotrf failed to launch");
+  int rc = potrf_dmma(V, n_aux, lam, Dinv, info, st);
+  if (rc) return rc;
   int info_h = 0;
   GSDFT_CUDA(cudaMemcpyAsync(&info_h, info, sizeof(int), cudaMemcpyDeviceToHost, st));
   GSDFT_CUDA(cudaStreamSynchronize(st));
   if (info_h != 0)
-    return fail(GSDFT_ERR_LINALG, "aux metric + lam I is not positive definite (potrf info %d)",
-                info_h);
-  dim3 grid(grid_1d(n_aux, 256), (unsigned)imin64(n_aux, 65535));
-  zero_upper_kernel<<<grid, 256, 0, st>>>(V, n_aux);
-  GSDFT_LAUNCHED("zero_upper");
+    return fail(GSDFT_ERR_LINALG,
+                "aux metric + lam I is not positive definite (pivot %d of %lld not positive)",
+                info_h, (long long)n_aux);
   return GSDFT_OK;
 }
 
@@ -327,18 +266,9 @@ extern "C" int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux
   GSDFT_REQUIRE(L && gamma && d && E, "null pointer");
   GSDFT_REQUIRE(d != gamma, "d must not alias gamma");
   cudaStream_t st = (cudaStream_t)stream;
-  Handles* h = nullptr;
-  int rc = get_handles(&h);
-  if (rc) return rc;
   GSDFT_CUDA(cudaMemcpyAsync(d, gamma, n_aux * sizeof(double), cudaMemcpyDeviceToDevice, st));
-  cublasSetStream(h->blas, st);
-  // Row-major lower L is the column-major upper U = L^T: L y = g  <=>  U^T y = g; L^T d = y <=> U d = y.
-  if (cublasDtrsv(h->blas, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_T, CUBLAS_DIAG_NON_UNIT, (int)n_aux, L,
-                  (int)n_aux, d, 1) != CUBLAS_STATUS_SUCCESS)
-    return fail(GSDFT_ERR_LINALG, "cublasDtrsv (forward) failed");
-  if (cublasDtrsv(h->blas, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N, CUBLAS_DIAG_NON_UNIT, (int)n_aux, L,
-                  (int)n_aux, d, 1) != CUBLAS_STATUS_SUCCESS)
-    return fail(GSDFT_ERR_LINALG, "cublasDtrsv (backward) failed");
+  int rc = trsv_llt(L, n_aux, d, st);
+  if (rc) return rc;
   half_dot_kernel<<<1, 1024, 0, st>>>(gamma, d, n_aux, E);
   GSDFT_LAUNCHED("half_dot");
   return GSDFT_OK;
@@ -352,19 +282,9 @@ extern "C" int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Lin
   GSDFT_REQUIRE(L != Linv, "Linv must not alias L");
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t n = n_aux;
-  identity_kernel<<<grid_1d(n * n, 256), 256, 0, st>>>(Linv, n);
-  GSDFT_LAUNCHED("identity");
-  Handles* h = nullptr;
-  int rc = get_handles(&h);
+  // L^-1 in the lower triangle (DMMA recursive doubling), then its mirror into the strict upper one
+  int rc = trtri_dmma(L, n, Linv, st);
   if (rc) return rc;
-  cublasSetStream(h->blas, st);
-  // Column-major, the row-major lower L is U = L^T (upper) and the row-major X is X^T. U Y = I gives
-  // Y = L^-T, i.e. X = L^-1 row-major (lower triangular; its strict upper triangle stays zero).
-  const double one = 1.0;
-  if (cublasDtrsm(h->blas, CUBLAS_SIDE_LEFT, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N,
-                  CUBLAS_DIAG_NON_UNIT, (int)n, (int)n, &one, L, (int)n, Linv, (int)n) !=
-      CUBLAS_STATUS_SUCCESS)
-    return fail(GSDFT_ERR_LINALG, "cublasDtrsm failed");
   const dim3 tg((unsigned)((n + 31) / 32), (unsigned)((n + 31) / 32));
   mirror_lower_kernel<<<tg, dim3(32, 8), 0, st>>>(Linv, n);
   GSDFT_LAUNCHED("mirror_lower");

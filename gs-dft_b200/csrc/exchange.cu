@@ -3,17 +3,15 @@
 //   M_PQ = sum_{o,o'} D[P,o,o'] D[Q,o,o'] = (D D^T)_PQ,  so  E_K = -|L^-1 D|_F^2  with V + lam I = L L^T.
 // Layout (row-major): Bt[a][P] = (P|a) for the representatives a (thread per aux, coalesced
 // stores), X[a][o n + o'] = C_io C_ko' (+ C_ko C_io' for a merged transposed twin, whose integral
-// is the same), D = Bt^T X. The contractions are plain library GEMMs (cuBLAS DGEMM, FP64 tensor
-// cores) and triangular solves with the metric's factor; the integral block and every reduction are
-// this file's kernels, all in a fixed order (bitwise reproducible).
-// Reverse: Ybar = dE/dD = -2 g L^-T L^-1 D; dE/dX = Bt Ybar; dE/d(P|a) = W[a][P] = (X Ybar^T)[a][P],
+// is the same), D = Bt^T X. The contractions are the library's own DMMA GEMMs (dense.cu): D split
+// over the pairs (its n_aux x n_occ^2 tiles alone cannot fill the device), Z = L^-1 D and its
+// reverse as products with the packed inverse factor read as a lower-triangular operand; the
+// integral block and every reduction are this file's kernels, all in a fixed order (bitwise
+// reproducible).
+// Reverse: Ybar = dE/dD = -2 g L^-T L^-1 D; dE/dX = Bt Ybar; dE/d(P|a) = W[P][a] = (Ybar X^T)[P][a],
 // which drives the same integral reverse pass as RI-J with a per-(P,a) weight
-// (gsdft_j_vjp_weighted); dE/dC from dE/dX per splat over the plan's groupings.
-#include <cublas_v2.h>
-
-#include <mutex>
-#include <unordered_map>
-
+// (gsdft_j_vjp_weighted, W stored aux-major so that a warp's pairs read consecutive entries);
+// dE/dC from dE/dX per splat over the plan's groupings.
 #include "common.cuh"
 
 extern "C" size_t gsdft_j_vjp_weighted_workspace_size(int64_t n_live, int64_t n_aux);
@@ -23,6 +21,14 @@ extern "C" int gsdft_j_vjp_weighted(const double* rec, int64_t n_live, const dou
                                     size_t ws_bytes, gsdft_stream_t stream);
 
 namespace gsdft {
+
+int gemm_dmma(bool ta, bool tb, bool tri_a, int64_t M, int64_t N, int64_t K, double alpha,
+              const double* A, int64_t lda, const double* B, int64_t ldb, double beta, double* C,
+              int64_t ldc, cudaStream_t st);
+int gemm_dmma_splitk(bool ta, int64_t M, int64_t N, int64_t K, double alpha, const double* A,
+                     int64_t lda, const double* B, int64_t ldb, double beta, double* C, int64_t ldc,
+                     double* part, int S, cudaStream_t st);
+int splitk_count(int64_t M, int64_t N, int64_t K);
 
 constexpr int kKThreads = 128;  // aux per CTA in the integral block kernel
 constexpr int kKTile = 32;      // pair records per CTA iteration
@@ -194,33 +200,9 @@ __global__ void k_cgrad_kernel(const int32_t* __restrict__ order_i, const int64_
   }
 }
 
-// One cuBLAS handle per device, created on first use.
-static std::mutex g_kmu;
-static std::unordered_map<int, cublasHandle_t> g_kblas;
-
-static int k_blas(cublasHandle_t* out, cudaStream_t st) {
-  int dev = 0;
-  GSDFT_CUDA(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lk(g_kmu);
-  cublasHandle_t& h = g_kblas[dev];
-  if (!h && cublasCreate(&h) != CUBLAS_STATUS_SUCCESS) {
-    h = nullptr;
-    return fail(GSDFT_ERR_LINALG, "cublasCreate failed");
-  }
-  if (cublasSetStream(h, st) != CUBLAS_STATUS_SUCCESS)
-    return fail(GSDFT_ERR_LINALG, "cublasSetStream failed");
-  *out = h;
-  return GSDFT_OK;
-}
-
-#define GSDFT_BLAS(call, what)                                     \
-  do {                                                             \
-    if ((call) != CUBLAS_STATUS_SUCCESS)                           \
-      return ::gsdft::fail(GSDFT_ERR_LINALG, "%s failed", what);   \
-  } while (0)
-
 struct KLayout {
-  double *Bt, *X, *Xbar, *Y, *part;
+  double *Bt, *X, *Xbar, *Y, *part, *split;
+  int S;
   void* vjp_ws;
   size_t vjp_bytes;
   bool ok;
@@ -235,6 +217,8 @@ static KLayout k_layout(void* ws, size_t ws_bytes, int64_t n_rep, int64_t n_aux,
   l.Xbar = c.take<double>((size_t)imax64(n_rep, 1) * K2);
   l.Y = c.take<double>((size_t)n_aux * K2);
   l.part = c.take<double>(kKRedBlocks);
+  l.S = splitk_count(n_aux, K2, imax64(n_rep, 1));
+  l.split = c.take<double>((size_t)l.S * n_aux * K2);
   l.vjp_bytes = gsdft_j_vjp_weighted_workspace_size(imax64(n_rep, 1), n_aux);
   l.vjp_ws = c.take<unsigned char>(l.vjp_bytes);
   l.ok = c.ok;
@@ -267,6 +251,7 @@ extern "C" size_t gsdft_k_workspace_size(int64_t n_rep, int64_t n_aux, int64_t n
   z.take<double>((size_t)imax64(n_rep, 1) * K2);
   z.take<double>((size_t)n_aux * K2);
   z.take<double>(kKRedBlocks);
+  z.take<double>((size_t)splitk_count(n_aux, K2, imax64(n_rep, 1)) * n_aux * K2);
   z.take<unsigned char>(gsdft_j_vjp_weighted_workspace_size(imax64(n_rep, 1), n_aux));
   return z.off + 256;
 }
@@ -274,39 +259,33 @@ extern "C" size_t gsdft_k_workspace_size(int64_t n_rep, int64_t n_aux, int64_t n
 extern "C" int gsdft_k_forward(const double* rec, const int32_t* pi, const int32_t* pj,
                                const int32_t* rep_pos, const int32_t* rep_twin, int64_t n_rep,
                                const double* beta, const double* R, const double* KN,
-                               int64_t n_aux, const double* L, const double* C_occ,
+                               int64_t n_aux, const double* Linv, const double* C_occ,
                                int64_t n_occ, double* Z, double* E, void* ws, size_t ws_bytes,
                                gsdft_stream_t stream) {
   GSDFT_REQUIRE(n_rep >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31) && n_occ > 0 &&
                     n_occ * n_occ < (int64_t(1) << 31) && n_rep < (int64_t(1) << 31),
                 "bad sizes");
-  GSDFT_REQUIRE(beta && R && KN && L && C_occ && Z && E && ws, "null pointer");
+  GSDFT_REQUIRE(beta && R && KN && Linv && C_occ && Z && E && ws, "null pointer");
   GSDFT_REQUIRE(n_rep == 0 || (rec && pi && pj && rep_pos && rep_twin), "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   KLayout l = k_layout(ws, ws_bytes, n_rep, n_aux, n_occ);
   if (!l.ok) return fail(GSDFT_ERR_ARG, "exchange workspace too small");
   const int64_t K2 = n_occ * n_occ;
-  cublasHandle_t h = nullptr;
-  int rc = k_blas(&h, st);
-  if (rc) return rc;
+  int rc = GSDFT_OK;
   if (n_rep == 0) {
     GSDFT_CUDA(cudaMemsetAsync(Z, 0, (size_t)n_aux * K2 * sizeof(double), st));
   } else {
     rc = k_block_and_x(rec, pi, pj, rep_pos, rep_twin, n_rep, beta, R, KN, n_aux, C_occ, n_occ, l,
                        st);
     if (rc) return rc;
-    // D (row-major n_aux x K2) = Bt^T X: column-major D^T = X^T Bt
-    const double one = 1.0, zero = 0.0;
-    GSDFT_BLAS(cublasDgemm(h, CUBLAS_OP_N, CUBLAS_OP_T, (int)K2, (int)n_aux, (int)n_rep, &one, l.X,
-                           (int)K2, l.Bt, (int)n_aux, &zero, Z, (int)K2),
-               "cublasDgemm (D)");
+    // D (n_aux x K2, in Y) = Bt^T X, split over the pairs
+    rc = gemm_dmma_splitk(true, n_aux, K2, n_rep, 1.0, l.Bt, n_aux, l.X, K2, 0.0, l.Y, K2, l.split,
+                          l.S, st);
+    if (rc) return rc;
+    // Z = L^-1 D: the packed inverse's lower triangle
+    rc = gemm_dmma(false, false, true, n_aux, K2, n_aux, 1.0, Linv, n_aux, l.Y, K2, 0.0, Z, K2, st);
+    if (rc) return rc;
   }
-  // Z = L^-1 D: column-major Z^T U = D^T with U = L^T (the row-major lower factor read column-major)
-  const double one = 1.0;
-  GSDFT_BLAS(cublasDtrsm(h, CUBLAS_SIDE_RIGHT, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_N,
-                         CUBLAS_DIAG_NON_UNIT, (int)K2, (int)n_aux, &one, L, (int)n_aux, Z,
-                         (int)K2),
-             "cublasDtrsm (L^-1 D)");
   k_sumsq_kernel<<<kKRedBlocks, 256, 0, st>>>(Z, n_aux * K2, l.part);
   GSDFT_LAUNCHED("k_sumsq");
   k_energy_kernel<<<1, 256, 0, st>>>(l.part, kKRedBlocks, E);
@@ -317,7 +296,7 @@ extern "C" int gsdft_k_forward(const double* rec, const int32_t* pi, const int32
 extern "C" int gsdft_k_backward(const double* rec, const int32_t* pi, const int32_t* pj,
                                 const int32_t* rep_pos, const int32_t* rep_twin, int64_t n_rep,
                                 const double* beta, const double* R, const double* KN,
-                                int64_t n_aux, const double* L, const double* C_occ,
+                                int64_t n_aux, const double* Linv, const double* C_occ,
                                 int64_t n_occ, const double* Z, const double* g_E,
                                 const int32_t* order_i, const int64_t* seg_i,
                                 const int32_t* partner_i, const int32_t* order_j,
@@ -327,7 +306,8 @@ extern "C" int gsdft_k_backward(const double* rec, const int32_t* pi, const int3
   GSDFT_REQUIRE(n_rep >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31) && n_occ > 0 && M > 0 &&
                     n_occ * n_occ < (int64_t(1) << 31) && n_rep < (int64_t(1) << 31),
                 "bad sizes");
-  GSDFT_REQUIRE(beta && R && KN && L && C_occ && Z && g_C && ws && seg_i && seg_j, "null pointer");
+  GSDFT_REQUIRE(beta && R && KN && Linv && C_occ && Z && g_C && ws && seg_i && seg_j,
+                "null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   if (n_rep == 0) {
     GSDFT_CUDA(cudaMemsetAsync(g_C, 0, (size_t)M * n_occ * sizeof(double), st));
@@ -339,30 +319,21 @@ extern "C" int gsdft_k_backward(const double* rec, const int32_t* pi, const int3
   KLayout l = k_layout(ws, ws_bytes, n_rep, n_aux, n_occ);
   if (!l.ok) return fail(GSDFT_ERR_ARG, "exchange workspace too small");
   const int64_t K2 = n_occ * n_occ;
-  cublasHandle_t h = nullptr;
-  int rc = k_blas(&h, st);
-  if (rc) return rc;
   // Bt and X from the forward (the same workspace, untouched in between)
-  // Y = L^-T Z: column-major Y^T U^T = Z^T
-  GSDFT_CUDA(cudaMemcpyAsync(l.Y, Z, (size_t)n_aux * K2 * sizeof(double),
-                             cudaMemcpyDeviceToDevice, st));
-  const double one = 1.0, zero = 0.0;
-  GSDFT_BLAS(cublasDtrsm(h, CUBLAS_SIDE_RIGHT, CUBLAS_FILL_MODE_UPPER, CUBLAS_OP_T,
-                         CUBLAS_DIAG_NON_UNIT, (int)K2, (int)n_aux, &one, L, (int)n_aux, l.Y,
-                         (int)K2),
-             "cublasDtrsm (L^-T Z)");
+  // Y = L^-T Z (the packed inverse's lower triangle, transposed), then Ybar = -2 g_E Y
+  int rc = gemm_dmma(true, false, true, n_aux, K2, n_aux, 1.0, Linv, n_aux, Z, K2, 0.0, l.Y, K2, st);
+  if (rc) return rc;
   k_scale_kernel<<<grid_1d(n_aux * K2, 256), 256, 0, st>>>(l.Y, n_aux * K2, g_E);
   GSDFT_LAUNCHED("k_scale");
-  // Xbar (row-major n_rep x K2) = Bt Ybar: column-major Xbar^T = Ybar^T Bt^T
-  GSDFT_BLAS(cublasDgemm(h, CUBLAS_OP_N, CUBLAS_OP_N, (int)K2, (int)n_rep, (int)n_aux, &one, l.Y,
-                         (int)K2, l.Bt, (int)n_aux, &zero, l.Xbar, (int)K2),
-             "cublasDgemm (dE/dX)");
-  // W (row-major n_rep x n_aux) = X Ybar^T, into Bt's storage: column-major W^T = Ybar X^T
+  // Xbar (n_rep x K2) = Bt Ybar
+  rc = gemm_dmma(false, false, false, n_rep, K2, n_aux, 1.0, l.Bt, n_aux, l.Y, K2, 0.0, l.Xbar, K2,
+                 st);
+  if (rc) return rc;
+  // W (n_aux x n_rep) = Ybar X^T, into Bt's storage (Bt is no longer needed)
   double* Wt = l.Bt;
-  GSDFT_BLAS(cublasDgemm(h, CUBLAS_OP_T, CUBLAS_OP_N, (int)n_aux, (int)n_rep, (int)K2, &one, l.Y,
-                         (int)K2, l.X, (int)K2, &zero, Wt, (int)n_aux),
-             "cublasDgemm (dE/d(P|a))");
-  rc = gsdft_j_vjp_weighted(rec, n_rep, beta, R, KN, Wt, n_aux, n_aux, sums, l.vjp_ws,
+  rc = gemm_dmma(false, true, false, n_aux, n_rep, K2, 1.0, l.Y, K2, l.X, K2, 0.0, Wt, n_rep, st);
+  if (rc) return rc;
+  rc = gsdft_j_vjp_weighted(rec, n_rep, beta, R, KN, Wt, n_rep, n_aux, sums, l.vjp_ws,
                             l.vjp_bytes, stream);
   if (rc) return rc;
   k_cgrad_kernel<<<(unsigned)M, 128, 0, st>>>(order_i, seg_i, partner_i, order_j, seg_j, partner_j,

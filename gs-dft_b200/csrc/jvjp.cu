@@ -50,8 +50,8 @@ __global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const doubl
   o[7] = 0.0;
 }
 
-// kW: the per-(P,a) weight of the reverse pass is W[a * ldw + P] x (the aux record's dbar KN)
-// (E = sum_{P,a} W[a][P] (P|a), as the RI-K gradient needs); without it the weight is dbar_P KN_P.
+// kW: the per-(P,a) weight of the reverse pass is W[P * ldw + a] x (the aux record's dbar KN)
+// (E = sum_{P,a} W[P][a] (P|a), as the RI-K gradient needs); without it the weight is dbar_P KN_P.
 // Node evaluations of the reverse kernel since the last reset ((aux, pair) units times the nodes
 // each evaluated). Read by gsdft_node_evals.
 static __device__ unsigned long long g_vjp_node_evals;
@@ -113,7 +113,8 @@ __global__ void GSDFT_VJP_BOUNDS
       const double* ar = tl + k * kAuxRec;
       const double b = ar[0], cP = ar[1], b2 = ar[6];
       double dk = ar[5];
-      if constexpr (kW) dk *= Wt[aa * ldw + (P0 + (int64_t)t * kVjpTile + k)];
+      // aux-major weights: the warp's pairs read consecutive entries of row P
+      if constexpr (kW) dk *= Wt[(P0 + (int64_t)t * kVjpTile + k) * ldw + aa];
       const double d0 = ar[2] - Pc[0], d1 = ar[3] - Pc[1], d2 = ar[4] - Pc[2];
       double y[3], m[3];
 #pragma unroll
@@ -559,7 +560,7 @@ extern "C" int gsdft_j_vjp_weighted(const double* rec, int64_t n_live, const dou
                                     const double* R, const double* KN, const double* Wt,
                                     int64_t ldw, int64_t n_aux, double* sums, void* ws,
                                     size_t ws_bytes, gsdft_stream_t stream) {
-  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31) && ldw >= n_aux,
+  GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31) && ldw >= n_live,
                 "bad sizes");
   if (n_live == 0) return GSDFT_OK;
   GSDFT_REQUIRE(rec && beta && R && KN && Wt && sums, "null pointer");

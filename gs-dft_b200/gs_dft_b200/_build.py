@@ -55,7 +55,7 @@ def build(verbose: bool = False, extra_flags: list[str] | None = None) -> str:
     if (not os.path.exists(LIB)
             or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)):
         cmd = [nvcc(), "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", LIB,
-               "-lcusolver", "-lcublas", "-lcudart"]
+               "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -37,6 +37,8 @@ SIGNATURES = {
     "gsdft_node_screening": (_i32, []),
     "gsdft_node_evals": (_i32, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                 _i32]),
+    "gsdft_dense_gemm": (_i32, [_i32, _i32, _i64, _i64, _i64, _f64, _c_p, _i64, _c_p, _i64, _f64,
+                                _c_p, _i64, _c_p]),
     "gsdft_splat_quantities": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p]),
     "gsdft_chart_vjp": (_i32, [_c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p]),
     "gsdft_pairs_workspace_size": (_sz, [_i64, _i64]),

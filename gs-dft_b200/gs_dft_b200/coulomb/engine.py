@@ -129,7 +129,7 @@ class RIJEngine:
         merge_twins: evaluate each (i,j)/(j,i) pair of a live transposed twin once (same integral).
         inverse_solve: form the packed inverse factor once (O(n_aux^3), n_aux <= 65536) so each
             step's solve is two parallel mat-vecs; for engines that run many steps. Off: per-step
-            triangular substitution (cuBLAS Dtrsv).
+            blocked triangular substitution.
         atoms: optional (n_atoms, 4) float64 device tensor of nuclei (x, y, z, Z) in Bohr: adds the
             screened nuclear attraction E_ne on the same pairs.
     """
@@ -322,7 +322,7 @@ class RIJEngine:
 class StepGraph:
     """A whole J-build + gradient step captured once in a CUDA graph and replayed.
 
-    ``step_fn`` launches every kernel (the library's and cuBLAS; never a collective) on the current
+    ``step_fn`` launches every kernel (the library's own; never a collective) on the current
     stream and returns its outputs. Its input tensors are
     read at their captured addresses: copy new parameters into them before ``replay()``. The
     outputs are the captured buffers, overwritten by every replay."""

@@ -4,22 +4,22 @@ Mirror of ``_exchange_M_streamed_screened`` / ``df_exchange_energy_screened``
 (gs_dft/coulomb/ri.py:497-544): D[P,o,o'] = sum_{live (i,k)} (P|ik) C_io C_ko',
 M = D D^T (over o, o'), E_K = -tr((V + lam I)^-1 M), differentiable in the splat parameters and
 the orbitals (aux, pairs and factor frozen, as for E_J). The integral block, the orbital products,
-every reduction and the reverse pass are the library's kernels; the contractions are cuBLAS DGEMM
-and triangular solves with the metric's factor (``gsdft_k_forward`` / ``gsdft_k_backward``), then
-the same pair chain, per-splat reductions and chart reverse as RI-J.
+every reduction, the reverse pass and the contractions (the library's DMMA GEMMs, with the packed
+inverse factor for L^-1 and L^-T) are the library's kernels (``gsdft_k_forward`` /
+``gsdft_k_backward``), then the same pair chain, per-splat reductions and chart reverse as RI-J.
 
 Differences from the reference, by design: the whole pair list is processed in one pass, holding
 the integral block and the orbital products (8 n_rep (n_aux + 2 n_occ^2) bytes, 1.8 GB at
 ethanol) instead of streaming over orbital chunks in O(n_aux^2) memory, so ``occ_chunk`` and
 ``chunk`` are accepted and unused and lists beyond ``max_bytes`` raise; the solve uses the
-Cholesky factor (the reference LU-solves V + lam I). ``omega`` (range-separated exchange) is not
-supported.
+Cholesky factor's inverse, formed once per engine (the reference LU-solves V + lam I). ``omega``
+(range-separated exchange) is not supported.
 """
 from __future__ import annotations
 
 import torch
 
-from .._lib import REC_FIELDS, SIDE_FIELDS, VJP_FIELDS, lib, ptr, stream_handle
+from .._lib import REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, lib, ptr, stream_handle
 from .. import _check
 from .engine import check_step_inputs, make_plan
 
@@ -54,6 +54,13 @@ class RIKEngine:
         self.KN = _check.f64(KN, "KN", (self.n_aux,))
         self.L = _check.f64(L, "L", (self.n_aux, self.n_aux))
         self.plan = make_plan(self.pi, self.pj, w, self.M, 0, 1, merge_twins)
+        # packed inverse factor (L^-1 in its lower triangle), formed once: the solves of every step
+        # are then two triangular products on the tensor cores
+        if self.n_aux > SOLVE_INV_MAX:
+            raise ValueError(f"screened RI-K supports n_aux <= {SOLVE_INV_MAX}")
+        self.Linv = torch.empty((self.n_aux, self.n_aux), dtype=F64, device=pi.device)
+        lib.call("gsdft_j_solve_inverse", ptr(self.L), self.n_aux, ptr(self.Linv),
+                 stream_handle(pi.device))
         dev, nl, n = self.device, self.plan.n_rep, self.plan.n
         self.ws_bytes = int(lib.gsdft_k_workspace_size(nl, self.n_aux, self.n_occ))
         if self.ws_bytes > max_bytes:
@@ -84,7 +91,7 @@ class RIKEngine:
                  ptr(self.rec), s)
         lib.call("gsdft_k_forward", ptr(self.rec), ptr(self.pi), ptr(self.pj),
                  ptr(self.plan.rep_pos), ptr(self.plan.rep_twin), nl, ptr(self.beta), ptr(self.R),
-                 ptr(self.KN), self.n_aux, ptr(self.L), ptr(C), self.n_occ, ptr(self.Z),
+                 ptr(self.KN), self.n_aux, ptr(self.Linv), ptr(C), self.n_occ, ptr(self.Z),
                  ptr(self.E), ptr(self.ws), self.ws_bytes, s)
         self.last_forward = object()
         return self.E
@@ -96,7 +103,7 @@ class RIKEngine:
         nl, p = self.plan.n_rep, self.plan
         lib.call("gsdft_k_backward", ptr(self.rec), ptr(self.pi), ptr(self.pj), ptr(p.rep_pos),
                  ptr(p.rep_twin), nl, ptr(self.beta), ptr(self.R), ptr(self.KN), self.n_aux,
-                 ptr(self.L), ptr(C), self.n_occ, ptr(self.Z), ptr(g_E), ptr(p.order_i),
+                 ptr(self.Linv), ptr(C), self.n_occ, ptr(self.Z), ptr(g_E), ptr(p.order_i),
                  ptr(p.seg_i), ptr(p.partner_i), ptr(p.order_j), ptr(p.seg_j), ptr(p.partner_j),
                  self.M, ptr(self.sums), ptr(self.g_C), ptr(self.ws), self.ws_bytes, s)
         lib.call("gsdft_k_unit_q", ptr(self.rec), nl, ptr(self.rec_K), s)

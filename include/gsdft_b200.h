@@ -9,14 +9,8 @@
  *   - all pointers are DEVICE pointers unless the name ends in _host; FP64 arrays are row-major;
  *   - buffers are owned and allocated by the caller, and scratch comes from an explicit workspace
  *     whose size the matching *_workspace_size() returns. No entry point allocates device memory for
- *     its data, with one exception: the entry points that call cuBLAS / cuSOLVER
- *     (gsdft_aux_cholesky_workspace_size, gsdft_aux_cholesky, gsdft_j_solve, gsdft_j_solve_inverse,
- *     gsdft_k_forward, gsdft_k_backward) create that library's handle for the current device on
- *     their first call there, and handle creation allocates. Make that first call on each device
- *     before any stream capture, and from a context that may allocate (outside a framework's
- *     preallocated pool); later calls allocate nothing. The per-step path of the RI-J engine
- *     (gsdft_pair_prep, gsdft_j_forward, gsdft_j_solve_inv, gsdft_j_vjp and the chain) calls no
- *     library;
+ *     its data, and no entry point calls a math library (cuBLAS, cuSOLVER): the dense contractions
+ *     and factorisations are the library's own DMMA kernels;
  *   - work is enqueued on `stream` (the last argument). Only gsdft_pairs_count / gsdft_pairs_build /
  *     gsdft_pair_plan / gsdft_aux_cholesky synchronise the stream, to read back integers (pair counts,
  *     the factorisation status), exactly where the reference syncs to the host
@@ -117,6 +111,14 @@ int gsdft_node_screening(void);
  * them. Synchronises the device. For work accounting (the roofline's evaluated FLOP count). No
  * reference counterpart. */
 int gsdft_node_evals(uint64_t* forward_host, uint64_t* reverse_host, int clear);
+
+/* C = alpha op(A) op(B) + beta C on the FP64 tensor cores (mma.sync f64), row-major, op = transpose
+ * when trans_a / trans_b (A then stored K x M, B stored N x K); M, N, K >= 0, leading dimensions in
+ * elements. The GEMM under the library's Cholesky, factor inverse and RI-K contractions, exported
+ * for direct use and testing. No reference counterpart (the reference's dense algebra is XLA's). */
+int gsdft_dense_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, double alpha,
+                     const double* A, int64_t lda, const double* B, int64_t ldb, double beta,
+                     double* C, int64_t ldc, gsdft_stream_t stream);
 
 /* ---- splat chart ------------------------------------------------------------------------------ */
 
@@ -317,10 +319,11 @@ int gsdft_vne(const double* rec, int64_t n_rep, const double* atoms, int64_t n_a
 int gsdft_density_pairs(const int32_t* pi, const int32_t* pj, int64_t n, const double* C_occ,
                         const double* occ, int64_t n_occ, double* P, gsdft_stream_t stream);
 
-/* The reverse pass of E = sum_{P,a} W[a][P] (P|a): gsdft_j_vjp with a per-(aux, pair) weight matrix
- * Wt (n_rep rows of leading dimension ldw >= n_aux) instead of dbar_P q_a; the sums then go to
- * gsdft_pair_chain with records whose q is 1 (gsdft_k_unit_q). Used by the RI-K gradient (the
- * reference differentiates gs_dft/coulomb/ri.py:497-544 with JAX autodiff). */
+/* The reverse pass of E = sum_{P,a} W[P][a] (P|a): gsdft_j_vjp with a per-(aux, pair) weight matrix
+ * Wt, stored aux-major (n_aux rows of leading dimension ldw >= n_rep: Wt[P * ldw + a]), instead of
+ * dbar_P q_a; the sums then go to gsdft_pair_chain with records whose q is 1 (gsdft_k_unit_q). Used
+ * by the RI-K gradient (the reference differentiates gs_dft/coulomb/ri.py:497-544 with JAX
+ * autodiff). */
 size_t gsdft_j_vjp_weighted_workspace_size(int64_t n_rep, int64_t n_aux);
 int gsdft_j_vjp_weighted(const double* rec, int64_t n_rep, const double* beta, const double* R,
                          const double* KN, const double* Wt, int64_t ldw, int64_t n_aux,
@@ -330,23 +333,25 @@ int gsdft_j_vjp_weighted(const double* rec, int64_t n_rep, const double* beta, c
  * E_K = -tr((V + lam I)^-1 D D^T) = -|L^-1 D|^2 (replaces _exchange_M_streamed_screened and
  * df_exchange_energy_screened, gs_dft/coulomb/ri.py:497-544, for omega = None). The pair list must
  * be an ordered 0/1 list (the reference masks with valid & occupied); a merged transposed twin adds
- * C_ko C_io'. Writes Z = L^-1 D (n_aux x n_occ^2, row-major; kept for the backward) and E (device
- * scalar). The workspace (gsdft_k_workspace_size: 8 n_rep (n_aux + 2 n_occ^2) bytes and more) holds
- * the integral block and the products between forward and backward: pass the same, untouched
- * workspace to gsdft_k_backward. */
+ * C_ko C_io'. Linv is the packed inverse factor of gsdft_j_solve_inverse (its lower triangle L^-1 is
+ * read). Writes Z = L^-1 D (n_aux x n_occ^2, row-major; kept for the backward) and E (device
+ * scalar). The contractions are the library's DMMA GEMMs. The workspace (gsdft_k_workspace_size:
+ * 8 n_rep (n_aux + 2 n_occ^2) bytes and more) holds the integral block and the products between
+ * forward and backward: pass the same, untouched workspace to gsdft_k_backward. */
 size_t gsdft_k_workspace_size(int64_t n_rep, int64_t n_aux, int64_t n_occ);
 int gsdft_k_forward(const double* rec, const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
                     const int32_t* rep_twin, int64_t n_rep, const double* beta, const double* R,
-                    const double* KN, int64_t n_aux, const double* L, const double* C_occ,
+                    const double* KN, int64_t n_aux, const double* Linv, const double* C_occ,
                     int64_t n_occ, double* Z, double* E, void* ws, size_t ws_bytes,
                     gsdft_stream_t stream);
 /* Gradient of g_E * E_K (g_E a device scalar, NULL = 1): the reverse-pass sums (for gsdft_pair_chain
  * with gsdft_k_unit_q records) and g_C (M x n_occ, written). Groupings and partners from
- * gsdft_pair_groups. Deterministic. */
+ * gsdft_pair_groups. Overwrites the workspace's integral block: a second backward needs the forward
+ * again. Deterministic. */
 int gsdft_k_backward(const double* rec, const int32_t* pi, const int32_t* pj,
                      const int32_t* rep_pos, const int32_t* rep_twin, int64_t n_rep,
                      const double* beta, const double* R, const double* KN, int64_t n_aux,
-                     const double* L, const double* C_occ, int64_t n_occ, const double* Z,
+                     const double* Linv, const double* C_occ, int64_t n_occ, const double* Z,
                      const double* g_E, const int32_t* order_i, const int64_t* seg_i,
                      const int32_t* partner_i, const int32_t* order_j, const int64_t* seg_j,
                      const int32_t* partner_j, int64_t M, double* sums, double* g_C, void* ws,

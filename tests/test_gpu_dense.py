@@ -1,0 +1,98 @@
+"""The library's dense FP64 routines on the tensor cores (DMMA), against host LAPACK / NumPy on the
+same inputs: the GEMM in every transpose combination with ragged sizes, the blocked Cholesky of
+V + lam I (including the not-positive-definite error), the packed inverse factor, and the one-shot
+blocked triangular solve. Well-conditioned random matrices bound the comparison at the level of
+rounding; the aux metrics themselves are covered end to end in test_gpu_parity.py and
+test_gpu_large.py."""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def g():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import gs_dft_b200
+    gs_dft_b200._lib.lib.load()
+    return gs_dft_b200
+
+
+def dev(a):
+    return torch.as_tensor(np.ascontiguousarray(a), dtype=torch.float64, device="cuda")
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+@pytest.mark.parametrize("ta", [0, 1])
+@pytest.mark.parametrize("tb", [0, 1])
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (64, 64, 16), (70, 130, 37), (257, 63, 1000),
+                                   (5, 300, 4100)])
+def test_gemm_matches_host(g, ta, tb, M, N, K):
+    from gs_dft_b200._lib import lib, ptr, stream_handle
+    rng = np.random.default_rng(M * 7 + N * 3 + K + 11 * ta + 13 * tb)
+    A = rng.standard_normal((K, M) if ta else (M, K))
+    B = rng.standard_normal((N, K) if tb else (K, N))
+    C0 = rng.standard_normal((M, N))
+    want = 0.75 * (A.T if ta else A) @ (B.T if tb else B) - 0.5 * C0
+    dA, dB, dC = dev(A), dev(B), dev(C0)
+    lib.call("gsdft_dense_gemm", ta, tb, M, N, K, 0.75, ptr(dA), A.shape[1], ptr(dB), B.shape[1],
+             -0.5, ptr(dC), N, stream_handle(dC.device))
+    got = host(dC)
+    # FP64 sums of K products: error ~ K u |A||B|
+    tol = 1e-15 * K * np.abs(A).max() * np.abs(B).max() + 1e-14
+    np.testing.assert_allclose(got, want, rtol=0, atol=tol)
+    assert got.shape == (M, N)
+
+
+def _spd(n, seed, cond=1e4):
+    rng = np.random.default_rng(seed)
+    Q, _ = np.linalg.qr(rng.standard_normal((n, n)))
+    ev = np.geomspace(1.0, 1.0 / cond, n)
+    V = (Q * ev) @ Q.T
+    return 0.5 * (V + V.T)
+
+
+@pytest.mark.parametrize("n", [1, 63, 64, 65, 300, 1000, 2051])
+def test_cholesky_inverse_and_solve(g, n):
+    from gs_dft_b200._lib import lib, ptr, stream_handle
+    from gs_dft_b200.coulomb.ri import cholesky_inplace
+    V = _spd(n, n)
+    lam = 1e-8
+    Lref = np.linalg.cholesky(V + lam * np.eye(n))
+    dL = cholesky_inplace(dev(V), lam)
+    L = host(dL)
+    assert np.all(np.triu(L, 1) == 0.0)
+    # a factor of a cond-1e4 matrix: entries agree to ~cond^(1/2) u
+    np.testing.assert_allclose(L, Lref, rtol=0, atol=1e-12 * np.abs(Lref).max())
+    st = stream_handle(dL.device)
+    X = torch.empty((n, n), dtype=torch.float64, device="cuda")
+    lib.call("gsdft_j_solve_inverse", ptr(dL), n, ptr(X), st)
+    Xh = host(X)
+    np.testing.assert_array_equal(np.triu(Xh, 1), np.tril(Xh, -1).T)
+    np.testing.assert_allclose(np.tril(Xh) @ L, np.eye(n), rtol=0, atol=1e-10)
+    rng = np.random.default_rng(n + 1)
+    gam = rng.standard_normal(n)
+    from scipy.linalg import cho_solve
+    d_ref = cho_solve((L, True), gam)
+    E_ref = 0.5 * gam @ d_ref
+    for name, args in (("gsdft_j_solve", (ptr(dL),)), ("gsdft_j_solve_inv", (ptr(X),))):
+        d = torch.empty(n, dtype=torch.float64, device="cuda")
+        E = torch.empty(1, dtype=torch.float64, device="cuda")
+        wb = max(int(lib.gsdft_j_solve_inv_workspace_size(n)), 256)
+        ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
+        lib.call(name, *args, ptr(dev(gam)), n, ptr(d), ptr(E), ptr(ws), wb, st)
+        np.testing.assert_allclose(host(d), d_ref, rtol=0, atol=1e-10 * np.abs(d_ref).max())
+        np.testing.assert_allclose(float(E), E_ref, rtol=1e-11)
+
+
+def test_cholesky_rejects_an_indefinite_matrix(g):
+    from gs_dft_b200.coulomb.ri import cholesky_inplace
+    V = _spd(200, 5)
+    V[150, 150] = -1.0
+    with pytest.raises(ValueError, match="not positive definite"):
+        cholesky_inplace(dev(V), 1e-8)
