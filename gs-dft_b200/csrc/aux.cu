@@ -129,12 +129,13 @@ __global__ void mirror_lower_kernel(double* X, int64_t n) {
   }
 }
 
-// y[i] = sum_{j in row i's triangle} A[i][j] x[j]: columns [0, i] (kLower) or [i, n) (upper).
-// With E != nullptr, block 0 also writes E = 1/2 x.x.
-template <bool kLower>
+// y[i] = sum_{j in row i's triangle} A[i][j] x[j]: columns [0, i] (kLower) or [i, n) (upper);
+// kMode 1 gives y = b - (that), kMode 2 y = b + (that). With E != nullptr, block 0 also writes
+// E = 1/2 x.x.
+template <bool kLower, int kMode>
 __global__ void __launch_bounds__(kTriWarps * 32)
     tri_rows_kernel(const double* __restrict__ A, const double* __restrict__ x, int64_t n,
-                    double* __restrict__ y, double* __restrict__ E) {
+                    double* __restrict__ y, double* __restrict__ E, const double* __restrict__ b) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t i = blockIdx.x * (int64_t)kTriWarps + warp;
   if (i < n) {
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(kTriWarps * 32)
     double v = (a0 + a1) + (a2 + a3);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-    if (lane == 0) y[i] = v;
+    if (lane == 0) y[i] = kMode == 1 ? b[i] - v : (kMode == 2 ? b[i] + v : v);
   }
   if (E != nullptr && blockIdx.x == 0) {
     __shared__ double part[kTriWarps];
@@ -175,6 +176,40 @@ __global__ void __launch_bounds__(kTriWarps * 32)
       *E = 0.5 * sum;
     }
   }
+}
+
+// part[s][i] = sum_{j in chunk s, j >= i} L[j][i] x[j]: the transposed lower-triangular product
+// L^T x read down columns, one column per thread (a warp's loads are consecutive in a row), the
+// rows cut into gridDim.y chunks for parallelism.
+constexpr int kLtCols = 128;
+constexpr int kLtChunks = 16;
+__global__ void __launch_bounds__(kLtCols)
+    trmv_lt_part_kernel(const double* __restrict__ L, const double* __restrict__ x, int64_t n,
+                        double* __restrict__ part) {
+  const int64_t i = blockIdx.x * (int64_t)kLtCols + threadIdx.x;
+  const int64_t chunk = (n + gridDim.y - 1) / gridDim.y;
+  const int64_t c0 = blockIdx.x * (int64_t)kLtCols;
+  const int64_t j0 = imax64(blockIdx.y * chunk, c0), j1 = imin64((blockIdx.y + 1) * chunk, n);
+  double a0 = 0.0, a1 = 0.0;
+  int64_t j = j0;
+  if (i < n) {
+    for (; j + 1 < j1; j += 2) {
+      if (j >= i) a0 = fma(L[j * n + i], x[j], a0);
+      if (j + 1 >= i) a1 = fma(L[(j + 1) * n + i], x[j + 1], a1);
+    }
+    if (j < j1 && j >= i) a0 = fma(L[j * n + i], x[j], a0);
+    part[blockIdx.y * n + i] = a0 + a1;
+  }
+}
+
+// t[i] = sum_s part[s][i] in split order.
+__global__ void sum_parts_kernel(const double* __restrict__ part, int S, int64_t n,
+                                 double* __restrict__ t) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  double acc = 0.0;
+  for (int s = 0; s < S; ++s) acc += part[(int64_t)s * n + i];
+  t[i] = acc;
 }
 
 int potrf_dmma(double* V, int64_t n, double lam, double* Dinv, int* info_dev, cudaStream_t st);
@@ -292,22 +327,49 @@ extern "C" int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Lin
 }
 
 extern "C" size_t gsdft_j_solve_inv_workspace_size(int64_t n_aux) {
-  return ((size_t)imax64(n_aux, 1) * sizeof(double) + 255) & ~(size_t)255;
+  Sizer z;
+  z.take<double>((size_t)imax64(n_aux, 1));                 // y
+  z.take<double>((size_t)imax64(n_aux, 1));                 // t = L^T d
+  z.take<double>((size_t)imax64(n_aux, 1));                 // residual
+  z.take<double>((size_t)kLtChunks * imax64(n_aux, 1));     // partial sums of L^T d
+  return z.off;
 }
 
-extern "C" int gsdft_j_solve_inv(const double* Linv, const double* gamma, int64_t n_aux, double* d,
-                                 double* E, void* ws, size_t ws_bytes, gsdft_stream_t stream) {
+extern "C" int gsdft_j_solve_inv(const double* Linv, const double* L, const double* gamma,
+                                 int64_t n_aux, double* d, double* E, void* ws, size_t ws_bytes,
+                                 gsdft_stream_t stream) {
   GSDFT_REQUIRE(n_aux > 0 && n_aux <= GSDFT_SOLVE_INV_MAX, "n_aux out of range");
   GSDFT_REQUIRE(Linv && gamma && d && E && ws, "null pointer");
   GSDFT_REQUIRE(ws_bytes >= gsdft_j_solve_inv_workspace_size(n_aux), "workspace too small");
   GSDFT_REQUIRE(d != gamma, "d must not alias gamma");
   cudaStream_t st = (cudaStream_t)stream;
   const int64_t n = n_aux;
-  double* y = static_cast<double*>(ws);
+  Carver c(ws, ws_bytes);
+  double* y = c.take<double>((size_t)imax64(n, 1));
+  double* t = c.take<double>((size_t)imax64(n, 1));
+  double* r = c.take<double>((size_t)imax64(n, 1));
+  double* part = c.take<double>((size_t)kLtChunks * imax64(n, 1));
   const unsigned grid = (unsigned)((n + kTriWarps - 1) / kTriWarps);
-  tri_rows_kernel<true><<<grid, kTriWarps * 32, 0, st>>>(Linv, gamma, n, y, nullptr);
+  // d = L^-T (L^-1 gamma)
+  tri_rows_kernel<true, 0><<<grid, kTriWarps * 32, 0, st>>>(Linv, gamma, n, y, nullptr, nullptr);
   GSDFT_LAUNCHED("tri_rows");
-  tri_rows_kernel<false><<<grid, kTriWarps * 32, 0, st>>>(Linv, y, n, d, E);
+  tri_rows_kernel<false, 0><<<grid, kTriWarps * 32, 0, st>>>(Linv, y, n, d, L ? nullptr : E,
+                                                             nullptr);
   GSDFT_LAUNCHED("tri_rows");
+  if (L == nullptr) return GSDFT_OK;  // E = 1/2 |L^-1 gamma|^2 written above
+  // one step of refinement with the factor: r = gamma - L (L^T d), d += L^-T L^-1 r
+  dim3 lt((unsigned)((n + kLtCols - 1) / kLtCols), kLtChunks);
+  trmv_lt_part_kernel<<<lt, kLtCols, 0, st>>>(L, d, n, part);
+  GSDFT_LAUNCHED("trmv_lt");
+  sum_parts_kernel<<<grid_1d(n, 256), 256, 0, st>>>(part, kLtChunks, n, t);
+  GSDFT_LAUNCHED("sum_parts");
+  tri_rows_kernel<true, 1><<<grid, kTriWarps * 32, 0, st>>>(L, t, n, r, nullptr, gamma);
+  GSDFT_LAUNCHED("tri_rows");
+  tri_rows_kernel<true, 0><<<grid, kTriWarps * 32, 0, st>>>(Linv, r, n, y, nullptr, nullptr);
+  GSDFT_LAUNCHED("tri_rows");
+  tri_rows_kernel<false, 2><<<grid, kTriWarps * 32, 0, st>>>(Linv, y, n, d, nullptr, d);
+  GSDFT_LAUNCHED("tri_rows");
+  half_dot_kernel<<<1, 1024, 0, st>>>(gamma, d, n, E);
+  GSDFT_LAUNCHED("half_dot");
   return GSDFT_OK;
 }

@@ -67,7 +67,7 @@ SIGNATURES = {
     "gsdft_j_solve": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_j_solve_inverse": (_i32, [_c_p, _i64, _c_p, _c_p]),
     "gsdft_j_solve_inv_workspace_size": (_sz, [_i64]),
-    "gsdft_j_solve_inv": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_j_solve_inv": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_j_vjp_workspace_size": (_sz, [_i64, _i64]),
     "gsdft_j_vjp": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _sz,
                            _c_p]),

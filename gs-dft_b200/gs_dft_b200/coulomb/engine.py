@@ -255,7 +255,7 @@ class RIJEngine:
     def solve(self):
         """d = (L L^T)^-1 gamma, E = 1/2 gamma.d (replicated tail)."""
         if self.Linv is not None:
-            lib.call("gsdft_j_solve_inv", ptr(self.Linv), ptr(self.gamma), self.n_aux,
+            lib.call("gsdft_j_solve_inv", ptr(self.Linv), ptr(self.L), ptr(self.gamma), self.n_aux,
                      ptr(self.d), ptr(self.E), ptr(self.ws), self.ws_bytes,
                      stream_handle(self.device))
         else:

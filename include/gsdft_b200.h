@@ -242,8 +242,9 @@ int gsdft_j_forward(const double* rec, int64_t n_rep, const double* beta, const 
 int gsdft_j_forward_noalloc(const double* rec, int64_t n_rep, const double* beta, const double* R,
                             const double* KN, int64_t n_aux, double* gamma, gsdft_stream_t stream);
 
-/* d = (L L^T)^-1 gamma, E = 1/2 gamma.d (E is a device scalar). Replaces df_coulomb_solve with
- * cholV (gs_dft/coulomb/ri.py:472-482). */
+/* d = (L L^T)^-1 gamma, E = 1/2 gamma.d (E is a device scalar), by blocked substitution (panels
+ * of 64: the diagonal block in shared memory, the rest of the right-hand side updated by row-parallel
+ * panel products). Replaces df_coulomb_solve with cholV (gs_dft/coulomb/ri.py:472-482). */
 size_t gsdft_j_solve_workspace_size(int64_t n_aux);
 int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d, double* E,
                   void* ws, size_t ws_bytes, gsdft_stream_t stream);
@@ -252,16 +253,20 @@ int gsdft_j_solve(const double* L, const double* gamma, int64_t n_aux, double* d
  * gsdft_j_solve_inverse (once per refresh) writes Linv (n_aux, n_aux), row-major and packed: its
  * lower triangle with the diagonal is L^-1 and its strict upper triangle is that of L^-T (the
  * mirror of the strict lower one), from the lower factor L (n_aux <= GSDFT_SOLVE_INV_MAX; one n_aux^2
- * buffer, 22.5 GB at n_aux = 53,000). gsdft_j_solve_inv then gives d = L^-T (L^-1 gamma) and
- * E = 1/2 |L^-1 gamma|^2 (= 1/2 gamma.d) as two row-parallel triangular mat-vecs that read the
- * packed matrix once, with no sequential substitution and no library call. Same outputs as
- * gsdft_j_solve to rounding (the factor's condition number times the unit roundoff). Replaces, per
- * step, cho_solve in df_coulomb_solve (gs_dft/coulomb/ri.py:472-482). */
+ * buffer, 22.5 GB at n_aux = 53,000; computed on the tensor cores by recursive doubling).
+ * gsdft_j_solve_inv then gives d = L^-T (L^-1 gamma) as two row-parallel triangular mat-vecs that
+ * read the packed matrix once, with no sequential substitution and no library call. With the factor
+ * L (non-NULL) it adds one step of iterative refinement, r = gamma - L (L^T d), d += L^-T L^-1 r,
+ * and E = 1/2 gamma.d: the result then matches a substitution solve (gsdft_j_solve) to the
+ * accuracy of a backward-stable solve, where the multiplication by a computed inverse alone carries
+ * errors of order cond(L) times the unit roundoff; this streams the factor and the inverse twice
+ * each. With L = NULL, E = 1/2 |L^-1 gamma|^2. Replaces, per step, cho_solve in df_coulomb_solve
+ * (gs_dft/coulomb/ri.py:472-482). */
 #define GSDFT_SOLVE_INV_MAX 65536
 int gsdft_j_solve_inverse(const double* L, int64_t n_aux, double* Linv, gsdft_stream_t stream);
 size_t gsdft_j_solve_inv_workspace_size(int64_t n_aux);
-int gsdft_j_solve_inv(const double* Linv, const double* gamma, int64_t n_aux, double* d, double* E,
-                      void* ws, size_t ws_bytes, gsdft_stream_t stream);
+int gsdft_j_solve_inv(const double* Linv, const double* L, const double* gamma, int64_t n_aux,
+                      double* d, double* E, void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
 /* Reverse pass over (representative x aux): with dbar = g_E * d (g_E device scalar, NULL = 1), the
  * per-pair sums, (n_rep, GSDFT_VJP_FIELDS), from which J_a = sum_P (P|a) dbar_P and the cotangents

@@ -80,12 +80,14 @@ def test_cholesky_inverse_and_solve(g, n):
     from scipy.linalg import cho_solve
     d_ref = cho_solve((L, True), gam)
     E_ref = 0.5 * gam @ d_ref
-    for name, args in (("gsdft_j_solve", (ptr(dL),)), ("gsdft_j_solve_inv", (ptr(X),))):
+    gam_d = dev(gam)
+    for name, args in (("gsdft_j_solve", (ptr(dL),)), ("gsdft_j_solve_inv", (ptr(X), ptr(dL))),
+                       ("gsdft_j_solve_inv", (ptr(X), None))):
         d = torch.empty(n, dtype=torch.float64, device="cuda")
         E = torch.empty(1, dtype=torch.float64, device="cuda")
         wb = max(int(lib.gsdft_j_solve_inv_workspace_size(n)), 256)
         ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
-        lib.call(name, *args, ptr(dev(gam)), n, ptr(d), ptr(E), ptr(ws), wb, st)
+        lib.call(name, *args, ptr(gam_d), n, ptr(d), ptr(E), ptr(ws), wb, st)
         np.testing.assert_allclose(host(d), d_ref, rtol=0, atol=1e-10 * np.abs(d_ref).max())
         np.testing.assert_allclose(float(E), E_ref, rtol=1e-11)
 

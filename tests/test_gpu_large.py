@@ -199,7 +199,7 @@ def test_metric_rows_and_inverse_factor_large(g):
     ws = torch.empty(wb, dtype=torch.uint8, device="cuda")
     d1 = torch.empty(n, dtype=torch.float64, device="cuda")
     E1 = torch.empty(1, dtype=torch.float64, device="cuda")
-    lib.call("gsdft_j_solve_inv", ptr(Linv), ptr(gam), n, ptr(d1), ptr(E1), ptr(ws), wb, st)
+    lib.call("gsdft_j_solve_inv", ptr(Linv), ptr(L), ptr(gam), n, ptr(d1), ptr(E1), ptr(ws), wb, st)
     d2 = torch.empty(n, dtype=torch.float64, device="cuda")
     E2 = torch.empty(1, dtype=torch.float64, device="cuda")
     lib.call("gsdft_j_solve", ptr(L), ptr(gam), n, ptr(d2), ptr(E2), None, 0, st)

@@ -179,7 +179,7 @@ def test_inverse_factor_solve(g, cfg, M):
     outs = []
     for _ in range(2):
         d_, E_ = torch.empty(n, dtype=torch.float64, device="cuda"), torch.empty(1, dtype=torch.float64, device="cuda")
-        lib.call("gsdft_j_solve_inv", ptr(Linv), ptr(gam), n, ptr(d_), ptr(E_), ptr(ws), wb, st)
+        lib.call("gsdft_j_solve_inv", ptr(Linv), ptr(L), ptr(gam), n, ptr(d_), ptr(E_), ptr(ws), wb, st)
         outs.append((host(d_), float(E_)))
     close(outs[0][0], d_ref)
     close(outs[0][1], E_ref)
