@@ -274,7 +274,8 @@ def main():
     L = g.aux_cholesky(aux, sy.lam)
     beta, R, KN = aux.quantities()
     R = R.contiguous()
-    sh = ShardedRIJ(pi, pj, valid, sy.M, sy.n_occ, beta, R, KN, L, rank, world)
+    sh = ShardedRIJ(pi, pj, valid, sy.M, sy.n_occ, beta, R, KN, L, rank, world,
+                    balance=(quat, log_scale, centers))
     torch.cuda.synchronize()
     refresh_s = time.perf_counter() - t0
     eng = sh.engine
@@ -426,7 +427,11 @@ def main():
                                       "last bit); nodes evaluated per (aux, pair) per step: "
                                       f"forward {evals_fwd / max(units, 1):.2f}, reverse "
                                       f"{evals_vjp / max(units, 1):.2f} of 20 (rank 0)"),
-                   "parallelism": f"pair-partition x{world}", "l2": "flushed between steps",
+                   "parallelism": f"pair-partition x{world}",
+                   "partition": ("contiguous slices of the representatives with equal estimated "
+                                 "integral cost (node counts of the screening rule on a sample of "
+                                 "the aux)" if world > 1 else "one device"),
+                   "l2": "flushed between steps",
                    "execution": ("step replayed from CUDA graphs: one graph on 1 GPU; on N GPUs the "
                                  "compute segments between the two NCCL allreduces, which run eagerly")},
         "refresh_s": refresh_s,

@@ -355,6 +355,85 @@ extern "C" int gsdft_device_status(int* status_host, int clear) {
   return GSDFT_OK;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Estimated integral cost of each representative, for a cost-balanced partition across devices:
+// over a strided sample of the aux, the node screening rule of the integral kernels applied per
+// (aux, pair) (first node at which the exponent has grown kNodeSkipLog2 past the first node's, at the
+// same check nodes), plus one node's worth of per-(aux, pair) fixed work. Integer, so the prefix
+// sums that cut the list are exact and identical on every rank.
+// ------------------------------------------------------------------------------------------------
+__global__ void rep_cost_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
+                                const int32_t* __restrict__ pi, const int32_t* __restrict__ pj,
+                                const int32_t* __restrict__ rep_pos, int64_t n_rep,
+                                const double* __restrict__ beta, const double* __restrict__ R,
+                                int64_t n_aux, int64_t stride, double skip2,
+                                int64_t* __restrict__ cost) {
+  const int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_rep) return;
+  const int64_t e = rep_pos[a];
+  const int i = pi[e], j = pj[e];
+  double Ai[9], Aj[9], mui[3], muj[3];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    Ai[k] = A9[9 * (int64_t)i + k];
+    Aj[k] = A9[9 * (int64_t)j + k];
+  }
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    mui[k] = mu[3 * (int64_t)i + k];
+    muj[k] = mu[3 * (int64_t)j + k];
+  }
+  double Ah[9], P[3], KN, det;
+  pair_quantities_rn(Ai, Aj, mui, muj, 1.0, 1.0, Ah, P, &KN, &det);
+  double sm[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) sm[r][c] = 0.5 * (Ah[3 * r + c] + Ah[3 * c + r]);
+  double lam[3], U[9];
+  jacobi_eig3(sm, lam, U);
+  int64_t total = 0;
+  for (int64_t q = 0; q < n_aux; q += stride) {
+    const double b = beta[q];
+    const double d0 = R[3 * q] - P[0], d1 = R[3 * q + 1] - P[1], d2 = R[3 * q + 2] - P[2];
+    double m[3];
+#pragma unroll
+    for (int c = 0; c < 3; ++c) {
+      const double y = U[c] * d0 + U[3 + c] * d1 + U[6 + c] * d2;
+      m[c] = -kLog2e * b * lam[c] * y * y;
+    }
+    int nodes = GSDFT_NQUAD;
+    double e0 = 0.0;
+    for (int n = 0; n < GSDFT_NQUAD; ++n) {
+      const double t2 = kQuadT2[n];
+      double x = 0.0;
+#pragma unroll
+      for (int c = 0; c < 3; ++c) x += m[c] / fma(t2, lam[c] + b, lam[c] * b);
+      if (n == 0) e0 = x * t2;
+      if (node_check(n) && x * t2 - e0 < -skip2) {
+        nodes = n + 1;
+        break;
+      }
+    }
+    total += nodes + 1;
+  }
+  cost[a] = total;
+}
+
+extern "C" int gsdft_rep_cost(const double* A9, const double* mu, int64_t M, const int32_t* pi,
+                              const int32_t* pj, const int32_t* rep_pos, int64_t n_rep,
+                              const double* beta, const double* R, int64_t n_aux, int64_t n_sample,
+                              int64_t* cost, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n_aux > 0 && n_sample > 0, "bad sizes");
+  if (n_rep == 0) return GSDFT_OK;
+  GSDFT_REQUIRE(A9 && mu && pi && pj && rep_pos && beta && R && cost, "null pointer");
+  const int64_t stride = imax64(1, n_aux / n_sample);
+  rep_cost_kernel<<<grid_1d(n_rep, 128), 128, 0, (cudaStream_t)stream>>>(
+      A9, mu, pi, pj, rep_pos, n_rep, beta, R, n_aux, stride, node_skip_threshold(), cost);
+  GSDFT_LAUNCHED("rep_cost");
+  return GSDFT_OK;
+}
+
 extern "C" int gsdft_pair_prep(const double* A9, const double* mu, const double* N, int64_t M,
                                const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
                                const double* rep_w, int64_t n_rep, const double* C_occ,

@@ -49,6 +49,8 @@ SIGNATURES = {
     "gsdft_pair_plan_workspace_size": (_sz, [_i64, _i64]),
     "gsdft_pair_reps": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _i32, _c_p, _c_p, _c_p, _pi64, _c_p,
                                _sz, _c_p]),
+    "gsdft_rep_cost": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _i64, _i64, _c_p,
+                              _c_p]),
     "gsdft_pair_groups_workspace_size": (_sz, [_i64, _i64]),
     "gsdft_pair_groups": (_i32, [_c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                  _c_p, _sz, _c_p]),

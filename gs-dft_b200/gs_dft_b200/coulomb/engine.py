@@ -62,7 +62,26 @@ class PairPlan:
         return self.r1 - self.r0
 
 
-def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: bool = True):
+def partition_bounds(n_rep: int, world: int, cost=None):
+    """Rank boundaries [r_0 = 0, ..., r_world = n_rep] of the representatives: equal counts, or with
+    ``cost`` (int64 per representative, on any device) contiguous ranges of equal estimated cost
+    (r_k = the number of leading representatives whose cumulative cost is <= k/world of the total).
+    Integer arithmetic throughout, so every rank computes the same cut."""
+    if cost is None or world <= 1 or n_rep == 0:
+        return [n_rep * k // world for k in range(world + 1)]
+    cum = torch.cumsum(cost[:n_rep].to(torch.int64), 0)
+    total = int(cum[-1])
+    targets = torch.tensor([total * k // world for k in range(world + 1)], dtype=torch.int64,
+                           device=cum.device)
+    b = torch.searchsorted(cum, targets, right=True).tolist()
+    b[0], b[-1] = 0, n_rep
+    return [int(x) for x in b]
+
+
+def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: bool = True,
+              cost_fn=None):
+    """The plan of this rank's slice. ``cost_fn(rep_pos, n_rep)`` (optional) returns the int64
+    estimated cost of every representative; the slices then balance cost instead of count."""
     _check.pair_indices(pi, pj, M)
     _check.f64(w, "pair weights", (int(pi.shape[0]),))
     dev = pi.device
@@ -76,7 +95,9 @@ def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: boo
     lib.call("gsdft_pair_reps", ptr(pi), ptr(pj), ptr(w), n, M, int(bool(merge_twins)), ptr(pos),
              ptr(rw), ptr(tw), ctypes.byref(nr), ptr(ws), ws_bytes, stream_handle(dev))
     n_rep = int(nr.value)
-    r0, r1 = n_rep * rank // world, n_rep * (rank + 1) // world
+    cost = cost_fn(pos, n_rep) if (cost_fn is not None and world > 1 and n_rep > 0) else None
+    bounds = partition_bounds(n_rep, world, cost)
+    r0, r1 = bounds[rank], bounds[rank + 1]
     pos, rw, tw = pos[r0:max(r1, r0 + 1)], rw[r0:max(r1, r0 + 1)], tw[r0:max(r1, r0 + 1)]
     k = r1 - r0
     oi = torch.empty(max(k, 1), dtype=torch.int32, device=dev)
@@ -132,10 +153,13 @@ class RIJEngine:
             blocked triangular substitution.
         atoms: optional (n_atoms, 4) float64 device tensor of nuclei (x, y, z, Z) in Bohr: adds the
             screened nuclear attraction E_ne on the same pairs.
+        balance: optional (quat, log_scale, centers) of the splats at refresh: with world > 1 the
+            ranks' slices then carry equal estimated integral cost (``gsdft_rep_cost``: node
+            screening makes distant pairs cheaper), instead of equal representative counts.
     """
 
     def __init__(self, pi, pj, w, M, n_occ, beta=None, R=None, KN=None, L=None, rank=0, world=1,
-                 merge_twins=True, inverse_solve=True, atoms=None):
+                 merge_twins=True, inverse_solve=True, atoms=None, balance=None):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi = pi.to(torch.int32).contiguous()
@@ -152,7 +176,10 @@ class RIJEngine:
         self.n_aux = int(beta.shape[0]) if self.rij else 0
         if not self.rij and atoms is None:
             raise ValueError("RIJEngine needs the aux quantities (beta, R, KN), atoms, or both")
-        self.plan = make_plan(self.pi, self.pj, self.w, self.M, rank, world, merge_twins)
+        cost_fn = None
+        if balance is not None and world > 1 and self.rij:
+            cost_fn = self._cost_fn(*balance)
+        self.plan = make_plan(self.pi, self.pj, self.w, self.M, rank, world, merge_twins, cost_fn)
         dev, nl, n = self.device, self.plan.n_rep, self.plan.n
         e = lambda *s: torch.empty(s, dtype=F64, device=dev)
         self.A9, self.N = e(self.M, 9), e(self.M)
@@ -196,6 +223,18 @@ class RIJEngine:
         # token of the forward whose pair records, gamma and d the buffers hold (a backward after
         # another forward on this engine must re-run its own forward first)
         self.last_forward = None
+
+    def _cost_fn(self, quat, log_scale, centers, n_sample: int = 256):
+        """Estimated cost per representative from the splats' geometry and a sample of the aux."""
+        def fn(rep_pos, n_rep):
+            check_step_inputs(self.M, 0, quat, log_scale, centers)
+            A9, _ = splat_quantities(quat, log_scale)
+            cost = torch.empty(n_rep, dtype=torch.int64, device=self.device)
+            lib.call("gsdft_rep_cost", ptr(A9), ptr(centers), self.M, ptr(self.pi), ptr(self.pj),
+                     ptr(rep_pos), n_rep, ptr(self.beta), ptr(self.R), self.n_aux,
+                     min(n_sample, self.n_aux), ptr(cost), stream_handle(self.device))
+            return cost
+        return fn
 
     def _bracket(self, name):
         if not self.timing:

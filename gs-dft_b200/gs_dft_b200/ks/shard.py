@@ -8,9 +8,10 @@ computes bit-identical replicated values.
 
 Partition: every rank builds the same refresh-time plan of the whole list (live entries, with each
 (i,j)/(j,i) twin merged into one representative) and evaluates a contiguous slice of the
-representatives, equal to within one: every representative costs the same N_aux integrals and
-padding costs nothing, so equal counts are equal work, and contiguity keeps each rank's per-splat
-scatter local. The reference instead deals the padded list round-robin (``stripe_pairs``) because
+representatives. Every representative has N_aux integrals, but node screening makes distant
+(aux, pair) combinations cheaper, so with ``balance`` (the splats at refresh) the slices carry equal
+estimated cost (``gsdft_rep_cost``), else equal counts; padding costs nothing, and contiguity keeps
+each rank's per-splat scatter local. The reference instead deals the padded list round-robin (``stripe_pairs``) because
 its padding is appended; striped lists are accepted too (a stripe only reorders the same pairs).
 
 With ``atoms`` each rank also evaluates the screened nuclear attraction on its slice (the
@@ -36,9 +37,11 @@ class ShardedRIJ:
     """
 
     def __init__(self, pi, pj, valid, M, n_occ, beta, R, KN, L, rank: int, world: int,
-                 group=None, engine_cls=RIJEngine, atoms=None):
+                 group=None, engine_cls=RIJEngine, atoms=None, balance=None):
         self.rank, self.world, self.group = rank, world, group
         kw = {} if atoms is None else {"atoms": atoms}
+        if balance is not None:
+            kw["balance"] = balance
         self.engine = engine_cls(pi.contiguous(), pj.contiguous(), pair_weight(valid).contiguous(),
                                  M, n_occ, beta, R, KN, L, rank=rank, world=world, **kw)
         self.M, self.n_occ = int(M), int(n_occ)

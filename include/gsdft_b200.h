@@ -182,6 +182,17 @@ int gsdft_pair_groups(const int32_t* pi, const int32_t* pj, const int32_t* rep_p
                       int32_t* order_j, int64_t* seg_j, int32_t* partner_j, void* ws,
                       size_t ws_bytes, gsdft_stream_t stream);
 
+/* Estimated integral cost of each representative (int64, n_rep), for partitioning the list across
+ * devices by work: over every (n_aux / n_sample)-th aux, the number of Laplace nodes the integral
+ * kernels' node screening would evaluate for that (aux, pair), plus one for the fixed per-(aux, pair)
+ * work. Integer costs make the prefix sums that cut the list exact, so every rank computes the same
+ * cut. Refresh-time. The north star's "balanced by estimated integral cost"; the reference deals
+ * the padded list round-robin instead (gs_dft/ks/shard.py:146-166). */
+int gsdft_rep_cost(const double* A9, const double* mu, int64_t M, const int32_t* pi,
+                   const int32_t* pj, const int32_t* rep_pos, int64_t n_rep, const double* beta,
+                   const double* R, int64_t n_aux, int64_t n_sample, int64_t* cost,
+                   gsdft_stream_t stream);
+
 /* ---- auxiliary basis, metric, factor ------------------------------------------------------------ */
 
 /* Frozen product aux: per listed pair (pi == NULL: the M self-products), alpha0 = det(A_hat)^(1/3)

@@ -210,3 +210,33 @@ def test_metric_rows_and_inverse_factor_large(g):
     close(float(E2), E_ref)
     close(host(d1), d_ref, rtol=1e-9, atol_rel=1e-11)
     close(host(d2), d_ref, rtol=1e-9, atol_rel=1e-11)
+
+
+def test_cost_balanced_rank_slices(g):
+    """Configuration 2 split over 2 and 8 ranks by estimated cost: the slices are contiguous and
+    cover every representative, the ranks' estimated costs agree to within a few percent, and the
+    ranks' partial gammas sum to the one-device gamma."""
+    from gs_dft_b200.coulomb.engine import make_plan
+    sy, s, pi, pj, v, aux, L = system(g, 2)
+    beta, R, KN = aux.quantities()
+    w = torch.ones(int(pi.shape[0]), dtype=torch.float64, device="cuda")
+    C, occ = dev(sy.C_occ), dev(sy.occ)
+    one = g.RIJEngine(pi, pj, w, sy.M, sy.n_occ, beta, R.contiguous(), KN, L)
+    gam = host(one.forward_local(s.quat, s.log_scale, s.centers, C, occ)).copy()
+    cost = one._cost_fn(s.quat, s.log_scale, s.centers)(one.plan.rep_pos, one.plan.n_rep)
+    cost = host(cost)
+    assert cost.min() > 0
+    for world in (2, 8):
+        total = np.zeros_like(gam)
+        prev = 0
+        rank_cost = []
+        for rank in range(world):
+            eng = g.RIJEngine(pi, pj, w, sy.M, sy.n_occ, beta, R.contiguous(), KN, L, rank=rank,
+                              world=world, balance=(s.quat, s.log_scale, s.centers))
+            assert eng.plan.r0 == prev
+            prev = eng.plan.r1
+            rank_cost.append(int(cost[eng.plan.r0:eng.plan.r1].sum()))
+            total += host(eng.forward_local(s.quat, s.log_scale, s.centers, C, occ))
+        assert prev == one.plan.n_rep_total
+        assert max(rank_cost) / min(rank_cost) < 1.02
+        close(total, gam, rtol=1e-12, atol_rel=1e-14)

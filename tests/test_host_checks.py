@@ -51,3 +51,22 @@ def test_pair_indices_dtype_length_and_range():
         _check.pair_indices(pi - 1, pj, 3, cuda=False)
     with pytest.raises(ValueError, match="CUDA"):
         make_plan(pi, pj, torch.ones(3, dtype=F64), 3)
+
+
+def test_partition_bounds_balance_cost():
+    """Rank boundaries: equal counts without costs; with integer costs, contiguous ranges whose
+    cumulative cost first passes k/world of the total (exact integer arithmetic)."""
+    import torch
+    from gs_dft_b200.coulomb.engine import partition_bounds
+    assert partition_bounds(10, 3) == [0, 3, 6, 10]
+    assert partition_bounds(0, 4) == [0, 0, 0, 0, 0]
+    cost = torch.tensor([10, 1, 1, 1, 1, 1, 1, 1, 1, 2], dtype=torch.int64)   # total 20
+    b = partition_bounds(10, 2, cost)
+    assert b == [0, 1, 10]                     # the first representative alone is half the work
+    rng = torch.Generator().manual_seed(0)
+    cost = torch.randint(1, 40, (1000,), generator=rng, dtype=torch.int64)
+    for world in (2, 3, 8):
+        b = partition_bounds(1000, world, cost)
+        assert b[0] == 0 and b[-1] == 1000 and all(x <= y for x, y in zip(b, b[1:]))
+        sums = [int(cost[b[k]:b[k + 1]].sum()) for k in range(world)]
+        assert max(sums) - min(sums) <= 2 * int(cost.max())
