@@ -37,11 +37,13 @@ class ShardedRIJ:
     """
 
     def __init__(self, pi, pj, valid, M, n_occ, beta, R, KN, L, rank: int, world: int,
-                 group=None, engine_cls=RIJEngine, atoms=None, balance=None):
+                 group=None, engine_cls=RIJEngine, atoms=None, balance=None, inverse_solve=True):
         self.rank, self.world, self.group = rank, world, group
         kw = {} if atoms is None else {"atoms": atoms}
         if balance is not None:
             kw["balance"] = balance
+        if not inverse_solve:
+            kw["inverse_solve"] = False
         self.engine = engine_cls(pi.contiguous(), pj.contiguous(), pair_weight(valid).contiguous(),
                                  M, n_occ, beta, R, KN, L, rank=rank, world=world, **kw)
         self.M, self.n_occ = int(M), int(n_occ)
