@@ -147,13 +147,19 @@ __global__ void pair_density_thread_kernel(const int32_t* __restrict__ pi,
 }
 
 // ------------------------------------------------------------------------------------------------
-// Forward: one aux per thread (registers), pair-record tiles staged in shared memory by bulk copy.
+// Forward: a block holds kFwAux aux functions resident in shared memory for its whole run and
+// streams its slice of the pair representatives past them in chunks of 128, one representative
+// per thread (eigenframe, centre and q KN in registers), two aux at a time per thread. The 32
+// lanes of a warp are 32 consecutive representatives (mostly one row of the lexsorted list, so
+// neighbouring pairs), which keeps node screening's per-warp node count close to the per-pair one.
+// gamma_P is reduced over the warp's lanes by a fixed shuffle tree and accumulated per warp in
+// shared memory; the warps' partial sums are added in warp order at the end. The loop has no
+// block-wide barrier and no asynchronous copy: warps needing different numbers of nodes never wait
+// for each other.
 // ------------------------------------------------------------------------------------------------
-constexpr int kFwThreads = 128;  // aux per CTA
-constexpr int kFwTile = 32;      // pair records per staged tile (32 x 144 B)
-#ifndef GSDFT_FW_NP
-#define GSDFT_FW_NP 2
-#endif
+constexpr int kFwThreads = 128;  // representatives per chunk (one per thread)
+constexpr int kFwWarps = kFwThreads / 32;
+constexpr int kFwAux = 256;      // aux resident per block
 #ifndef GSDFT_FW_EXP2_BITS
 #define GSDFT_FW_EXP2_BITS 6
 #endif
@@ -166,85 +172,83 @@ constexpr int kFwTile = 32;      // pair records per staged tile (32 x 144 B)
 #else
 #define GSDFT_FW_BOUNDS __launch_bounds__(kFwThreads)
 #endif
-constexpr int kFwNP = GSDFT_FW_NP;  // pairs evaluated together per thread (independent chains)
+#ifndef GSDFT_FW_NA
+#define GSDFT_FW_NA 2
+#endif
+constexpr int kFwNA = GSDFT_FW_NA;  // aux evaluated together per thread (independent chains)
 constexpr int kFwBits = GSDFT_FW_EXP2_BITS;  // 2^kFwBits-entry weighted exp2 table per node
 constexpr size_t kFwDynSmem = sizeof(double) * GSDFT_NQUAD * (1 << kFwBits);
+static_assert(kFwAux % kFwNA == 0, "aux groups must tile the resident block");
 
 // Node evaluations of the forward kernel since the last reset: (aux, pair) units times the nodes
 // each evaluated (20 without screening). Read by gsdft_node_evals.
 static __device__ unsigned long long g_fw_node_evals;
 
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
 __global__ void GSDFT_FW_BOUNDS
     j_forward_kernel(const double* __restrict__ rec, int64_t n_live,
                      const double* __restrict__ beta, const double* __restrict__ R,
                      const double* __restrict__ KN, int64_t n_aux, int64_t per_split,
-                     double skip2, double* __restrict__ partial) {
-  __shared__ __align__(128) double tile[2][kFwTile * GSDFT_REC_FIELDS];
-  __shared__ __align__(8) uint64_t bar[2];
+                     int aux_per_block, double skip2, double* __restrict__ partial) {
+  __shared__ double sb[kFwAux], scp[kFwAux], sr0[kFwAux], sr1[kFwAux], sr2[kFwAux];
+  __shared__ double red[kFwWarps][kFwAux];
   extern __shared__ __align__(16) double etab[];  // GSDFT_NQUAD x 2^kFwBits weighted table
   load_wexp2_tables<kFwBits>(etab);
-  const int64_t P = blockIdx.x * (int64_t)kFwThreads + threadIdx.x;
-  const bool has_aux = P < n_aux;
-  const double b = has_aux ? beta[P] : 1.0;
-  const double r0 = has_aux ? R[3 * P] : 0.0;
-  const double r1 = has_aux ? R[3 * P + 1] : 0.0;
-  const double r2 = has_aux ? R[3 * P + 2] : 0.0;
-  const double cP = -kLog2e * b;
-  const bool warp_active = __any_sync(0xffffffffu, has_aux);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t P0 = blockIdx.x * (int64_t)aux_per_block;
+  const int naux = (int)imin64(aux_per_block, n_aux - P0);
+  for (int k = threadIdx.x; k < kFwAux; k += kFwThreads) {
+    const bool in = k < naux;
+    const double b = in ? beta[P0 + k] : 1.0;
+    sb[k] = b;
+    scp[k] = -kLog2e * b;
+    sr0[k] = in ? R[3 * (P0 + k)] : 0.0;
+    sr1[k] = in ? R[3 * (P0 + k) + 1] : 0.0;
+    sr2[k] = in ? R[3 * (P0 + k) + 2] : 0.0;
+#pragma unroll
+    for (int w = 0; w < kFwWarps; ++w) red[w][k] = 0.0;
+  }
+  __syncthreads();  // tables and the resident aux; the only block-wide barrier before the end
   const int64_t a0 = blockIdx.y * per_split;
   const int64_t a1 = imin64(a0 + per_split, n_live);
-  const int64_t npairs = a1 > a0 ? a1 - a0 : 0;
-  const int ntiles = (int)((npairs + kFwTile - 1) / kFwTile);
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
-  }
-  __syncthreads();
-  auto issue = [&](int t) {
-    int64_t s = a0 + (int64_t)t * kFwTile;
-    int cnt = (int)imin64(kFwTile, a1 - s);
-    uint32_t bytes = (uint32_t)cnt * GSDFT_REC_FIELDS * sizeof(double);
-    fence_proxy_async();
-    mbar_expect_tx(&bar[t & 1], bytes);
-    bulk_g2s(tile[t & 1], rec + s * GSDFT_REC_FIELDS, bytes, &bar[t & 1]);
-  };
-  if (threadIdx.x == 0) {
-    if (ntiles > 0) issue(0);
-    if (ntiles > 1) issue(1);
-  }
-
-  double acc = 0.0;
-  unsigned long long evals = 0;  // node evaluations per real (aux, pair), warp-uniform
-  bool ok = true;
-  for (int t = 0; t < ntiles && ok; ++t) {
-    // block-uniform: a thread whose bounded wait ran out takes the whole block out of the loop
-    ok = __syncthreads_and(mbar_wait(&bar[t & 1], (t >> 1) & 1));
-    if (!ok) break;
-    const double* tl = tile[t & 1];
-    const int cnt = (int)imin64(kFwTile, a1 - (a0 + (int64_t)t * kFwTile));
-    // a warp with no aux (the tail of the last aux tile) only takes part in the barriers
-    for (int k = 0; warp_active && k < cnt; k += kFwNP) {
-      double m[kFwNP][3], g[kFwNP][3], h[kFwNP][3], qk[kFwNP], coul[kFwNP], e0[kFwNP];
+  const int ngroups = (naux + kFwNA - 1) / kFwNA;
+  unsigned long long evals = 0;  // node evaluations of real (aux, pair) units, warp-uniform
+  for (int64_t c0 = a0; c0 < a1; c0 += kFwThreads) {
+    const int64_t a = c0 + threadIdx.x;
+    const bool live = a < a1;
+    const unsigned lanes = __popc(__ballot_sync(0xffffffffu, live));
+    if (lanes == 0) continue;  // warp-uniform: the tail chunk's empty warps
+    const double* rr = rec + (live ? a : a0) * GSDFT_REC_FIELDS;
+    double L[3], U[9], Pc[3];
 #pragma unroll
-      for (int p = 0; p < kFwNP; ++p) {
-        const int kk = k + p < cnt ? k + p : k;  // a duplicate of pair k stands in, weight 0
-        const double* rr = tl + kk * GSDFT_REC_FIELDS;
-        const double d0 = r0 - rr[GSDFT_REC_P0];
-        const double d1 = r1 - rr[GSDFT_REC_P1];
-        const double d2 = r2 - rr[GSDFT_REC_P2];
+    for (int k = 0; k < 3; ++k) L[k] = rr[GSDFT_REC_L0 + k];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) U[k] = rr[GSDFT_REC_U00 + k];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) Pc[k] = rr[GSDFT_REC_P0 + k];
+    const double qk = live ? rr[GSDFT_REC_QK] : 0.0;  // a tail lane stands in with weight 0
+#pragma unroll 1
+    for (int grp = 0; grp < ngroups; ++grp) {
+      double m[kFwNA][3], g[kFwNA][3], h[kFwNA][3], coul[kFwNA], e0[kFwNA];
+#pragma unroll
+      for (int u = 0; u < kFwNA; ++u) {
+        const int k = grp * kFwNA + u;  // k < kFwAux always; beyond naux a dummy aux, dropped
+        const double b = sb[k], cP = scp[k];
+        const double d0 = sr0[k] - Pc[0], d1 = sr1[k] - Pc[1], d2 = sr2[k] - Pc[2];
 #pragma unroll
         for (int c = 0; c < 3; ++c) {
-          const double y = rr[GSDFT_REC_U00 + c] * d0 + rr[GSDFT_REC_U10 + c] * d1 +
-                           rr[GSDFT_REC_U20 + c] * d2;
-          const double L = rr[GSDFT_REC_L0 + c];
-          m[p][c] = (cP * L) * (y * y);
-          g[p][c] = L * b;
-          h[p][c] = L + b;
+          const double y = U[c] * d0 + U[3 + c] * d1 + U[6 + c] * d2;
+          m[u][c] = (cP * L[c]) * (y * y);
+          g[u][c] = L[c] * b;
+          h[u][c] = L[c] + b;
         }
-        qk[p] = k + p < cnt ? rr[GSDFT_REC_QK] : 0.0;
-        coul[p] = 0.0;
-        e0[p] = 0.0;
+        coul[u] = 0.0;
+        e0[u] = 0.0;
       }
       int nodes = GSDFT_NQUAD;
 #pragma unroll
@@ -252,20 +256,20 @@ __global__ void GSDFT_FW_BOUNDS
         const double t2 = kQuadT2[n];
         bool far = node_check(n);  // tested at the check nodes only (the exponent is monotone)
 #pragma unroll
-        for (int p = 0; p < kFwNP; ++p) {
-          const double G0 = fma(t2, h[p][0], g[p][0]);
-          const double G1 = fma(t2, h[p][1], g[p][1]);
-          const double G2 = fma(t2, h[p][2], g[p][2]);
+        for (int u = 0; u < kFwNA; ++u) {
+          const double G0 = fma(t2, h[u][0], g[u][0]);
+          const double G1 = fma(t2, h[u][1], g[u][1]);
+          const double G2 = fma(t2, h[u][2], g[u][2]);
           const double p12 = G1 * G2;
           const double prod = G0 * p12;
-          const double num = fma(m[p][0], p12, G0 * fma(m[p][1], G2, m[p][2] * G1));
+          const double num = fma(m[u][0], p12, G0 * fma(m[u][1], G2, m[u][2] * G1));
           const double y = rsqrt_pos(prod);
           const double inv = y * y;
           const double x = num * inv;  // node exponent / t^2, log2 units
           const double ew = wexp2<kFwBits>(x, t2, etab + (n << kFwBits));
-          coul[p] = fma(y, ew, coul[p]);
-          if (n == 0) e0[p] = x * t2;
-          if (node_check(n)) far = far && fma(x, t2, -e0[p]) < -skip2;
+          coul[u] = fma(y, ew, coul[u]);
+          if (n == 0) e0[u] = x * t2;
+          if (node_check(n)) far = far && fma(x, t2, -e0[u]) < -skip2;
         }
         // node screening (warp-uniform): every later node is below the last bit of every lane's sum
         if (node_check(n) && __all_sync(0xffffffffu, far)) {
@@ -273,16 +277,26 @@ __global__ void GSDFT_FW_BOUNDS
           break;
         }
       }
-      evals += (unsigned long long)nodes * (unsigned long long)imin64(kFwNP, cnt - k);
+      const int real = (int)imin64(kFwNA, naux - grp * kFwNA);
+      evals += (unsigned long long)nodes * (unsigned long long)(real * lanes);
+      // gamma_k += sum over the warp's representatives (fixed shuffle tree), per warp in order
+      double v[kFwNA];
 #pragma unroll
-      for (int p = 0; p < kFwNP; ++p) acc = fma(qk[p], coul[p], acc);
+      for (int u = 0; u < kFwNA; ++u) v[u] = warp_sum(qk * coul[u]);
+      if (lane == 0) {
+#pragma unroll
+        for (int u = 0; u < kFwNA; ++u) red[warp][grp * kFwNA + u] += v[u];
+      }
     }
-    __syncthreads();  // every thread is done with this buffer
-    if (threadIdx.x == 0 && t + 2 < ntiles) issue(t + 2);
   }
-  if (has_aux) partial[blockIdx.y * n_aux + P] = ok ? acc * KN[P] : __longlong_as_double(-1LL);
-  const unsigned lanes = __popc(__ballot_sync(0xffffffffu, has_aux));
-  if ((threadIdx.x & 31) == 0 && lanes) atomicAdd(&g_fw_node_evals, evals * lanes);
+  __syncthreads();
+  for (int k = threadIdx.x; k < naux; k += kFwThreads) {
+    double acc = red[0][k];
+#pragma unroll
+    for (int w = 1; w < kFwWarps; ++w) acc += red[w][k];
+    partial[blockIdx.y * n_aux + P0 + k] = acc * KN[P0 + k];
+  }
+  if (lane == 0 && evals) atomicAdd(&g_fw_node_evals, evals);
 }
 
 // gamma_P = sum_s partial[s][P], fixed order.
@@ -303,8 +317,18 @@ __global__ void sum_splits_kernel(const double* __restrict__ partial, int S, int
   out[P] = (a0 + a1) + (a2 + a3);
 }
 
-// Pair splits of the forward grid: aux tiles x S CTAs filling whole waves of resident CTAs, with at
-// least two pair tiles per split. The occupancy query runs once (a thread-safe static).
+// Aux per block: the fewest blocks of at most kFwAux, equally sized (a multiple of kFwNA), so that no
+// block is left with a short remainder while the others run full.
+static int forward_aux_per_block(int64_t n_aux) {
+  const int64_t blocks = (n_aux + kFwAux - 1) / kFwAux;
+  int64_t per = (n_aux + blocks - 1) / blocks;
+  per = (per + kFwNA - 1) / kFwNA * kFwNA;
+  return (int)imin64(per, kFwAux);
+}
+
+// Pair splits of the forward grid: aux blocks x S CTAs filling whole waves of resident CTAs, with at
+// least two chunks of representatives per split. The occupancy query runs once (a thread-safe
+// static).
 static int forward_splits(int64_t n_live, int64_t n_aux) {
   static const int per_sm = [] {
     int v = 0;
@@ -313,10 +337,11 @@ static int forward_splits(int64_t n_live, int64_t n_aux) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, j_forward_kernel, kFwThreads, kFwDynSmem);
     return v > 0 ? v : 1;
   }();
-  int64_t aux_tiles = (n_aux + kFwThreads - 1) / kFwThreads;
+  const int apb = forward_aux_per_block(n_aux);
+  int64_t aux_blocks = (n_aux + apb - 1) / apb;
   int64_t cap = (int64_t)device_sms() * per_sm;
-  int64_t max_s = imin64(4096, imax64(1, n_live / (2 * kFwTile)));
-  return best_splits(aux_tiles, cap, max_s);
+  int64_t max_s = imin64(4096, imax64(1, n_live / (2 * kFwThreads)));
+  return best_splits(aux_blocks, cap, max_s);
 }
 
 }  // namespace gsdft
@@ -479,10 +504,11 @@ extern "C" int gsdft_j_forward(const double* rec, int64_t n_live, const double* 
   double* partial = c.take<double>((size_t)S * n_aux);
   if (!c.ok) return fail(GSDFT_ERR_ARG, "forward workspace too small (%zu < %zu)", ws_bytes, c.off);
   int64_t per_split = (n_live + S - 1) / S;
-  per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
-  dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
+  const int apb = forward_aux_per_block(n_aux);
+  dim3 grid((unsigned)((n_aux + apb - 1) / apb), (unsigned)S);
   j_forward_kernel<<<grid, kFwThreads, kFwDynSmem, st>>>(rec, n_live, beta, R, KN, n_aux,
-                                                         per_split, node_skip_threshold(), partial);
+                                                         per_split, apb, node_skip_threshold(),
+                                                         partial);
   GSDFT_LAUNCHED("j_forward");
   sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(partial, S, n_aux, gamma);
   GSDFT_LAUNCHED("sum_splits");
@@ -553,10 +579,10 @@ extern "C" int gsdft_j_forward_noalloc(const double* rec, int64_t n_rep, const d
   int64_t S = forward_splits(n_rep, n_aux);
   S = imin64(S, kNoAllocScratchDoubles / n_aux);
   int64_t per_split = (n_rep + S - 1) / S;
-  per_split = (per_split + kFwNP - 1) / kFwNP * kFwNP;
-  dim3 grid((unsigned)((n_aux + kFwThreads - 1) / kFwThreads), (unsigned)S);
+  const int apb = forward_aux_per_block(n_aux);
+  dim3 grid((unsigned)((n_aux + apb - 1) / apb), (unsigned)S);
   j_forward_kernel<<<grid, kFwThreads, kFwDynSmem, st>>>(rec, n_rep, beta, R, KN, n_aux, per_split,
-                                                         node_skip_threshold(), scratch);
+                                                         apb, node_skip_threshold(), scratch);
   GSDFT_LAUNCHED("j_forward_noalloc");
   sum_splits_kernel<<<grid_1d(n_aux, 256), 256, 0, st>>>(scratch, (int)S, n_aux, gamma);
   GSDFT_LAUNCHED("sum_splits_noalloc");
