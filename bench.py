@@ -40,10 +40,13 @@ FLOP_FWD, FLOP_VJP = 706, 2050
 FLOP_FWD_FIXED, FLOP_FWD_NODE = 26, 34
 FLOP_VJP_FIXED, FLOP_VJP_NODE = 70, 99
 FP64_DATASHEET = 37e12
-# DRAM bytes (read + write) per launch of each integral kernel from one ncu capture of this bench
-# at configuration 1 on one GPU. Only that workload has a capture; other configs and N > 1 report
-# null.
-NCU_TRAFFIC_CFG1_N1 = {"j_vjp_kernel": 22.364160e6 + 65.776128e6, "j_forward_kernel": 21.477120e6}
+# DRAM bytes (read + write) per launch of each integral kernel, from one ncu capture (1-pass
+# dram__bytes metrics) of this bench's own workload on one GPU, per configuration. Only the
+# captured workloads are filled; others (and N > 1, whose slices change the reverse kernel's split
+# count) report null.
+NCU_TRAFFIC_N1 = {
+    3: {"j_vjp_kernel": 1065.27e6 + 757.69e6, "j_forward_kernel": 8032.55e6 + 50.20e6},
+}
 L2_FLUSH_BYTES = 256 << 20
 # FP64 work per (pair, atom) unit of the screened nuclear attraction kernel with its reverse sums,
 # counted from gsdft_vne's operations (FMA = 2): 20 nodes x 50, y and m in two node passes 48, the
@@ -447,8 +450,9 @@ def main():
                                        f"{FLOP_FWD_FIXED} + {FLOP_FWD_NODE}/node forward)"),
                      "nodes_per_unit": nodes_per_unit,
                      "achieved_20node_equivalent": flop_20 / (t_dom * 1e-3) / 1e12,
-                     "traffic": (NCU_TRAFFIC_CFG1_N1[dom] if (args.config == 1 and world == 1
-                                                              and not args.pairs) else None),
+                     "traffic": (NCU_TRAFFIC_N1[args.config][dom]
+                                 if (args.config in NCU_TRAFFIC_N1 and world == 1
+                                     and not args.pairs) else None),
                      "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + write.sum)",
                      "algorithmic_bytes": alg_bytes},
         "gpu_launches": int(launches),
