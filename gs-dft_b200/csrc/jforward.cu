@@ -159,7 +159,10 @@ __global__ void pair_density_thread_kernel(const int32_t* __restrict__ pi,
 // ------------------------------------------------------------------------------------------------
 constexpr int kFwThreads = 128;  // representatives per chunk (one per thread)
 constexpr int kFwWarps = kFwThreads / 32;
-constexpr int kFwAux = 256;      // aux resident per block
+#ifndef GSDFT_FW_AUX
+#define GSDFT_FW_AUX 256
+#endif
+constexpr int kFwAux = GSDFT_FW_AUX;  // aux resident per block (at most)
 #ifndef GSDFT_FW_EXP2_BITS
 #define GSDFT_FW_EXP2_BITS 6
 #endif
