@@ -18,15 +18,31 @@ With ``atoms`` each rank also evaluates the screened nuclear attraction on its s
 reference's ``screened_external_energy`` on the local stripe, psum'd: gs_dft/ks/shard.py:223,
 267); its partial E_ne travels in one extra slot of the packed gradient allreduce, so the step
 keeps two collectives.
+
+Failure detection (the reference configures distributed-init timeouts, gs_dft/ks/shard.py:90-93):
+with ``heartbeat`` (seconds), every step starts with a host-side liveness check of all ranks over a
+gloo side group (``monitored_barrier``, which names the ranks that did not arrive), so a rank that
+failed or left between steps is reported as ``PeerFailure`` before any kernel or collective of the
+step is launched; an error raised by a collective itself (the process group's timeout) is reported
+as ``PeerFailure`` too. A rank leaves only between steps, never with its kernels or collectives in
+flight.
 """
 from __future__ import annotations
+
+from datetime import timedelta
 
 import torch
 
 from ..coulomb.engine import RIJEngine
 from ..screening.pairs import pair_weight, stripe_pairs
 
-__all__ = ["ShardedRIJ", "stripe_pairs"]
+__all__ = ["PeerFailure", "ShardedRIJ", "stripe_pairs"]
+
+
+class PeerFailure(RuntimeError):
+    """Another rank did not take part in a step: it failed, exited, or hung before the step's
+    collectives. Raised on the host before this rank launches the step's kernels (liveness check)
+    or when a collective ends with an error (the process group's timeout)."""
 
 
 class ShardedRIJ:
@@ -37,8 +53,15 @@ class ShardedRIJ:
     """
 
     def __init__(self, pi, pj, valid, M, n_occ, beta, R, KN, L, rank: int, world: int,
-                 group=None, engine_cls=RIJEngine, atoms=None, balance=None, inverse_solve=True):
+                 group=None, engine_cls=RIJEngine, atoms=None, balance=None, inverse_solve=True,
+                 heartbeat: float | None = None):
         self.rank, self.world, self.group = rank, world, group
+        self.heartbeat = heartbeat
+        self._hb_group = None
+        if heartbeat is not None and world > 1:
+            import torch.distributed as dist
+            # monitored_barrier needs gloo: a side group for the liveness check on any backend
+            self._hb_group = dist.new_group(backend="gloo")
         kw = {} if atoms is None else {"atoms": atoms}
         if balance is not None:
             kw["balance"] = balance
@@ -82,7 +105,23 @@ class ShardedRIJ:
     def _allreduce(self, t):
         if self.world > 1:
             import torch.distributed as dist
-            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+            try:
+                dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+            except RuntimeError as exc:   # a peer left or hung: the collective timed out or broke
+                raise PeerFailure(f"rank {self.rank}: allreduce failed: {exc}") from exc
+
+    def check_peers(self):
+        """Host-side liveness check of every rank (no-op without ``heartbeat`` or on one rank):
+        returns when all ranks reached it, raises ``PeerFailure`` naming the missing ones after
+        ``heartbeat`` seconds."""
+        if self._hb_group is None:
+            return
+        import torch.distributed as dist
+        try:
+            dist.monitored_barrier(group=self._hb_group, timeout=timedelta(seconds=self.heartbeat),
+                                   wait_all_ranks=True)
+        except RuntimeError as exc:
+            raise PeerFailure(f"rank {self.rank}: liveness check failed: {exc}") from exc
 
     def _outputs(self, E, d, g_quat, g_log):
         M, eng = self.M, self.engine
@@ -94,6 +133,7 @@ class ShardedRIJ:
         return out
 
     def step(self, quat, log_scale, centers, C_occ, occ, grad=True):
+        self.check_peers()
         gamma = self._forward(quat, log_scale, centers, C_occ, occ)
         self._allreduce(gamma)
         if not grad:
@@ -149,6 +189,7 @@ class _SegmentedStep:
         """One step; with ``phases`` (six events from ``phase_events``) each segment and each
         allreduce is bracketed on the current stream."""
         sh = self.sh
+        sh.check_peers()
         rec = (lambda k: phases[k].record()) if phases is not None else (lambda k: None)
         rec(0)
         gamma = self.gA.replay()

@@ -148,3 +148,51 @@ def test_two_rank_gloo_equals_single_rank(tmp_path, with_atoms):
         for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
             want = rj[k] + rn[k]
             np.testing.assert_allclose(one[k], want, rtol=1e-10, atol=1e-12 * np.abs(want).max())
+
+
+def _run_leave(rank, world, port, out, mode):
+    """Both ranks take one step; then rank 1 leaves (exits, or stalls past the liveness timeout)
+    and rank 0 tries the next step. Rank 0 records what happened and how long it took."""
+    import time
+    from datetime import timedelta
+    import torch.distributed as dist
+    from gs_dft_b200.ks.shard import PeerFailure, ShardedRIJ
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    s, pi, pj, v, aq, L = _problem()
+    T = torch.from_numpy
+    sh = ShardedRIJ(T(pi), T(pj), T(v), s.M, s.n_occ, T(aq[0]), T(aq[1]), T(aq[2]), T(L), rank,
+                    world, engine_cls=OracleEngine, heartbeat=3.0)
+    args = (T(s.quat), T(s.log_scale), T(s.centers), T(s.C_occ), T(s.occ))
+    E1 = float(sh.step(*args)["E"][0])
+    if rank == 1:
+        if mode == "stall":
+            time.sleep(10.0)
+        os._exit(0)                       # leaves between steps, nothing in flight
+    t0 = time.time()
+    try:
+        sh.step(*args)
+        res = "completed"
+    except PeerFailure as exc:
+        res = f"PeerFailure {exc}"
+    with open(out, "w") as f:
+        f.write(f"{E1!r}\n{time.time() - t0:.2f}\n{res}\n")
+    os._exit(0)                           # the group has a dead member: skip its teardown
+
+
+@pytest.mark.timeout(180)
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_peer_that_leaves_is_reported_not_waited_for(tmp_path, mode):
+    """A rank that exits, or stalls, between steps: the surviving rank's next step raises
+    PeerFailure from the host-side liveness check (3 s limit) before it launches anything, instead
+    of waiting in a collective."""
+    import torch.multiprocessing as mp
+    out = str(tmp_path / "leave.txt")
+    mp.start_processes(_run_leave, args=(2, _free_port(), out, mode), nprocs=2,
+                       start_method="spawn")
+    E1, dt, res = open(out).read().splitlines()
+    assert np.isfinite(float(E1))
+    assert res.startswith("PeerFailure"), res
+    assert float(dt) < 20.0
+    if mode == "stall":
+        assert "1" in res                  # the liveness check names the missing rank
