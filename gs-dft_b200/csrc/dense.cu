@@ -477,9 +477,218 @@ int trsv_llt(const double* L, int64_t n, double* d, cudaStream_t st) {
   return GSDFT_OK;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Orbital contractions on the pair list, as dense DMMA tiles over row blocks (gs_dft/coulomb/
+// ri.py:456 and its gradient). The splats are cut into blocks of 64 consecutive rows; block b's
+// partner list J_b is the sorted set of splats paired with its rows (consecutive splats sit on the
+// same atoms, so their neighbour sets nearly coincide and the 64 x |J_b| block is mostly live).
+// SDDMM: Q_b = (C_I diag(occ)) C_J^T into the block's dense tile, from which each representative
+//   reads its q (one cell per representative).
+// SpMM:  G_I (+)= T_b (C_J diag(occ)) with T_b the block's dense tile of per-representative values
+//   (J w), giving g_C row by row.
+// The partner rows of C are gathered by index inside the tile loads; every sum has a fixed order.
+// ------------------------------------------------------------------------------------------------
+struct BlockArgs {
+  const double* C;        // (M, n_occ)
+  const double* occ;      // (n_occ)
+  int64_t M, n_occ;
+  const int64_t* boff;    // per block: offset of its dense tile (elements), rows x nj
+  const int32_t* nj;      // per block: partners
+  const int64_t* joff;    // per block: offset into jidx
+  const int32_t* jidx;    // concatenated partner lists
+  double* buf;            // the blocks' dense tiles
+  double* out;            // SpMM: g_C (M, n_occ)
+  double beta;            // SpMM: out = beta out + tile products
+};
+
+// kSpmm = false (SDDMM): tile (64 rows of block b) x (64 partners), K = n_occ.
+// kSpmm = true (SpMM): tile (64 rows of block b) x (64 orbitals), K = nj_b.
+template <bool kSpmm>
+__global__ void __launch_bounds__(128) block_contract_kernel(BlockArgs g) {
+  const int64_t b = blockIdx.z;
+  const int64_t r0 = b * kGT;
+  const int64_t M = imin64(kGT, g.M - r0);
+  const int64_t nj = g.nj[b];
+  const int64_t N = kSpmm ? g.n_occ : nj;
+  const int64_t K = kSpmm ? nj : g.n_occ;
+  const int64_t n0 = (int64_t)blockIdx.x * kGT;
+  if (M <= 0 || n0 >= N) return;
+  const int32_t* __restrict__ J = g.jidx + g.joff[b];
+  double* __restrict__ T = g.buf + g.boff[b];
+
+  // A as [m][k]; B as [k][n] (SpMM: C_J rows) or [n][k] (SDDMM: C_J rows as the transposed operand)
+  __shared__ double As[kGT][kGK + kGPad];
+  __shared__ double Bs[kSpmm ? kGK : kGT][(kSpmm ? kGT : kGK) + kGPad];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+  const int ar = tid >> 1, ac = (tid & 1) * 8;
+  const int br = kSpmm ? (tid >> 3) : (tid >> 1), bc = kSpmm ? (tid & 7) * 8 : (tid & 1) * 8;
+  double ra[8], rb[8];
+
+  auto load = [&](int64_t k0) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int64_t r = ar, c = k0 + ac + e;
+      double v = 0.0;
+      if (r < M && c < K) {
+        if (kSpmm) v = T[r * nj + c];                                  // the block's tile
+        else v = g.C[(r0 + r) * g.n_occ + c] * g.occ[c];             // C_I diag(occ)
+      }
+      ra[e] = v;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      double v = 0.0;
+      if (kSpmm) {  // stored (k, n): row k is partner J[k], column n an orbital
+        const int64_t k = k0 + br, n = n0 + bc + e;
+        if (k < K && n < N) v = g.C[(int64_t)J[k] * g.n_occ + n] * g.occ[n];
+      } else {      // stored (n, k): row n is partner J[n], column k an orbital
+        const int64_t n = n0 + br, k = k0 + bc + e;
+        if (n < N && k < K) v = g.C[(int64_t)J[n] * g.n_occ + k];
+      }
+      rb[e] = v;
+    }
+  };
+  auto store = [&]() {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) As[ar][ac + e] = ra[e];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) Bs[br][bc + e] = rb[e];
+  };
+
+  double acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[i][j][r] = 0.0;
+  load(0);
+  store();
+  __syncthreads();
+  for (int64_t k0 = 0; k0 < K; k0 += kGK) {
+    const bool more = k0 + kGK < K;
+    if (more) load(k0 + kGK);
+#pragma unroll
+    for (int kk = 0; kk < kGK; kk += 4) {
+      double a0[2], a1[2], bv[4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int m = wm + mi * 16 + gq;
+        a0[mi] = As[m][kk + tq];
+        a1[mi] = As[m + 8][kk + tq];
+      }
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int n = wn + ni * 8 + gq;
+        bv[ni] = kSpmm ? Bs[kk + tq][n] : Bs[n][kk + tq];
+      }
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni) dmma_m16n8k4(acc[mi][ni], a0[mi], a1[mi], bv[ni]);
+    }
+    __syncthreads();
+    if (more) {
+      store();
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int64_t row = wm + mi * 16 + gq + (r >> 1) * 8;
+        const int64_t col = n0 + wn + ni * 8 + 2 * tq + (r & 1);
+        if (row < M && col < N) {
+          if (kSpmm) {
+            double* p = g.out + (r0 + row) * g.n_occ + col;
+            *p = g.beta == 0.0 ? acc[mi][ni][r] : fma(g.beta, *p, acc[mi][ni][r]);
+          } else {
+            T[row * nj + col] = acc[mi][ni][r];
+          }
+        }
+      }
+}
+
+// rec[a].q = w_a Q[cell_a] and rec[a].qk = q KN pref, after the SDDMM.
+__global__ void block_q_gather_kernel(const double* __restrict__ buf, const int64_t* __restrict__ cell,
+                                      const double* __restrict__ rep_w, int64_t n_rep,
+                                      double* __restrict__ rec) {
+  const int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a >= n_rep) return;
+  const double q = rep_w[a] * buf[cell[a]];
+  double* r = rec + a * GSDFT_REC_FIELDS;
+  r[GSDFT_REC_Q] = q;
+  r[GSDFT_REC_QK] = q * r[GSDFT_REC_KN];
+}
+
+// buf[cell_a] = v_a (every other cell zero), before an SpMM.
+__global__ void block_scatter_kernel(const double* __restrict__ v, const int64_t* __restrict__ cell,
+                                     int64_t n, double* __restrict__ buf) {
+  const int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (a < n) buf[cell[a]] = v[a];
+}
+
+static int block_launch(bool spmm, const BlockArgs& g, int64_t n_blocks, int64_t max_nj,
+                        cudaStream_t st) {
+  if (n_blocks <= 0) return GSDFT_OK;
+  GSDFT_REQUIRE(n_blocks <= 65535, "too many row blocks for one launch");
+  const int64_t ncols = spmm ? g.n_occ : max_nj;
+  if (ncols <= 0) return GSDFT_OK;
+  dim3 grid((unsigned)((ncols + kGT - 1) / kGT), 1, (unsigned)n_blocks);
+  if (spmm) block_contract_kernel<true><<<grid, 128, 0, st>>>(g);
+  else block_contract_kernel<false><<<grid, 128, 0, st>>>(g);
+  GSDFT_LAUNCHED("block_contract");
+  return GSDFT_OK;
+}
+
 }  // namespace gsdft
 
 using namespace gsdft;
+
+extern "C" int gsdft_block_density(const double* C_occ, const double* occ, int64_t M,
+                                   int64_t n_occ, int64_t n_blocks, const int64_t* boff,
+                                   const int32_t* nj, const int64_t* joff, const int32_t* jidx,
+                                   int64_t max_nj, const int64_t* cell, const double* rep_w,
+                                   int64_t n_rep, double* buf, double* rec,
+                                   gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_occ > 0 && n_blocks == (M + kGT - 1) / kGT && n_rep >= 0 && max_nj >= 0,
+                "bad sizes");
+  GSDFT_REQUIRE(C_occ && occ && boff && nj && joff && buf, "null pointer");
+  GSDFT_REQUIRE(n_rep == 0 || (jidx && cell && rep_w && rec), "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  BlockArgs g{C_occ, occ, M, n_occ, boff, nj, joff, jidx, buf, nullptr, 0.0};
+  int rc = block_launch(false, g, n_blocks, max_nj, st);
+  if (rc || n_rep == 0) return rc;
+  block_q_gather_kernel<<<grid_1d(n_rep, 256), 256, 0, st>>>(buf, cell, rep_w, n_rep, rec);
+  GSDFT_LAUNCHED("block_q_gather");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_block_density_grad(const double* vals, const int64_t* cell, int64_t n_rep,
+                                        const double* C_occ, const double* occ, int64_t M,
+                                        int64_t n_occ, int64_t n_blocks, const int64_t* boff,
+                                        const int32_t* nj, const int64_t* joff,
+                                        const int32_t* jidx, int64_t buf_len, double* buf,
+                                        double beta, double* g_C, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(M > 0 && n_occ > 0 && n_blocks == (M + kGT - 1) / kGT && n_rep >= 0 &&
+                    buf_len >= 0,
+                "bad sizes");
+  GSDFT_REQUIRE(C_occ && occ && boff && nj && joff && g_C && (buf_len == 0 || buf), "null pointer");
+  GSDFT_REQUIRE(n_rep == 0 || (vals && cell && jidx), "null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (buf_len > 0) GSDFT_CUDA(cudaMemsetAsync(buf, 0, (size_t)buf_len * sizeof(double), st));
+  if (n_rep > 0) {
+    block_scatter_kernel<<<grid_1d(n_rep, 256), 256, 0, st>>>(vals, cell, n_rep, buf);
+    GSDFT_LAUNCHED("block_scatter");
+  }
+  BlockArgs g{C_occ, occ, M, n_occ, boff, nj, joff, jidx, buf, g_C, beta};
+  return block_launch(true, g, n_blocks, 0, st);
+}
 
 extern "C" int gsdft_dense_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                                 double alpha, const double* A, int64_t lda, const double* B,

@@ -39,6 +39,10 @@ SIGNATURES = {
                                 _i32]),
     "gsdft_dense_gemm": (_i32, [_i32, _i32, _i64, _i64, _i64, _f64, _c_p, _i64, _c_p, _i64, _f64,
                                 _c_p, _i64, _c_p]),
+    "gsdft_block_density": (_i32, [_c_p, _c_p, _i64, _i64, _i64, _c_p, _c_p, _c_p, _c_p, _i64, _c_p,
+                                   _c_p, _i64, _c_p, _c_p, _c_p]),
+    "gsdft_block_density_grad": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _i64, _i64, _i64, _c_p, _c_p,
+                                        _c_p, _c_p, _i64, _c_p, _f64, _c_p, _c_p]),
     "gsdft_splat_quantities": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _c_p]),
     "gsdft_chart_vjp": (_i32, [_c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p]),
     "gsdft_pairs_workspace_size": (_sz, [_i64, _i64]),

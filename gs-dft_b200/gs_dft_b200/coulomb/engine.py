@@ -114,6 +114,53 @@ def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: boo
                     order_i=oi, seg_i=si, partner_i=qi, order_j=oj, seg_j=sj, partner_j=qj)
 
 
+# Orbital counts from which q and g_C run as dense DMMA tiles over 64-splat row blocks
+# (gsdft_block_density / gsdft_block_density_grad); below it, per-pair kernels.
+BLOCK_MIN_OCC = 64
+
+
+@dataclass
+class RowBlocks:
+    """Row blocks of 64 consecutive splats over this device's representatives: block b's sorted
+    partner list J_b (the splats its rows pair with), and each representative's cell in the blocks'
+    dense tiles (row = its own splat, column = its partner's place in J_b)."""
+
+    n_blocks: int
+    boff: torch.Tensor   # int64 (n_blocks): tile offsets
+    nj: torch.Tensor     # int32 (n_blocks)
+    joff: torch.Tensor   # int64 (n_blocks)
+    jidx: torch.Tensor   # int32: concatenated partner lists
+    cell: torch.Tensor   # int64 (n_rep)
+    max_nj: int
+    buf_len: int
+
+
+def row_blocks(rows, partners, M: int) -> RowBlocks:
+    """The block structure of representatives (rows[a], partners[a]) (int tensors on the device):
+    exact integer sorting (torch.unique), identical on every call."""
+    dev = rows.device
+    nb = (M + 63) // 64
+    r = rows.to(torch.int64)
+    key = (r // 64) * M + partners.to(torch.int64)
+    if key.numel() == 0:
+        z64 = torch.zeros(nb, dtype=torch.int64, device=dev)
+        return RowBlocks(nb, z64, z64.to(torch.int32), z64, torch.zeros(1, dtype=torch.int32,
+                         device=dev), torch.zeros(1, dtype=torch.int64, device=dev), 0, 0)
+    uniq, inv = torch.unique(key, sorted=True, return_inverse=True)
+    blk_u = uniq // M
+    nj = torch.bincount(blk_u, minlength=nb)
+    joff = torch.cumsum(nj, 0) - nj
+    rows_b = torch.clamp(M - 64 * torch.arange(nb, device=dev, dtype=torch.int64), max=64)
+    sizes = rows_b * nj
+    boff = torch.cumsum(sizes, 0) - sizes
+    b = r // 64
+    col = inv - joff[b]
+    cell = boff[b] + (r - 64 * b) * nj[b] + col
+    return RowBlocks(nb, boff.contiguous(), nj.to(torch.int32).contiguous(), joff.contiguous(),
+                     (uniq % M).to(torch.int32).contiguous(), cell.contiguous(),
+                     int(nj.max()), int(sizes.sum()))
+
+
 def check_step_inputs(M, n_occ, quat, log_scale, centers, C_occ=None, occ=None):
     """The per-step parameters as the kernels read them: contiguous float64 CUDA tensors of the
     engine's sizes (metadata only)."""
@@ -209,6 +256,13 @@ class RIJEngine:
             sizes.append(lib.gsdft_vne_workspace_size(nl))
         self.ws_bytes = max(sizes)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
+        # many orbitals: q and g_C as dense tiles over row blocks (by pi and by pj)
+        self.blocks = None
+        if self.n_occ >= BLOCK_MIN_OCC and nl > 0:
+            rp = self.plan.rep_pos[:nl].to(torch.int64)
+            ri, rj = self.pi[rp], self.pj[rp]
+            self.blocks = (row_blocks(ri, rj, self.M), row_blocks(rj, ri, self.M))
+            self.block_buf = [e(max(bl.buf_len, 1)) for bl in self.blocks]
         # the packed inverse factor [L^-1 lower | L^-T strict upper] once per refresh: the per-step
         # solve is then two row-parallel mat-vecs over one n_aux^2 matrix
         self.Linv = None
@@ -260,9 +314,17 @@ class RIJEngine:
         s = stream_handle(self.device)
         lib.call("gsdft_splat_quantities", ptr(quat), ptr(log_scale), self.M, ptr(self.A9),
                  ptr(self.N), s)
+        blocks = self.blocks is not None
         lib.call("gsdft_pair_prep", ptr(self.A9), ptr(centers), ptr(self.N), self.M, ptr(self.pi),
                  ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_w), self.plan.n_rep,
-                 ptr(C_occ), ptr(occ), self.n_occ, ptr(self.rec), s)
+                 None if blocks else ptr(C_occ), None if blocks else ptr(occ),
+                 0 if blocks else self.n_occ, ptr(self.rec), s)
+        if blocks:
+            bl = self.blocks[0]
+            lib.call("gsdft_block_density", ptr(C_occ), ptr(occ), self.M, self.n_occ, bl.n_blocks,
+                     ptr(bl.boff), ptr(bl.nj), ptr(bl.joff), ptr(bl.jidx), bl.max_nj, ptr(bl.cell),
+                     ptr(self.plan.rep_w), self.plan.n_rep, ptr(self.block_buf[0]), ptr(self.rec),
+                     s)
 
     def external(self, sums=False, add=False, g_E=None):
         """This device's E_ne = sum_a q_a V_a and V per list entry (after ``prepare``); with
@@ -324,7 +386,14 @@ class RIJEngine:
         lib.call("gsdft_splat_reduce", ptr(self.side), ptr(self.plan.order_i),
                  ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl, self.M,
                  ptr(self.gA6), ptr(self.gmu), ptr(self.gN), s)
-        if self.n_occ > 0:
+        if self.blocks is not None:
+            # g_C = occ (T_i C_J + T_j C_I): the J w values in each grouping's tiles, two block SpMMs
+            for k, bl in enumerate(self.blocks):
+                lib.call("gsdft_block_density_grad", ptr(self.jw), ptr(bl.cell), nl, ptr(C_occ),
+                         ptr(occ), self.M, self.n_occ, bl.n_blocks, ptr(bl.boff), ptr(bl.nj),
+                         ptr(bl.joff), ptr(bl.jidx), bl.buf_len, ptr(self.block_buf[k]),
+                         float(k), ptr(self.g_C), s)
+        elif self.n_occ > 0:
             lib.call("gsdft_density_grad", ptr(self.plan.order_i), ptr(self.plan.seg_i),
                      ptr(self.plan.partner_i), ptr(self.plan.order_j), ptr(self.plan.seg_j),
                      ptr(self.plan.partner_j), ptr(self.jw), nl, self.M, ptr(C_occ), ptr(occ),

@@ -313,6 +313,29 @@ int gsdft_density_grad(const int32_t* order_i, const int64_t* seg_i, const int32
                        const double* jw, int64_t n_rep, int64_t M, const double* C_occ,
                        const double* occ, int64_t n_occ, double* g_C, gsdft_stream_t stream);
 
+/* The same q and g_C for many orbitals, as dense tiles on the FP64 tensor cores. The splats are cut
+ * into n_blocks = ceil(M / 64) row blocks; block b has the sorted partner list
+ * jidx[joff[b] .. joff[b] + nj[b]) (the splats paired with its rows) and a dense tile of
+ * rows_b x nj[b] doubles at buf + boff[b] (rows_b = min(64, M - 64 b)); representative a's cell is
+ * cell[a] (its row splat's row, its partner's column).
+ * gsdft_block_density: tile_b = (C_I diag(occ)) C_J^T (an SDDMM over the block, max_nj = max nj[b]),
+ * then q_a = rep_w[a] tile[cell[a]] into rec (Q and QK) for the n_rep representatives.
+ * gsdft_block_density_grad: zeroes buf (buf_len doubles), scatters vals[a] (J w) to cell[a], and sets
+ * g_C = beta g_C + tile (C_J diag(occ)) row block by row block (an SpMM). Called for the by-pi
+ * grouping (beta = 0) then the by-pj grouping (beta = 1), it gives gsdft_density_grad's g_C.
+ * Deterministic. Replaces the same expressions as gsdft_pair_prep's q (gs_dft/coulomb/ri.py:456) and
+ * gsdft_density_grad (its gradient); the grouping is refresh-time state of the host layer. */
+int gsdft_block_density(const double* C_occ, const double* occ, int64_t M, int64_t n_occ,
+                        int64_t n_blocks, const int64_t* boff, const int32_t* nj, const int64_t* joff,
+                        const int32_t* jidx, int64_t max_nj, const int64_t* cell,
+                        const double* rep_w, int64_t n_rep, double* buf, double* rec,
+                        gsdft_stream_t stream);
+int gsdft_block_density_grad(const double* vals, const int64_t* cell, int64_t n_rep,
+                             const double* C_occ, const double* occ, int64_t M, int64_t n_occ,
+                             int64_t n_blocks, const int64_t* boff, const int32_t* nj,
+                             const int64_t* joff, const int32_t* jidx, int64_t buf_len,
+                             double* buf, double beta, double* g_C, gsdft_stream_t stream);
+
 /* Screened nuclear attraction on the pair representatives: V_a = -2 pi KN_a sum_A Z_A sum_t w_t
  * det(A_hat + t^2 I)^-1/2 exp(-t^2 d.A_hat (A_hat + t^2 I)^-1 d), d = R_A - P_a, and
  * E_ne = sum_a q_a V_a (q from rec, so pair weights and twin merging apply). Replaces

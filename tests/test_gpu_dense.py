@@ -98,3 +98,51 @@ def test_cholesky_rejects_an_indefinite_matrix(g):
     V[150, 150] = -1.0
     with pytest.raises(ValueError, match="not positive definite"):
         cholesky_inplace(dev(V), 1e-8)
+
+
+@pytest.mark.parametrize("M,n_occ,n_pairs", [(200, 65, 3000), (130, 128, 700), (64, 300, 1)])
+def test_block_density_and_gradient(g, M, n_occ, n_pairs):
+    """q and g_C as row-block DMMA tiles (SDDMM, SpMM) against NumPy on a random pair pattern:
+    ragged last row block and orbital tile, row blocks without partners (splats 64..127 pair with
+    nothing when M = 200), a single pair, representatives with i = j. q_a = w_a sum_o occ_o C_io
+    C_jo; g_C[s] = occ (sum_{a: i_a = s} v_a C_{j_a} + sum_{a: j_a = s} v_a C_{i_a})."""
+    from gs_dft_b200._lib import lib, ptr, stream_handle
+    from gs_dft_b200.coulomb.engine import row_blocks
+    rng = np.random.default_rng(M + n_occ)
+    live = np.r_[np.arange(0, min(M, 64)), np.arange(128, M)]
+    pairs = {(int(rng.choice(live)), int(rng.choice(live))) for _ in range(n_pairs)}
+    pairs |= {(int(live[-1]), int(live[-1]))}
+    pi = np.array(sorted(p[0] for p in pairs))
+    pj = np.array([p[1] for p in sorted(pairs)])
+    n = pi.size
+    C = rng.standard_normal((M, n_occ))
+    occ = rng.uniform(0.5, 2.0, n_occ)
+    w = rng.choice([1.0, 2.0], n)
+    v = rng.standard_normal(n)
+    dpi = torch.as_tensor(pi, dtype=torch.int32, device="cuda")
+    dpj = torch.as_tensor(pj, dtype=torch.int32, device="cuda")
+    by_i, by_j = row_blocks(dpi, dpj, M), row_blocks(dpj, dpi, M)
+    dC, docc, dw, dv = dev(C), dev(occ), dev(w), dev(v)
+    st = stream_handle(dC.device)
+    rec = torch.zeros((n, 18), dtype=torch.float64, device="cuda")
+    rec[:, 17] = 3.0   # GSDFT_REC_KN
+    buf = torch.empty(max(by_i.buf_len, by_j.buf_len), dtype=torch.float64, device="cuda")
+    lib.call("gsdft_block_density", ptr(dC), ptr(docc), M, n_occ, by_i.n_blocks, ptr(by_i.boff),
+             ptr(by_i.nj), ptr(by_i.joff), ptr(by_i.jidx), by_i.max_nj, ptr(by_i.cell), ptr(dw), n,
+             ptr(buf), ptr(rec), st)
+    q_ref = w * np.einsum("ao,o,ao->a", C[pi], occ, C[pj])
+    scale = np.abs(C).max() ** 2 * occ.max() * n_occ * 1e-15 * 2
+    np.testing.assert_allclose(host(rec[:, 16]), q_ref, rtol=0, atol=scale)
+    np.testing.assert_allclose(host(rec[:, 15]), 3.0 * q_ref, rtol=0, atol=3 * scale)
+    gC = dev(rng.standard_normal((M, n_occ)))   # overwritten (beta = 0 first)
+    for k, bl in enumerate((by_i, by_j)):
+        lib.call("gsdft_block_density_grad", ptr(dv), ptr(bl.cell), n, ptr(dC), ptr(docc), M,
+                 n_occ, bl.n_blocks, ptr(bl.boff), ptr(bl.nj), ptr(bl.joff), ptr(bl.jidx),
+                 bl.buf_len, ptr(buf), float(k), ptr(gC), st)
+    want = np.zeros((M, n_occ))
+    np.add.at(want, pi, v[:, None] * C[pj])
+    np.add.at(want, pj, v[:, None] * C[pi])
+    want *= occ
+    tol = 1e-14 * (np.abs(v).sum() * np.abs(C).max() * occ.max() + 1)
+    np.testing.assert_allclose(host(gC), want, rtol=0, atol=tol)
+    assert not host(gC)[64:128].any()

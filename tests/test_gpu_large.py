@@ -2,8 +2,8 @@
 
 Configuration 2 is (H2O)64 (M = 3,000 splats, n_occ = 320, 1.16e6 significant pairs) and
 configuration 3 is (H2O)343 (M = 20,000, n_occ = 1,715, 1.29e7 significant pairs): the sizes the
-metric is quoted on. They run the code paths the small golden systems never reach: the warp-per-pair
-density kernel and the many-orbital density gradient (n_occ > 32), int64 flat pair keys over 4e8
+metric is quoted on. They run the code paths the small golden systems never reach: q and g_C as
+DMMA tiles over 64-splat row blocks (n_occ >= 64), int64 flat pair keys over 4e8
 candidates, the packed inverse factor above N_aux = 16,384, and node screening, which only pays on
 spatially extended systems.
 
@@ -117,6 +117,7 @@ def _engine_step(g, sy, s, pi, pj, aux, L, C_occ, screening=True):
         lib.call("gsdft_node_evals", ctypes.byref(f), ctypes.byref(r), 1)
         out["evals"] = (int(f.value), int(r.value))
         out["units"] = eng.plan.n_rep * eng.n_aux
+        out["block"] = eng.blocks is not None
         del eng
     finally:
         lib.call("gsdft_set_node_screening", 1)
@@ -126,8 +127,8 @@ def _engine_step(g, sy, s, pi, pj, aux, L, C_occ, screening=True):
 @pytest.mark.parametrize("cfg,k", [(2, 6000), (3, 3000)])
 def test_step_subset_vs_oracle_large(g, cfg, k):
     """E_J, gamma, J and the gradients (quat, log_scale, centres, C_occ) on a random subset of the
-    configuration's significant pairs, all aux, against the C oracle; n_occ = 320 / 1715 runs the
-    warp-per-pair q build and the chunked many-orbital density gradient. Node screening on (the
+    configuration's significant pairs, all aux, against the C oracle; n_occ = 320 / 1715 runs q
+    and g_C as row-block DMMA tiles (SDDMM and SpMM). Node screening on (the
     product default) and off agree with each other to 1e-12 and with the oracle to 1e-10."""
     sy, s, pi, pj, v, aux, L = system(g, cfg)
     sel = _subset(int(pi.shape[0]), k, seed=cfg)
@@ -151,10 +152,11 @@ def test_step_subset_vs_oracle_large(g, cfg, k):
     assert 4 * units <= f < 20 * units and 4 * units <= r < 20 * units
 
 
-@pytest.mark.parametrize("n_occ", [24, 40])
+@pytest.mark.parametrize("n_occ", [24, 40, 100])
 def test_orbital_count_branches(g, n_occ):
-    """Ethanol's geometry with 24 (thread-per-pair q, 32-wide register density gradient) and 40
-    (warp-per-pair q, chunked density gradient) occupied orbitals, on a 3000-pair subset."""
+    """Ethanol's geometry with 24 (thread-per-pair q, 32-wide register density gradient), 40
+    (warp-per-pair q, chunked density gradient) and 100 (row-block DMMA tiles, with a ragged last
+    orbital tile and a ragged last row block) occupied orbitals, on a 3000-pair subset."""
     from gs_dft_b200.systems import make_config
     sy = make_config(1)
     C = np.linalg.qr(np.random.default_rng(n_occ).standard_normal((sy.M, n_occ)))[0]
@@ -166,6 +168,8 @@ def test_orbital_count_branches(g, n_occ):
     sel = _subset(int(pi.shape[0]), 3000, seed=n_occ)
     spi, spj = host(pi)[sel], host(pj)[sel]
     out = _engine_step(g, sy, s, dev(spi, torch.int32), dev(spj, torch.int32), aux, L, sy.C_occ)
+    from gs_dft_b200.coulomb.engine import BLOCK_MIN_OCC
+    assert out["block"] == (n_occ >= BLOCK_MIN_OCC) and (sy.M % 64 != 0 or n_occ < 64)
     aq = tuple(host(t) for t in aux.quantities())
     ref = O.energy_and_grad_c((sy.quat, sy.log_scale, sy.centers, sy.C_occ, sy.occ), aq, host(L),
                               spi, spj, np.ones(spi.size, bool))
