@@ -475,6 +475,7 @@ extern "C" int gsdft_pair_prep(const double* A9, const double* mu, const double*
   cudaStream_t st = (cudaStream_t)stream;
   pair_prep_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(A9, mu, N, pi, pj, rep_pos, n_rep, rec);
   GSDFT_LAUNCHED("pair_prep");
+  if (n_occ == 0 && !C_occ) return GSDFT_OK;  // q and qk come from gsdft_block_density
   if (n_occ <= 32) {
     pair_density_thread_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(pi, pj, rep_w, rep_pos, n_rep,
                                                                    C_occ, occ, n_occ, rec);

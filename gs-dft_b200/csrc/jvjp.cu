@@ -228,44 +228,60 @@ __global__ void pair_chain_kernel(const double* __restrict__ A9, const double* _
                                   const int32_t* __restrict__ twin,
                                   const double* __restrict__ rep_w, int64_t n_live,
                                   const double* __restrict__ rec, const double* __restrict__ sums,
-                                  double* __restrict__ side, double* __restrict__ J,
-                                  double* __restrict__ jw) {
+                                  const double* __restrict__ xc, double* __restrict__ side,
+                                  double* __restrict__ J, double* __restrict__ jw) {
   int64_t a = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (a >= n_live) return;
   const double* r = rec + a * GSDFT_REC_FIELDS;
-  const double* sm = sums + a * GSDFT_VJP_FIELDS;
   const int64_t e = live_idx[a];
   const int i = pi[e], j = pj[e];
   const double q = r[GSDFT_REC_Q], kn = r[GSDFT_REC_KN], qk = r[GSDFT_REC_QK];
-  const double SJ = sm[GSDFT_VJP_SJ];
-  J[e] = kn * SJ;
-  if (twin[a] >= 0) J[twin[a]] = kn * SJ;  // the merged transpose carries the same integral
-  jw[a] = (kn * SJ) * rep_w[a];            // J w, the weight of q_a's gradient
-  const double KNbar = q * kPref * SJ;
-  // eigenframe cotangent of A_hat: M_kl = -qk SZ_kl - 1/2 qk SD_k delta_kl
-  double Mm[3][3];
-  Mm[0][0] = -qk * sm[GSDFT_VJP_SZ00] - 0.5 * qk * sm[GSDFT_VJP_SD0];
-  Mm[1][1] = -qk * sm[GSDFT_VJP_SZ11] - 0.5 * qk * sm[GSDFT_VJP_SD1];
-  Mm[2][2] = -qk * sm[GSDFT_VJP_SZ22] - 0.5 * qk * sm[GSDFT_VJP_SD2];
-  Mm[0][1] = Mm[1][0] = -qk * sm[GSDFT_VJP_SZ01];
-  Mm[0][2] = Mm[2][0] = -qk * sm[GSDFT_VJP_SZ02];
-  Mm[1][2] = Mm[2][1] = -qk * sm[GSDFT_VJP_SZ12];
-  double U[3][3], L[3], Pe[3];
-  for (int rr = 0; rr < 3; ++rr)
-    for (int c = 0; c < 3; ++c) U[rr][c] = r[GSDFT_REC_U00 + 3 * rr + c];
-  for (int k = 0; k < 3; ++k) {
-    L[k] = r[GSDFT_REC_L0 + k];
-    Pe[k] = 2.0 * qk * L[k] * sm[GSDFT_VJP_SV0 + k];
+  double Ab[3][3] = {{0.0, 0.0, 0.0}, {0.0, 0.0, 0.0}, {0.0, 0.0, 0.0}};
+  double Pb[3] = {0.0, 0.0, 0.0};
+  double Jq = 0.0, KNbar = 0.0;
+  if (sums) {
+    const double* sm = sums + a * GSDFT_VJP_FIELDS;
+    const double SJ = sm[GSDFT_VJP_SJ];
+    Jq = kn * SJ;
+    KNbar = q * kPref * SJ;
+    // eigenframe cotangent of A_hat: M_kl = -qk SZ_kl - 1/2 qk SD_k delta_kl
+    double Mm[3][3];
+    Mm[0][0] = -qk * sm[GSDFT_VJP_SZ00] - 0.5 * qk * sm[GSDFT_VJP_SD0];
+    Mm[1][1] = -qk * sm[GSDFT_VJP_SZ11] - 0.5 * qk * sm[GSDFT_VJP_SD1];
+    Mm[2][2] = -qk * sm[GSDFT_VJP_SZ22] - 0.5 * qk * sm[GSDFT_VJP_SD2];
+    Mm[0][1] = Mm[1][0] = -qk * sm[GSDFT_VJP_SZ01];
+    Mm[0][2] = Mm[2][0] = -qk * sm[GSDFT_VJP_SZ02];
+    Mm[1][2] = Mm[2][1] = -qk * sm[GSDFT_VJP_SZ12];
+    double U[3][3], Pe[3];
+    for (int rr = 0; rr < 3; ++rr)
+      for (int c = 0; c < 3; ++c) U[rr][c] = r[GSDFT_REC_U00 + 3 * rr + c];
+    for (int k = 0; k < 3; ++k) Pe[k] = 2.0 * qk * r[GSDFT_REC_L0 + k] * sm[GSDFT_VJP_SV0 + k];
+    // Abar = U M U^T (symmetric), Pbar = U Pe
+    double UM[3][3];
+    for (int rr = 0; rr < 3; ++rr)
+      for (int c = 0; c < 3; ++c) UM[rr][c] = U[rr][0] * Mm[0][c] + U[rr][1] * Mm[1][c] + U[rr][2] * Mm[2][c];
+    for (int rr = 0; rr < 3; ++rr)
+      for (int c = 0; c < 3; ++c) Ab[rr][c] = UM[rr][0] * U[c][0] + UM[rr][1] * U[c][1] + UM[rr][2] * U[c][2];
+    for (int rr = 0; rr < 3; ++rr) Pb[rr] = U[rr][0] * Pe[0] + U[rr][1] * Pe[1] + U[rr][2] * Pe[2];
   }
-  // Abar = U M U^T (symmetric), Pbar = U Pe
-  double UM[3][3];
-  for (int rr = 0; rr < 3; ++rr)
-    for (int c = 0; c < 3; ++c) UM[rr][c] = U[rr][0] * Mm[0][c] + U[rr][1] * Mm[1][c] + U[rr][2] * Mm[2][c];
-  double Ab[3][3];
-  for (int rr = 0; rr < 3; ++rr)
-    for (int c = 0; c < 3; ++c) Ab[rr][c] = UM[rr][0] * U[c][0] + UM[rr][1] * U[c][1] + UM[rr][2] * U[c][2];
-  double Pb[3];
-  for (int rr = 0; rr < 3; ++rr) Pb[rr] = U[rr][0] * Pe[0] + U[rr][1] * Pe[1] + U[rr][2] * Pe[2];
+  if (xc) {  // cotangents given directly
+    const double* x = xc + a * GSDFT_XC_FIELDS;
+    Ab[0][0] += x[GSDFT_XC_A00];
+    Ab[1][1] += x[GSDFT_XC_A11];
+    Ab[2][2] += x[GSDFT_XC_A22];
+    Ab[0][1] += x[GSDFT_XC_A01];
+    Ab[1][0] += x[GSDFT_XC_A01];
+    Ab[0][2] += x[GSDFT_XC_A02];
+    Ab[2][0] += x[GSDFT_XC_A02];
+    Ab[1][2] += x[GSDFT_XC_A12];
+    Ab[2][1] += x[GSDFT_XC_A12];
+    for (int k = 0; k < 3; ++k) Pb[k] += x[GSDFT_XC_P0 + k];
+    KNbar += x[GSDFT_XC_KN];
+    Jq += x[GSDFT_XC_J];
+  }
+  J[e] = Jq;
+  if (twin[a] >= 0) J[twin[a]] = Jq;  // the merged transpose carries the same integral
+  jw[a] = Jq * rep_w[a];              // J w, the weight of q_a's gradient
 
   double Ai[9], Aj[9], mui[3], muj[3];
   for (int k = 0; k < 9; ++k) {
@@ -571,8 +587,9 @@ extern "C" int gsdft_j_vjp_weighted(const double* rec, int64_t n_live, const dou
 extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
                                 const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
                                 const int32_t* rep_twin, const double* rep_w, int64_t n_rep,
-                                int64_t n, const double* rec, const double* sums, double* side,
-                                double* J, double* jw, gsdft_stream_t stream) {
+                                int64_t n, const double* rec, const double* sums,
+                                const double* xc, double* side, double* J, double* jw,
+                                gsdft_stream_t stream) {
   GSDFT_REQUIRE(M > 0 && n_rep >= 0 && n >= n_rep, "bad sizes");
   cudaStream_t st = (cudaStream_t)stream;
   if (n > 0) {
@@ -580,11 +597,10 @@ extern "C" int gsdft_pair_chain(const double* A9, const double* mu, const double
     GSDFT_CUDA(cudaMemsetAsync(J, 0, n * sizeof(double), st));
   }
   if (n_rep == 0) return GSDFT_OK;
-  GSDFT_REQUIRE(A9 && mu && N && pi && pj && rep_pos && rep_twin && rep_w && rec && sums &&
-                    side && jw,
+  GSDFT_REQUIRE(A9 && mu && N && pi && pj && rep_pos && rep_twin && rep_w && rec && side && jw,
                 "null pointer");
   pair_chain_kernel<<<grid_1d(n_rep, 128), 128, 0, st>>>(A9, mu, N, pi, pj, rep_pos, rep_twin,
-                                                         rep_w, n_rep, rec, sums, side, J, jw);
+                                                         rep_w, n_rep, rec, sums, xc, side, J, jw);
   GSDFT_LAUNCHED("pair_chain");
   return GSDFT_OK;
 }

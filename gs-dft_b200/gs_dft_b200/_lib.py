@@ -16,8 +16,9 @@ ERR_ARG, ERR_CUDA, ERR_OVERFLOW, ERR_LINALG = 1, 2, 3, 4
 REC_FIELDS = 18
 VJP_FIELDS = 13
 SIDE_FIELDS = 20
+XC_FIELDS = 11
 SOLVE_INV_MAX = 65536   # GSDFT_SOLVE_INV_MAX
-ABI_VERSION = 2         # GSDFT_ABI_VERSION
+ABI_VERSION = 3         # GSDFT_ABI_VERSION
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -78,7 +79,7 @@ SIGNATURES = {
     "gsdft_j_vjp": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _sz,
                            _c_p]),
     "gsdft_pair_chain": (_i32, [_c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64,
-                                _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
+                                _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
     "gsdft_splat_reduce": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p,
                                   _c_p]),
     "gsdft_vne_workspace_size": (_sz, [_i64]),
@@ -97,6 +98,8 @@ SIGNATURES = {
     "gsdft_k_unit_q": (_i32, [_c_p, _i64, _c_p, _c_p]),
     "gsdft_exact_j_workspace_size": (_sz, [_i64]),
     "gsdft_exact_j": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_exact_j_vjp_workspace_size": (_sz, [_i64]),
+    "gsdft_exact_j_vjp": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
                                   _i64, _c_p, _c_p]),
 }

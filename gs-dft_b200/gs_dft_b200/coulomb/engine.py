@@ -24,7 +24,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import _check
-from .._lib import (REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, lib, ptr,
+from .._lib import (REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, XC_FIELDS, lib, ptr,
                     stream_handle)
 
 F64 = torch.float64
@@ -203,10 +203,13 @@ class RIJEngine:
         balance: optional (quat, log_scale, centers) of the splats at refresh: with world > 1 the
             ranks' slices then carry equal estimated integral cost (``gsdft_rep_cost``: node
             screening makes distant pairs cheaper), instead of equal representative counts.
+        exact: the Hartree term is the exact (pair|pair) E_J over the representatives
+            (``gsdft_exact_j`` / ``gsdft_exact_j_vjp``, O(n_rep^2)) instead of the density fit;
+            no aux, one device.
     """
 
     def __init__(self, pi, pj, w, M, n_occ, beta=None, R=None, KN=None, L=None, rank=0, world=1,
-                 merge_twins=True, inverse_solve=True, atoms=None, balance=None):
+                 merge_twins=True, inverse_solve=True, atoms=None, balance=None, exact=False):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi = pi.to(torch.int32).contiguous()
@@ -220,9 +223,14 @@ class RIJEngine:
                 _check.f64(L, "L", (n_aux, n_aux))
         self.beta, self.R, self.KN, self.L = beta, R, KN, L
         self.rij = beta is not None
+        self.exact = bool(exact)
         self.n_aux = int(beta.shape[0]) if self.rij else 0
-        if not self.rij and atoms is None:
-            raise ValueError("RIJEngine needs the aux quantities (beta, R, KN), atoms, or both")
+        if self.exact and (self.rij or world != 1):
+            raise ValueError("the exact Hartree term replaces the density fit (no aux) and runs "
+                             "on one device")
+        if not self.rij and not self.exact and atoms is None:
+            raise ValueError("RIJEngine needs the aux quantities (beta, R, KN), exact=True, "
+                             "atoms, or a Hartree term and atoms")
         cost_fn = None
         if balance is not None and world > 1 and self.rij:
             cost_fn = self._cost_fn(*balance)
@@ -254,6 +262,10 @@ class RIJEngine:
                       lib.gsdft_j_solve_inv_workspace_size(self.n_aux)]
         if self.atoms is not None:
             sizes.append(lib.gsdft_vne_workspace_size(nl))
+        self.xc = self.Jx = None
+        if self.exact:
+            self.xc, self.Jx = e(max(nl, 1), XC_FIELDS), e(max(nl, 1))
+            sizes += [lib.gsdft_exact_j_workspace_size(nl), lib.gsdft_exact_j_vjp_workspace_size(nl)]
         self.ws_bytes = max(sizes)
         self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=dev)
         # many orbitals: q and g_C as dense tiles over row blocks (by pi and by pj)
@@ -344,6 +356,10 @@ class RIJEngine:
         nl = self.plan.n_rep
         self.prepare(quat, log_scale, centers, C_occ, occ)
         self.last_forward = object()
+        if self.exact:
+            lib.call("gsdft_exact_j", ptr(self.rec), nl, ptr(self.Jx), ptr(self.E), ptr(self.ws),
+                     self.ws_bytes, s)
+            return self.E
         if not self.rij:
             return None
         end = self._bracket("forward")
@@ -377,11 +393,16 @@ class RIJEngine:
                      self.ws_bytes, s)
             if end is not None:
                 end.record(torch.cuda.current_stream(self.device))
+        if self.exact:
+            lib.call("gsdft_exact_j_vjp", ptr(self.rec), nl, ptr(g_E), ptr(self.xc), ptr(self.ws),
+                     self.ws_bytes, s)
         if self.atoms is not None:
             self.external(sums=True, add=self.rij, g_E=g_E_ne)
+        has_sums = self.rij or self.atoms is not None
         lib.call("gsdft_pair_chain", ptr(self.A9), ptr(centers), ptr(self.N), self.M,
                  ptr(self.pi), ptr(self.pj), ptr(self.plan.rep_pos), ptr(self.plan.rep_twin),
-                 ptr(self.plan.rep_w), nl, self.plan.n, ptr(self.rec), ptr(self.sums),
+                 ptr(self.plan.rep_w), nl, self.plan.n, ptr(self.rec),
+                 ptr(self.sums) if has_sums else None, ptr(self.xc) if self.exact else None,
                  ptr(self.side), ptr(self.J), ptr(self.jw), s)
         lib.call("gsdft_splat_reduce", ptr(self.side), ptr(self.plan.order_i),
                  ptr(self.plan.seg_i), ptr(self.plan.order_j), ptr(self.plan.seg_j), nl, self.M,
@@ -415,6 +436,8 @@ class RIJEngine:
         if self.rij:
             self.solve()
             out.update(E=self.E, gamma=self.gamma, d=self.d)
+        elif self.exact:
+            out.update(E=self.E)
         if grad:
             self.backward_local(centers, C_occ, occ, g_E, g_E_ne)
             self.chart(quat, log_scale)

@@ -109,8 +109,8 @@ class RIKEngine:
         lib.call("gsdft_k_unit_q", ptr(self.rec), nl, ptr(self.rec_K), s)
         lib.call("gsdft_pair_chain", ptr(self.A9), ptr(centers), ptr(self.N), self.M,
                  ptr(self.pi), ptr(self.pj), ptr(p.rep_pos), ptr(p.rep_twin), ptr(p.rep_w), nl,
-                 p.n, ptr(self.rec_K), ptr(self.sums), ptr(self.side), ptr(self.J), ptr(self.jw),
-                 s)
+                 p.n, ptr(self.rec_K), ptr(self.sums), None, ptr(self.side), ptr(self.J),
+                 ptr(self.jw), s)
         lib.call("gsdft_splat_reduce", ptr(self.side), ptr(p.order_i), ptr(p.seg_i),
                  ptr(p.order_j), ptr(p.seg_j), nl, self.M, ptr(self.gA6), ptr(self.gmu),
                  ptr(self.gN), s)

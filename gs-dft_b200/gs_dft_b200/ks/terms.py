@@ -84,8 +84,8 @@ class ScreenedProductDFCoulomb:
 class ScreenedExactCoulomb:
     """Exact streamed ERI over the significant pairs (DF-free), PBE-class only: the reference's
     ``ScreenedExactCoulomb`` (gs_dft/ks/terms.py:195-205). ``energy(basis, C_orth, P, occ, state)
-    -> (E_J, 0)``; the value only (its gradient is not on the B200 path), and hybrids are rejected
-    as in the reference (there is no screened exact K)."""
+    -> (E_J, 0)``, differentiable in the splats and ``C_orth``; hybrids are rejected as in the
+    reference (there is no screened exact K)."""
 
     def __init__(self, chunk: int = 128, hf_coeff: float = 0.0):
         if hf_coeff != 0.0:
@@ -95,12 +95,6 @@ class ScreenedExactCoulomb:
 
     def energy(self, basis, C_orth, P, occ, state):
         from ..coulomb.stream import screened_coulomb_energy
-        if torch.is_grad_enabled() and any(
-                t.requires_grad for t in (basis.quat, basis.log_scale, basis.centers, C_orth)):
-            raise NotImplementedError(
-                "ScreenedExactCoulomb on the B200 path gives the value of E_J only; its gradient "
-                "is not built. Evaluate it under torch.no_grad() (or on detached inputs), or train "
-                "with the density-fitted Coulomb (df()).")
         pi, pj, valid = state.pairs
         e_j = screened_coulomb_energy(basis, C_orth, occ, pi, pj, valid=valid,
                                       bra_chunk=self.chunk)

@@ -74,9 +74,20 @@ enum {
 
 #define GSDFT_SIDE_FIELDS 20 /* per live pair: i-side (gA6, gmu3, gN) then j-side */
 
+/* Per-representative cotangents handed to gsdft_pair_chain directly (xc[a * GSDFT_XC_FIELDS + f]):
+ * of A_hat (the symmetric matrix's entries), of P, of KN (the product N_i N_j exp(...)), and dE/dq
+ * per unit weight. Written by gsdft_exact_j_vjp. */
+enum {
+  GSDFT_XC_A00 = 0, GSDFT_XC_A11, GSDFT_XC_A22, GSDFT_XC_A01, GSDFT_XC_A02, GSDFT_XC_A12,
+  GSDFT_XC_P0, GSDFT_XC_P1, GSDFT_XC_P2,
+  GSDFT_XC_KN,
+  GSDFT_XC_J,
+  GSDFT_XC_FIELDS
+};
+
 /* Version of this ABI (entry points, argument meaning, record layouts); gsdft_version() returns it.
  * A host binding checks it at load time so that a library built from older sources is refused. */
-#define GSDFT_ABI_VERSION 2
+#define GSDFT_ABI_VERSION 3
 
 const char* gsdft_last_error_string(void);
 int gsdft_version(void);
@@ -224,7 +235,8 @@ int gsdft_aux_cholesky(double* V, int64_t n_aux, double lam, void* ws, size_t ws
 
 /* Per pair representative: A_hat, P, KN (gs_dft/coulomb/stream.py:203-215), the eigen-decomposition of A_hat
  * (gs_dft/coulomb/ri.py:145), and q = w sum_o occ_o C_io C_jo (gs_dft/coulomb/ri.py:456), for
- * each representative (w its summed weight).
+ * each representative (w its summed weight). With n_occ = 0 and C_occ = NULL, Q and QK are left
+ * unwritten, for gsdft_block_density to fill (n_occ = 0 with C_occ set writes q = 0).
  * rec is (n_rep, GSDFT_REC_FIELDS). */
 int gsdft_pair_prep(const double* A9, const double* mu, const double* N, int64_t M,
                     const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
@@ -292,12 +304,14 @@ int gsdft_j_vjp(const double* rec, int64_t n_rep, const double* beta, const doub
  * N_j) contributions side (n_rep, GSDFT_SIDE_FIELDS); J (n, list order: written at each
  * representative's position and at its merged transpose's; 0 on zero-weight entries); jw (n_rep)
  * = J times the representative's summed weight, the factor of q's gradient. The reverse of
- * gs_dft/coulomb/stream.py:203-215. */
+ * gs_dft/coulomb/stream.py:203-215. sums (gsdft_j_vjp's layout) and xc (GSDFT_XC_FIELDS per
+ * representative, cotangents given directly, e.g. by gsdft_exact_j_vjp) are each optional (NULL)
+ * and add. */
 int gsdft_pair_chain(const double* A9, const double* mu, const double* N, int64_t M,
                      const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
                      const int32_t* rep_twin, const double* rep_w, int64_t n_rep, int64_t n,
-                     const double* rec, const double* sums, double* side, double* J, double* jw,
-                     gsdft_stream_t stream);
+                     const double* rec, const double* sums, const double* xc, double* side,
+                     double* J, double* jw, gsdft_stream_t stream);
 
 /* Deterministic per-splat sums of the side contributions (plan groupings) -> gA6 (M,6), gmu (M,3),
  * gN (M). Replaces the segment scatter of JAX autodiff through A[pi], A[pj]. */
@@ -406,6 +420,15 @@ int gsdft_k_unit_q(const double* rec, int64_t n_rep, double* rec_out, gsdft_stre
 size_t gsdft_exact_j_workspace_size(int64_t n_rep);
 int gsdft_exact_j(const double* rec, int64_t n_rep, double* J, double* E, void* ws, size_t ws_bytes,
                   gsdft_stream_t stream);
+
+/* Reverse pass of g_E * E_J (g_E a device scalar, NULL = 1) of gsdft_exact_j: per representative the
+ * cotangents of A_hat, P and KN and dE/dq into xc (n_rep, GSDFT_XC_FIELDS), for gsdft_pair_chain
+ * (sums NULL, or V_ne's). Each (a, b) evaluates dF/dH and dF/dd of the node sum in closed form over
+ * the same 20 nodes (the derivative the reference takes by autodiff of the streamed Schur block,
+ * gs_dft/coulomb/stream.py:144-189, 294-320). O(n_rep^2). Deterministic. */
+size_t gsdft_exact_j_vjp_workspace_size(int64_t n_rep);
+int gsdft_exact_j_vjp(const double* rec, int64_t n_rep, const double* g_E, double* xc, void* ws,
+                      size_t ws_bytes, gsdft_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -622,6 +622,75 @@ def screened_coulomb_energy_exact(sys_arrays, pi, pj, valid, bra_chunk=128):
         jv[sl] = eri_block_schur(q, pi[sl], pj[sl], ki, kj) @ Pk
     return 0.5 * float(np.sum(jv * Pw)), jv
 
+def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64):
+    """Exact E_J (as ``screened_coulomb_energy_exact``), J per listed pair (0 on zero-weight
+    entries) and the gradient of E_J with respect to (quat, log_scale, centers, C_occ), pair list
+    frozen: the derivative the reference takes by autodiff of its streamed block
+    (gs_dft/coulomb/stream.py:144-189, 294-320), written out. The 6x6 determinant of the Schur
+    block is det A_a det A_b det(I + t^2 H) and its exponent t^2 d.(I + t^2 H)^-1 d, with
+    H = A_a^-1 + A_b^-1 and d = P_a - P_b, so (a|b) = (2/sqrt(pi)) pi^3 g_a g_b F(H, d),
+    g = KN det(A)^-1/2 and F = sum_t w_t det(I + t^2 H)^-1/2 exp(-t^2 d.K_t d), K_t = (I + t^2 H)^-1:
+      dF/dH = sum_t f_t (-1/2 t^2 K_t + t^4 u_t u_t^T),  dF/dd = -2 sum_t f_t t^2 u_t,  u_t = K_t d.
+    Each node's K_t is a direct 3x3 inverse here (no power expansion)."""
+    quat, log_scale, centers, C_occ, occ = sys_arrays
+    qs = full_quantities(quat, log_scale, centers)
+    n = pi.shape[0]
+    w = np.ones(n) if valid is None else np.asarray(valid, np.float64)
+    live = w != 0
+    idx = np.nonzero(live)[0]
+    ci, cj, cw = pi[live], pj[live], w[live]
+    q = pair_density(C_occ, occ, ci, cj, cw)
+    Ah, Pa, KNa = full_pair_quantities(qs, ci, cj)
+    Ainv = np.linalg.inv(Ah)
+    g = KNa / np.sqrt(det3(Ah))
+    pref = (2.0 / math.sqrt(PI)) * PI ** 3
+    nl = ci.shape[0]
+    Jl = np.zeros(nl)
+    GH = np.zeros((nl, 3, 3))
+    GD = np.zeros((nl, 3))
+    T = np.zeros(nl)
+    eye = np.eye(3)
+    wk = q * g                                                   # q_b g_b
+    for a0 in range(0, nl, bra_chunk):
+        sl = slice(a0, a0 + bra_chunk)
+        H = Ainv[sl, None] + Ainv[None, :]                        # (B, K, 3, 3)
+        d = Pa[sl, None, :] - Pa[None, :, :]
+        F = np.zeros(H.shape[:2])
+        gH = np.zeros(H.shape)
+        gD = np.zeros(d.shape)
+        for t, wq in zip(QUAD_T, QUAD_W):
+            s2 = t * t
+            X = eye + s2 * H
+            K = np.linalg.inv(X)
+            u = np.einsum("bkij,bkj->bki", K, d)
+            f = wq / np.sqrt(np.linalg.det(X)) * np.exp(-s2 * np.sum(d * u, -1))
+            F += f
+            gH += f[..., None, None] * (-0.5 * s2 * K + (s2 * s2) * u[..., :, None] * u[..., None, :])
+            gD += (-2.0 * s2 * f)[..., None] * u
+        T[sl] = F @ wk
+        GH[sl] = np.einsum("bkij,k->bij", gH, wk)
+        GD[sl] = np.einsum("bki,k->bi", gD, wk)
+    Jl = pref * g * T
+    E = 0.5 * float(np.sum(q * Jl))
+    sc = (q * pref * g)
+    Ainv_bar = sc[:, None, None] * GH
+    Pbar = sc[:, None] * GD
+    gbar = q * pref * T
+    Abar = (-np.einsum("bij,bjk,bkl->bil", Ainv, Ainv_bar, Ainv)
+            - (0.5 * gbar * g)[:, None, None] * Ainv)
+    KNbar = gbar / np.sqrt(det3(Ah))
+    M = centers.shape[0]
+    gA = np.zeros((M, 3, 3))
+    gmu = np.zeros((M, 3))
+    gN = np.zeros(M)
+    gC = np.zeros_like(C_occ)
+    _scatter_pair_grads(qs, ci, cj, cw, Jl, Abar, Pbar, KNbar, C_occ, occ, gA, gmu, gN, gC)
+    g_quat, g_log = chart_vjp(quat, log_scale, gA, gN)
+    J = np.zeros(n)
+    J[idx] = Jl
+    return dict(E=E, J=J, g_quat=g_quat, g_log_scale=g_log, g_centers=gmu, g_C=gC, gA=gA,
+                gmu=gmu, gN=gN)
+
 # ----------------------------------------------------------------------------------------------
 #  Screened RI-K  (gs_dft/coulomb/ri.py:497-544)
 # ----------------------------------------------------------------------------------------------

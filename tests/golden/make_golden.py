@@ -30,7 +30,12 @@ Outputs (compressed .npz, a few hundred KB in all):
     list of the 48-splat one, and the first 2000 ordered pairs of CO2 (the full CO2 list takes the
     NumPy stand-in half an hour).
 
-``python tests/golden/make_golden.py vne`` (or ``k``, ``exact``) regenerates only that file.
+  * ``ref_exact_grad.npz`` — the gradient of the screened exact Hartree energy w.r.t. (quat,
+    log_scale, centers, C_occ) by Richardson central differences of the executed reference
+    (``screened_coulomb_energy``) on the 10-splat system, pair list frozen.
+
+``python tests/golden/make_golden.py vne`` (or ``k``, ``exact``, ``exact_grad``) regenerates only
+that file.
 """
 from __future__ import annotations
 
@@ -272,6 +277,41 @@ def make_exact(eps=1e-7):
     np.savez_compressed(os.path.join(HERE, "ref_exact.npz"), **out)
 
 
+def make_exact_grad(eps=1e-7):
+    spec, _, pairs, _ = _modules()
+    cs = jaxshim.load("gs_dft.coulomb.stream")
+    s = small_random_system(10, 3, seed=3, spread=1.0, n_atoms=3)
+    sp0 = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+    pi, pj, _ = pairs.neighbor_pairs(sp0, eps=eps)
+    n = int(pi.shape[0])
+    pi, pj, v = pairs.neighbor_pairs(sp0, eps=eps, pad_to=n + 7)
+
+    def energy(quat, ls, cen, C):
+        sp = spec.Splat(quat=J(quat), log_scale=J(ls), centers=J(cen))
+        return float(cs.screened_coulomb_energy(sp, J(C), J(s.occ), pi, pj, valid=v,
+                                                bra_chunk=32))
+
+    x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy()]
+
+    def fd(k, h):
+        g = np.zeros_like(x0[k])
+        for idx in np.ndindex(x0[k].shape):
+            xp = [a.copy() for a in x0]
+            xm = [a.copy() for a in x0]
+            xp[k][idx] += h
+            xm[k][idx] -= h
+            g[idx] = (energy(*xp) - energy(*xm)) / (2 * h)
+        return g
+
+    out = dict(quat=s.quat, log_scale=s.log_scale, centers=s.centers, C_occ=s.C_occ, occ=s.occ,
+               pi=np.asarray(pi), pj=np.asarray(pj), valid=np.asarray(v), E=energy(*x0), eps=eps)
+    for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
+        h = 1e-3
+        out[name] = (4 * fd(k, h / 2) - fd(k, h)) / 3      # Richardson, O(h^4)
+    np.savez_compressed(os.path.join(HERE, "ref_exact_grad.npz"), **out)
+    print("exact grad: M=10 E_J=", out["E"])
+
+
 if __name__ == "__main__":
     if sys.argv[1:] == ["exact"]:
         make_exact()
@@ -282,6 +322,9 @@ if __name__ == "__main__":
     if sys.argv[1:] == ["k"]:
         make_k()
         sys.exit(0)
+    if sys.argv[1:] == ["exact_grad"]:
+        make_exact_grad()
+        sys.exit(0)
     for name, s in _cases().items():
         make_case(name, s)
     make_grad()
@@ -289,3 +332,4 @@ if __name__ == "__main__":
     make_vne()
     make_k()
     make_exact()
+    make_exact_grad()

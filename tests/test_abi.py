@@ -79,7 +79,8 @@ def test_python_constants_match_header():
     assert int(defs["GSDFT_SIDE_FIELDS"]) == _lib.SIDE_FIELDS
     assert int(defs["GSDFT_SOLVE_INV_MAX"]) == _lib.SOLVE_INV_MAX
     assert int(defs["GSDFT_ABI_VERSION"]) == _lib.ABI_VERSION
-    for enum, width in (("GSDFT_REC_FIELDS", _lib.REC_FIELDS), ("GSDFT_VJP_FIELDS", _lib.VJP_FIELDS)):
+    for enum, width in (("GSDFT_REC_FIELDS", _lib.REC_FIELDS), ("GSDFT_VJP_FIELDS", _lib.VJP_FIELDS),
+                        ("GSDFT_XC_FIELDS", _lib.XC_FIELDS)):
         body = re.search(r"enum\s*\{([^}]*\b" + enum + r"\b[^}]*)\}", text).group(1)
         body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
         names = [t.strip().split("=")[0].strip() for t in body.split(",") if t.strip()]

@@ -221,3 +221,16 @@ def test_exact_coulomb_energy_matches_reference(case):
     if name == "rand48":
         Eu, _ = O.screened_coulomb_energy_exact(arr, g["uni_pi"], g["uni_pj"], g["uni_w"])
         np.testing.assert_allclose(Eu, float(r["rand48_E_unique"]), rtol=1e-12)
+
+
+def test_exact_coulomb_gradient_matches_reference():
+    """The oracle's closed-form gradient of the screened exact E_J against Richardson central
+    differences of the executed reference's ``screened_coulomb_energy`` (10 splats, padded ordered
+    list, pair list frozen)."""
+    r = load_golden("ref_exact_grad.npz")
+    arr = (r["quat"], r["log_scale"], r["centers"], r["C_occ"], r["occ"])
+    res = O.screened_coulomb_exact_and_grad(arr, r["pi"], r["pj"], r["valid"])
+    np.testing.assert_allclose(res["E"], float(r["E"]), rtol=1e-12)
+    for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
+        ref = r[k]
+        np.testing.assert_allclose(res[k], ref, rtol=0, atol=5e-9 * np.abs(ref).max())
