@@ -45,7 +45,7 @@ FP64_DATASHEET = 37e12
 # captured workloads are filled; others (and N > 1, whose slices change the reverse kernel's split
 # count) report null.
 NCU_TRAFFIC_N1 = {
-    3: {"j_vjp_kernel": 1065.27e6 + 757.69e6, "j_forward_kernel": 8032.55e6 + 50.20e6},
+    3: {"j_vjp_kernel": 1065.62e6 + 763.24e6, "j_forward_kernel": 8141.51e6 + 53.38e6},
 }
 L2_FLUSH_BYTES = 256 << 20
 # FP64 work per (pair, atom) unit of the screened nuclear attraction kernel with its reverse sums,
@@ -533,8 +533,8 @@ def measure_k(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flu
     # integral block (forward integrand) + weighted reverse pass + the three n_aux x n_rep x K2 GEMMs
     flop = integrals * (FLOP_FWD + FLOP_VJP) + 3 * 2.0 * integrals * K2
     return {"what": "screened RI-K on the pair list: E_K + full gradient per step (integral "
-                    "block, orbital products, cuBLAS DGEMM x 3 + trsm, weighted reverse pass, "
-                    "chain), not part of the metric",
+                    "block, orbital products and their inverse-factor products as DMMA GEMMs, "
+                    "weighted reverse pass, chain), not part of the metric",
             "ms_per_step": ms, "steps_timed": K, "evaluated_pairs": n_rep, "n_aux": n_aux,
             "n_occ": sy.n_occ, "integrals_per_s": integrals / (ms * 1e-3),
             "flop_per_step": flop, "achieved_tflops": flop / (ms * 1e-3) / 1e12,
@@ -544,30 +544,46 @@ def measure_k(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flu
 
 def measure_exact(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flush, peak,
                   args, **_):
-    """The screened exact Hartree energy (value; O(n_rep^2) pair-pair integrals) on the same pair
-    list, one warm-up and two timed evaluations with CUDA events (not part of the metric)."""
-    s = g.Splat(quat, log_scale, centers)
-    E = g.screened_coulomb_energy(s, C, occ, pi, pj, valid=valid)
-    torch.cuda.synchronize()
-    total, K = 0.0, 2
-    for k in range(K):
-        flush.fill_(float(k))
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        E = g.screened_coulomb_energy(s, C, occ, pi, pj, valid=valid)
-        b.record()
-        b.synchronize()
-        total += a.elapsed_time(b)
-    ms = total / K
+    """The screened exact Hartree energy on the same pair list (O(n_rep^2) pair-pair integrals):
+    the value, and the value with its full gradient (autograd through gsdft_exact_j_vjp); one
+    warm-up and two timed evaluations of each with CUDA events (not part of the metric)."""
+    def run(grad):
+        if grad:
+            leaves = [t.detach().clone().requires_grad_(True) for t in (quat, log_scale, centers, C)]
+            E = g.screened_coulomb_energy(g.Splat(*leaves[:3]), leaves[3], occ, pi, pj,
+                                          valid=valid)
+            E.backward()
+            return E
+        return g.screened_coulomb_energy(g.Splat(quat, log_scale, centers), C, occ, pi, pj,
+                                         valid=valid)
+
+    def timed(grad):
+        run(grad)
+        torch.cuda.synchronize()
+        total, K = 0.0, 2
+        for k in range(K):
+            flush.fill_(float(k))
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            E = run(grad)
+            b.record()
+            b.synchronize()
+            total += a.elapsed_time(b)
+        return total / K, K, E
+
+    ms, K, E = timed(False)
+    ms_grad, _, _ = timed(True)
     from gs_dft_b200.coulomb.engine import make_plan
     n_rep = make_plan(pi.to(torch.int32).contiguous(), pj.to(torch.int32).contiguous(),
                       valid.to(torch.float64).contiguous(), sy.M).n_rep_total
     pp = float(n_rep) * n_rep
-    return {"what": "screened exact E_J (Schur-equivalent 20-node (pair|pair) kernel, value; "
-                    "plan, pair prep and gsdft_exact_j per call), not part of the metric",
-            "ms": ms, "evaluations_timed": K, "evaluated_pairs": n_rep,
-            "pair_pairs_per_s": pp / (ms * 1e-3), "E_J_exact": float(E)}
+    return {"what": "screened exact E_J (Schur-equivalent 20-node (pair|pair) kernel; plan, pair "
+                    "prep and gsdft_exact_j per call) and E_J with its gradient (+ "
+                    "gsdft_exact_j_vjp, chain, reductions), not part of the metric",
+            "ms": ms, "ms_with_gradient": ms_grad, "evaluations_timed": K,
+            "evaluated_pairs": n_rep, "pair_pairs_per_s": pp / (ms * 1e-3),
+            "pair_pairs_per_s_reverse": pp / ((ms_grad - ms) * 1e-3), "E_J_exact": float(E)}
 
 
 def measure_e2e(torch, g, ks, sy, dev, pi, pj, valid, aux, L, args, world, rank, sh, barrier):

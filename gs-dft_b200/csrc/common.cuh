@@ -227,6 +227,32 @@ __device__ __forceinline__ double wexp2(double a, double t2, const double* __res
   return __hiloint2double(hi, lo);
 }
 
+// wexp2x<B>(x, tab) = w 2^x for an already formed exponent x (the product rounded once), clamped
+// at -2048 so that the table index and the exponent field stay in range for any x <= 0 (2^-2048 is
+// flushed to zero). For the exact (pair|pair) kernels, whose exponents reach far beyond the
+// 3-centre ones; the rounding of x adds a relative error |x| 2^-53 to a term of size 2^x.
+template <int B>
+__device__ __forceinline__ double wexp2x(double x, const double* __restrict__ tab) {
+  const double kRound = 6755399441055744.0 / (double)(1 << B);
+  x = fmax(x, -2048.0);
+  const double kd = x + kRound;
+  const int n = __double2loint(kd);
+  const double r = x - (kd - kRound);
+  double p = kExp2T5[5];
+  p = fma(p, r, kExp2T5[4]);
+  p = fma(p, r, kExp2T5[3]);
+  p = fma(p, r, kExp2T5[2]);
+  p = fma(p, r, kExp2T5[1]);
+  p = fma(p, r, kExp2T5[0]);
+  static_assert(B == 6, "wexp2x uses the degree-5 polynomial of the 64-entry tables");
+  const double v = tab[n & ((1 << B) - 1)] * p;
+  const int k = n >> B;
+  const bool keep = k >= -1000;
+  const int hi = keep ? __double2hiint(v) + (k << 20) : 0;
+  const int lo = keep ? __double2loint(v) : 0;
+  return __hiloint2double(hi, lo);
+}
+
 // Copy the per-node weighted tables kExp2WTab<B> (GSDFT_NQUAD x 2^B doubles) into shared memory
 // (all threads; the caller synchronises before use).
 template <int B>

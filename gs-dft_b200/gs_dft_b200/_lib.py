@@ -97,9 +97,9 @@ SIGNATURES = {
                                 _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_k_unit_q": (_i32, [_c_p, _i64, _c_p, _c_p]),
     "gsdft_exact_j_workspace_size": (_sz, [_i64]),
-    "gsdft_exact_j": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_exact_j": (_i32, [_c_p, _i64, _i32, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_exact_j_vjp_workspace_size": (_sz, [_i64]),
-    "gsdft_exact_j_vjp": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_exact_j_vjp": (_i32, [_c_p, _i64, _i32, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_density_grad": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p,
                                   _i64, _c_p, _c_p]),
 }

@@ -114,6 +114,9 @@ def make_plan(pi, pj, w, M: int, rank: int = 0, world: int = 1, merge_twins: boo
                     order_i=oi, seg_i=si, partner_i=qi, order_j=oj, seg_j=sj, partner_j=qj)
 
 
+# Quadrature rules of the exact (pair|pair) Hartree term (GSDFT_EXACT_SCHUR20 / _FUSED32).
+EXACT_RULES = {"schur": 0, "fused": 1}
+
 # Orbital counts from which q and g_C run as dense DMMA tiles over 64-splat row blocks
 # (gsdft_block_density / gsdft_block_density_grad); below it, per-pair kernels.
 BLOCK_MIN_OCC = 64
@@ -205,11 +208,14 @@ class RIJEngine:
             screening makes distant pairs cheaper), instead of equal representative counts.
         exact: the Hartree term is the exact (pair|pair) E_J over the representatives
             (``gsdft_exact_j`` / ``gsdft_exact_j_vjp``, O(n_rep^2)) instead of the density fit;
-            no aux, one device.
+            no aux, one device. ``exact_rule``: "schur" (the 20-node rule of
+            full_eri_block_schur) or "fused" (the 32-node Boys-scaled rule of
+            full_eri_block_fused).
     """
 
     def __init__(self, pi, pj, w, M, n_occ, beta=None, R=None, KN=None, L=None, rank=0, world=1,
-                 merge_twins=True, inverse_solve=True, atoms=None, balance=None, exact=False):
+                 merge_twins=True, inverse_solve=True, atoms=None, balance=None, exact=False,
+                 exact_rule="schur"):
         self.device = pi.device
         self.M, self.n_occ = int(M), int(n_occ)
         self.pi = pi.to(torch.int32).contiguous()
@@ -224,6 +230,9 @@ class RIJEngine:
         self.beta, self.R, self.KN, self.L = beta, R, KN, L
         self.rij = beta is not None
         self.exact = bool(exact)
+        if exact_rule not in EXACT_RULES:
+            raise ValueError(f"exact_rule must be one of {sorted(EXACT_RULES)}")
+        self.exact_rule = EXACT_RULES[exact_rule]
         self.n_aux = int(beta.shape[0]) if self.rij else 0
         if self.exact and (self.rij or world != 1):
             raise ValueError("the exact Hartree term replaces the density fit (no aux) and runs "
@@ -357,8 +366,8 @@ class RIJEngine:
         self.prepare(quat, log_scale, centers, C_occ, occ)
         self.last_forward = object()
         if self.exact:
-            lib.call("gsdft_exact_j", ptr(self.rec), nl, ptr(self.Jx), ptr(self.E), ptr(self.ws),
-                     self.ws_bytes, s)
+            lib.call("gsdft_exact_j", ptr(self.rec), nl, self.exact_rule, ptr(self.Jx),
+                     ptr(self.E), ptr(self.ws), self.ws_bytes, s)
             return self.E
         if not self.rij:
             return None
@@ -394,8 +403,8 @@ class RIJEngine:
             if end is not None:
                 end.record(torch.cuda.current_stream(self.device))
         if self.exact:
-            lib.call("gsdft_exact_j_vjp", ptr(self.rec), nl, ptr(g_E), ptr(self.xc), ptr(self.ws),
-                     self.ws_bytes, s)
+            lib.call("gsdft_exact_j_vjp", ptr(self.rec), nl, self.exact_rule, ptr(g_E),
+                     ptr(self.xc), ptr(self.ws), self.ws_bytes, s)
         if self.atoms is not None:
             self.external(sums=True, add=self.rij, g_E=g_E_ne)
         has_sums = self.rij or self.atoms is not None

@@ -46,20 +46,26 @@ class _ScreenedExactEnergy(torch.autograd.Function):
         return g_quat.clone(), g_log.clone(), eng.gmu.clone(), g_C, None, None
 
 
-def exact_engine(splats, C_orth, pi, pj, valid=None, merge_twins: bool = True):
+def exact_engine(splats, C_orth, pi, pj, valid=None, merge_twins: bool = True,
+                 block: str = "schur"):
     """The engine of the exact energy over the listed pairs (plan, records, buffers)."""
     dev = splats.centers.device
     n = int(pi.shape[0])
     w = (torch.ones(n, dtype=F64, device=dev) if valid is None else valid.to(F64).contiguous())
     return RIJEngine(pi.to(torch.int32).contiguous(), pj.to(torch.int32).contiguous(), w,
-                     splats.n_basis, int(C_orth.shape[1]), merge_twins=merge_twins, exact=True)
+                     splats.n_basis, int(C_orth.shape[1]), merge_twins=merge_twins, exact=True,
+                     exact_rule=block)
 
 
 def screened_coulomb_energy(splats, C_orth, occ, pi, pj, valid=None, bra_chunk: int = 128,
-                            merge_twins: bool = True, return_j: bool = False):
-    """Exact E_J over the listed pairs. With ``return_j`` also J_a = sum_b (a|b) P_b per
-    representative and the plan (representative -> list position in ``plan.rep_pos``)."""
-    eng = exact_engine(splats, C_orth, pi, pj, valid, merge_twins)
+                            merge_twins: bool = True, return_j: bool = False,
+                            block: str = "schur"):
+    """Exact E_J over the listed pairs. ``block`` picks the (pair|pair) quadrature: "schur" (the
+    reference's default, the 20-node rule of full_eri_block_schur) or "fused" (the 32-node
+    Boys-scaled rule of full_eri_block_fused, stream.py:323-458). With ``return_j`` also
+    J_a = sum_b (a|b) P_b per representative and the plan (representative -> list position in
+    ``plan.rep_pos``)."""
+    eng = exact_engine(splats, C_orth, pi, pj, valid, merge_twins, block)
     E = _ScreenedExactEnergy.apply(splats.quat, splats.log_scale, splats.centers, C_orth, occ, eng)
     if return_j:
         return E, eng.Jx[:eng.plan.n_rep].clone(), eng.plan

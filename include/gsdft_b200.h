@@ -412,23 +412,30 @@ int gsdft_k_backward(const double* rec, const int32_t* pi, const int32_t* pj,
 /* rec_out = rec with q = 1 (Q = 1, QK = KN pref), for the chain of a weighted reverse pass. */
 int gsdft_k_unit_q(const double* rec, int64_t n_rep, double* rec_out, gsdft_stream_t stream);
 
+/* Quadrature rules of the exact (pair|pair) integral: the 20-node half-line rule of the Schur block
+ * (full_eri_block_schur, gs_dft/coulomb/stream.py:249-283) and the 32-node Boys-scaled rule of the
+ * fused block (full_eri_block_fused, :323-458: nodes t^2 = rho c_k with a per-(a, b) scale rho). */
+enum { GSDFT_EXACT_SCHUR20 = 0, GSDFT_EXACT_FUSED32 = 1 };
+
 /* Screened exact Hartree energy E_J = 1/2 sum_{a,b} q_a q_b (a|b) over the pair representatives
  * (q from rec: pair weights, densities and merged twins included), (a|b) the exact 6-D Coulomb
- * integral of two product Gaussians on the reference's 20-node rule. Replaces
- * screened_coulomb_energy with full_eri_block_schur (gs_dft/coulomb/stream.py:249-320); value only.
- * Writes J (n_rep: J_a = sum_b q_b (a|b)) and E (device scalar). O(n_rep^2). Deterministic. */
+ * integral of two product Gaussians on the given rule. Replaces screened_coulomb_energy
+ * (gs_dft/coulomb/stream.py:294-320) with either block. Writes J (n_rep: J_a = sum_b q_b (a|b)) and
+ * E (device scalar). O(n_rep^2). Deterministic. The workspace size covers both rules. */
 size_t gsdft_exact_j_workspace_size(int64_t n_rep);
-int gsdft_exact_j(const double* rec, int64_t n_rep, double* J, double* E, void* ws, size_t ws_bytes,
-                  gsdft_stream_t stream);
+int gsdft_exact_j(const double* rec, int64_t n_rep, int rule, double* J, double* E, void* ws,
+                  size_t ws_bytes, gsdft_stream_t stream);
 
 /* Reverse pass of g_E * E_J (g_E a device scalar, NULL = 1) of gsdft_exact_j: per representative the
  * cotangents of A_hat, P and KN and dE/dq into xc (n_rep, GSDFT_XC_FIELDS), for gsdft_pair_chain
  * (sums NULL, or V_ne's). Each (a, b) evaluates dF/dH and dF/dd of the node sum in closed form over
- * the same 20 nodes (the derivative the reference takes by autodiff of the streamed Schur block,
- * gs_dft/coulomb/stream.py:144-189, 294-320). O(n_rep^2). Deterministic. */
+ * the same nodes (and, for the fused rule, the derivative through its per-(a, b) scale): the
+ * derivative the reference takes by autodiff of the streamed blocks with the fused rule's
+ * hand-written node VJP (gs_dft/coulomb/stream.py:144-189, 294-320, 356-398). O(n_rep^2).
+ * Deterministic. */
 size_t gsdft_exact_j_vjp_workspace_size(int64_t n_rep);
-int gsdft_exact_j_vjp(const double* rec, int64_t n_rep, const double* g_E, double* xc, void* ws,
-                      size_t ws_bytes, gsdft_stream_t stream);
+int gsdft_exact_j_vjp(const double* rec, int64_t n_rep, int rule, const double* g_E, double* xc,
+                      void* ws, size_t ws_bytes, gsdft_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -606,9 +606,51 @@ def eri_block_schur(q_splat, bi, bj, ki, kj):
     return (KNa[:, None] * KNb[None, :]) * coul
 
 
-def screened_coulomb_energy_exact(sys_arrays, pi, pj, valid, bra_chunk=128):
+def boys_scaled_nodes(n=32):
+    """The fused block's rule: Gauss-Legendre on u in [0,1), t^2 = rho c_k, c = u^2/(1-u^2),
+    e = (w/2)(1-u^2)^-3/2 (gs_dft/coulomb/stream.py:341-347)."""
+    x, w = np.polynomial.legendre.leggauss(n)
+    u = (x + 1.0) / 2.0
+    wu = w / 2.0
+    return u * u / (1.0 - u * u), wu * (1.0 - u * u) ** -1.5
+
+
+def eri_block_fused(q_splat, bi, bj, ki, kj, n_nodes=32):
+    """(a|b) for bra pairs x ket pairs by the fused scalar kernel (gs_dft/coulomb/stream.py:406-458):
+    C = A_a (A_a + A_b)^-1 A_b, its invariants I1, I2, I3, q2 = d.C d, q1 = I1 q2 - |C d|^2,
+    q0 = I3 |d|^2, the per-(a, b) scale rho = I3^(1/3) / (1 + q2), and
+    (a|b) = KN_a KN_b (2/sqrt(pi)) pi^3 sqrt(rho / det S) sum_k e_k exp(-s N(s)/D(s)) / sqrt(D(s)),
+    s = rho c_k, D(s) = ((s + I1) s + I2) s + I3, N(s) = q0 + s (q1 + s q2)."""
+    Aa, Pa, KNa = full_pair_quantities(q_splat, bi, bj)
+    Ab, Pb, KNb = full_pair_quantities(q_splat, ki, kj)
+    S = Aa[:, None] + Ab[None, :]
+    detS = det3(S)
+    C = np.einsum("akl,abln,bnm->abkm", Aa, adj3(S), Ab) / detS[..., None, None]
+    C = 0.5 * (C + np.swapaxes(C, -1, -2))
+    I1 = np.trace(C, axis1=-2, axis2=-1)
+    I2 = (C[..., 0, 0] * C[..., 1, 1] + C[..., 1, 1] * C[..., 2, 2] + C[..., 2, 2] * C[..., 0, 0]
+          - C[..., 0, 1] ** 2 - C[..., 0, 2] ** 2 - C[..., 1, 2] ** 2)
+    I3 = (det3(Aa)[:, None] * det3(Ab)[None, :]) / detS
+    d = Pa[:, None, :] - Pb[None, :, :]
+    Cd = np.einsum("abkl,abl->abk", C, d)
+    q2 = np.sum(d * Cd, -1)
+    q1 = I1 * q2 - np.sum(Cd * Cd, -1)
+    q0 = I3 * np.sum(d * d, -1)
+    rho = np.cbrt(I3) / (1.0 + q2)
+    acc = np.zeros_like(I1)
+    for c, e in zip(*boys_scaled_nodes(n_nodes)):
+        s = rho * c
+        D = ((s + I1) * s + I2) * s + I3
+        acc = acc + e * np.exp(-s * (q0 + s * (q1 + s * q2)) / D) / np.sqrt(D)
+    pref = 2.0 * PI ** 3 / math.sqrt(PI)
+    return (KNa[:, None] * KNb[None, :]) * pref * np.sqrt(rho / detS) * acc
+
+
+def screened_coulomb_energy_exact(sys_arrays, pi, pj, valid, bra_chunk=128, block="schur"):
     """Exact E_J = 1/2 sum_{a,b} P_a P_b (a|b) over the listed pairs, P_a = valid_a sum_o occ_o
-    C_io C_jo (gs_dft/coulomb/stream.py:294-320). Returns (E, Jvec) with Jvec_a = sum_b (a|b) P_b."""
+    C_io C_jo (gs_dft/coulomb/stream.py:294-320), with the Schur block (the reference's choice) or
+    the fused 32-node block. Returns (E, Jvec) with Jvec_a = sum_b (a|b) P_b."""
+    blk = eri_block_schur if block == "schur" else eri_block_fused
     quat, log_scale, centers, C, occ = sys_arrays
     q = full_quantities(quat, log_scale, centers)
     n = pi.shape[0]
@@ -619,10 +661,10 @@ def screened_coulomb_energy_exact(sys_arrays, pi, pj, valid, bra_chunk=128):
     jv = np.zeros(n)
     for a in range(0, n, bra_chunk):
         sl = slice(a, a + bra_chunk)
-        jv[sl] = eri_block_schur(q, pi[sl], pj[sl], ki, kj) @ Pk
+        jv[sl] = blk(q, pi[sl], pj[sl], ki, kj) @ Pk
     return 0.5 * float(np.sum(jv * Pw)), jv
 
-def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64):
+def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64, block="schur"):
     """Exact E_J (as ``screened_coulomb_energy_exact``), J per listed pair (0 on zero-weight
     entries) and the gradient of E_J with respect to (quat, log_scale, centers, C_occ), pair list
     frozen: the derivative the reference takes by autodiff of its streamed block
@@ -631,7 +673,10 @@ def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64):
     H = A_a^-1 + A_b^-1 and d = P_a - P_b, so (a|b) = (2/sqrt(pi)) pi^3 g_a g_b F(H, d),
     g = KN det(A)^-1/2 and F = sum_t w_t det(I + t^2 H)^-1/2 exp(-t^2 d.K_t d), K_t = (I + t^2 H)^-1:
       dF/dH = sum_t f_t (-1/2 t^2 K_t + t^4 u_t u_t^T),  dF/dd = -2 sum_t f_t t^2 u_t,  u_t = K_t d.
-    Each node's K_t is a direct 3x3 inverse here (no power expansion)."""
+    Each node's K_t is a direct 3x3 inverse here (no power expansion). ``block="fused"``: the
+    32-node rule t^2 = rho c_k with F = sqrt(rho) sum_k e_k (...), rho = det(H)^-1/3/(1 + d.H^-1 d),
+    which adds dF/drho (drho/dH, drho/dd), with d/ds of a node term f (-1/2 tr(K H) - |u|^2)."""
+    fused = block == "fused"
     quat, log_scale, centers, C_occ, occ = sys_arrays
     qs = full_quantities(quat, log_scale, centers)
     n = pi.shape[0]
@@ -651,6 +696,8 @@ def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64):
     T = np.zeros(nl)
     eye = np.eye(3)
     wk = q * g                                                   # q_b g_b
+    nodes = (list(zip(*boys_scaled_nodes(32))) if fused
+             else [(t * t, wq) for t, wq in zip(QUAD_T, QUAD_W)])
     for a0 in range(0, nl, bra_chunk):
         sl = slice(a0, a0 + bra_chunk)
         H = Ainv[sl, None] + Ainv[None, :]                        # (B, K, 3, 3)
@@ -658,15 +705,34 @@ def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64):
         F = np.zeros(H.shape[:2])
         gH = np.zeros(H.shape)
         gD = np.zeros(d.shape)
-        for t, wq in zip(QUAD_T, QUAD_W):
-            s2 = t * t
-            X = eye + s2 * H
+        rho = np.ones(H.shape[:2])
+        if fused:
+            Hinv = np.linalg.inv(H)
+            w_ = np.einsum("bkij,bkj->bki", Hinv, d)
+            q2 = np.sum(d * w_, -1)
+            rho = np.cbrt(1.0 / np.linalg.det(H)) / (1.0 + q2)
+            dF_drho = np.zeros(H.shape[:2])
+        for c, wq in nodes:
+            s2 = rho * c                                          # t^2 at this node
+            X = eye + s2[..., None, None] * H
             K = np.linalg.inv(X)
             u = np.einsum("bkij,bkj->bki", K, d)
             f = wq / np.sqrt(np.linalg.det(X)) * np.exp(-s2 * np.sum(d * u, -1))
             F += f
-            gH += f[..., None, None] * (-0.5 * s2 * K + (s2 * s2) * u[..., :, None] * u[..., None, :])
+            gH += f[..., None, None] * (-0.5 * s2[..., None, None] * K
+                                        + (s2 * s2)[..., None, None] * u[..., :, None] * u[..., None, :])
             gD += (-2.0 * s2 * f)[..., None] * u
+            if fused:
+                trKH = np.einsum("bkij,bkji->bk", K, H)
+                dF_drho += c * f * (-0.5 * trKH - np.sum(u * u, -1))
+        if fused:
+            sq = np.sqrt(rho)
+            dFr = 0.5 * F / sq + sq * dF_drho
+            F, gH, gD = sq * F, sq[..., None, None] * gH, sq[..., None] * gD
+            kr = (dFr * rho)
+            gH += kr[..., None, None] * (-Hinv / 3.0 + (w_[..., :, None] * w_[..., None, :])
+                                         / (1.0 + q2)[..., None, None])
+            gD += (-2.0 * kr / (1.0 + q2))[..., None] * w_
         T[sl] = F @ wk
         GH[sl] = np.einsum("bkij,k->bij", gH, wk)
         GD[sl] = np.einsum("bki,k->bi", gD, wk)

@@ -32,7 +32,9 @@ Outputs (compressed .npz, a few hundred KB in all):
 
   * ``ref_exact_grad.npz`` — the gradient of the screened exact Hartree energy w.r.t. (quat,
     log_scale, centers, C_occ) by Richardson central differences of the executed reference
-    (``screened_coulomb_energy``) on the 10-splat system, pair list frozen.
+    (``screened_coulomb_energy``) on the 10-splat system, pair list frozen; the same for the sum
+    over the fused 32-node block (``full_eri_block_fused``), and that sum's value on rand24's
+    padded ordered list.
 
 ``python tests/golden/make_golden.py vne`` (or ``k``, ``exact``, ``exact_grad``) regenerates only
 that file.
@@ -291,25 +293,45 @@ def make_exact_grad(eps=1e-7):
         return float(cs.screened_coulomb_energy(sp, J(C), J(s.occ), pi, pj, valid=v,
                                                 bra_chunk=32))
 
+    def energy_fused(quat, ls, cen, C):
+        # the same sum over the fused block (the reference's screened energy is Schur-only)
+        sp = spec.Splat(quat=J(quat), log_scale=J(ls), centers=J(cen))
+        Pw = np.asarray(v, np.float64) * np.sum(s.occ[None, :] * C[np.asarray(pi)]
+                                                * C[np.asarray(pj)], axis=1)
+        blk = np.asarray(cs.full_eri_block_fused(sp, pi, pj, pi, pj))
+        return 0.5 * float(Pw @ (blk @ Pw))
+
     x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy()]
 
-    def fd(k, h):
+    def fd(fn, k, h):
         g = np.zeros_like(x0[k])
         for idx in np.ndindex(x0[k].shape):
             xp = [a.copy() for a in x0]
             xm = [a.copy() for a in x0]
             xp[k][idx] += h
             xm[k][idx] -= h
-            g[idx] = (energy(*xp) - energy(*xm)) / (2 * h)
+            g[idx] = (fn(*xp) - fn(*xm)) / (2 * h)
         return g
 
     out = dict(quat=s.quat, log_scale=s.log_scale, centers=s.centers, C_occ=s.C_occ, occ=s.occ,
-               pi=np.asarray(pi), pj=np.asarray(pj), valid=np.asarray(v), E=energy(*x0), eps=eps)
-    for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
-        h = 1e-3
-        out[name] = (4 * fd(k, h / 2) - fd(k, h)) / 3      # Richardson, O(h^4)
+               pi=np.asarray(pi), pj=np.asarray(pj), valid=np.asarray(v), E=energy(*x0),
+               fused_E=energy_fused(*x0), eps=eps)
+    for prefix, fn in (("", energy), ("fused_", energy_fused)):
+        for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
+            h = 1e-3
+            out[prefix + name] = (4 * fd(fn, k, h / 2) - fd(fn, k, h)) / 3   # Richardson, O(h^4)
+    # the fused block's energy on rand24's padded ordered list
+    r24 = _cases()["rand24"]
+    sp = spec.Splat(quat=J(r24.quat), log_scale=J(r24.log_scale), centers=J(r24.centers))
+    qi, qj, _ = pairs.neighbor_pairs(sp, eps=eps)
+    qi, qj, qv = pairs.neighbor_pairs(sp, eps=eps, pad_to=int(qi.shape[0]) + 37)
+    Pw = np.asarray(qv, np.float64) * np.sum(r24.occ[None, :] * r24.C_occ[np.asarray(qi)]
+                                             * r24.C_occ[np.asarray(qj)], axis=1)
+    blk = np.asarray(cs.full_eri_block_fused(sp, qi, qj, qi, qj))
+    out["rand24_fused_E"] = 0.5 * float(Pw @ (blk @ Pw))
     np.savez_compressed(os.path.join(HERE, "ref_exact_grad.npz"), **out)
-    print("exact grad: M=10 E_J=", out["E"])
+    print("exact grad: M=10 E_J=", out["E"], "fused", out["fused_E"], "rand24 fused",
+          out["rand24_fused_E"])
 
 
 if __name__ == "__main__":

@@ -77,7 +77,7 @@ def _leaf(a):
     return dev(a).requires_grad_(True)
 
 
-def _grads(g, quat, log_scale, centers, C, occ, pi, pj, v, term=False):
+def _grads(g, quat, log_scale, centers, C, occ, pi, pj, v, term=False, block="schur"):
     """E and the autograd gradient of the exact E_J (direct call, or through the KS term)."""
     s = g.Splat(_leaf(quat), _leaf(log_scale), _leaf(centers))
     Ct = _leaf(C)
@@ -86,7 +86,7 @@ def _grads(g, quat, log_scale, centers, C, occ, pi, pj, v, term=False):
     if term:
         E, _ = g.ScreenedExactCoulomb().energy(s, Ct, None, dev(occ), g.SplatState(pairs=(pit, pjt, vt)))
     else:
-        E = g.screened_coulomb_energy(s, Ct, dev(occ), pit, pjt, valid=vt)
+        E = g.screened_coulomb_energy(s, Ct, dev(occ), pit, pjt, valid=vt, block=block)
     E.backward()
     return float(E), {"g_quat": s.quat.grad, "g_log_scale": s.log_scale.grad,
                       "g_centers": s.centers.grad, "g_C": Ct.grad}
@@ -98,24 +98,28 @@ def _close(got, want, rtol, what):
                                err_msg=what)
 
 
-def test_exact_gradient_vs_reference_fd(g):
+@pytest.mark.parametrize("block", ["schur", "fused"])
+def test_exact_gradient_vs_reference_fd(g, block):
     """gsdft_exact_j_vjp + the pair chain against Richardson central differences of the executed
-    reference's screened_coulomb_energy (10 splats, padded ordered list)."""
+    reference (10 splats, padded ordered list): screened_coulomb_energy (Schur block) and the same
+    sum over full_eri_block_fused (the 32-node rule)."""
     r = load_golden("ref_exact_grad.npz")
+    pre = "" if block == "schur" else "fused_"
     E, gr = _grads(g, r["quat"], r["log_scale"], r["centers"], r["C_occ"], r["occ"], r["pi"],
-                   r["pj"], r["valid"])
-    np.testing.assert_allclose(E, float(r["E"]), rtol=1e-10)
+                   r["pj"], r["valid"], block=block)
+    np.testing.assert_allclose(E, float(r[pre + "E"]), rtol=1e-10)
     for k, v in gr.items():
-        ref = r[k]
+        ref = r[pre + k]
         np.testing.assert_allclose(v.cpu().numpy(), ref, rtol=0, atol=5e-9 * np.abs(ref).max(),
                                    err_msg=k)
 
 
-@pytest.mark.parametrize("case", ["ref_rand24.npz", "ref_co2.npz"])
-def test_exact_gradient_vs_oracle(g, case):
+@pytest.mark.parametrize("case,block", [("ref_rand24.npz", "schur"), ("ref_co2.npz", "schur"),
+                                        ("ref_rand24.npz", "fused"), ("ref_co2.npz", "fused")])
+def test_exact_gradient_vs_oracle(g, case, block):
     """The exact-E_J gradient against the oracle's closed form (direct 3x3 inverses per node) at
-    relative 1e-10: rand24's padded ordered list (twins merged on the GPU, zero-weight padding) and
-    the first 600 ordered pairs of CO2 (unmatched twins)."""
+    relative 1e-10, for both rules: rand24's padded ordered list (twins merged on the GPU,
+    zero-weight padding) and the first 600 ordered pairs of CO2 (unmatched twins)."""
     d = load_golden(case)
     if case == "ref_co2.npz":
         r = load_golden("ref_exact.npz")
@@ -123,11 +127,14 @@ def test_exact_gradient_vs_oracle(g, case):
     else:
         pi, pj, v = d["pad_pi"], d["pad_pj"], d["pad_v"]
     arr = (d["quat"], d["log_scale"], d["centers"], d["C_occ"], d["occ"])
-    ref = O.screened_coulomb_exact_and_grad(arr, pi, pj, v)
-    E, gr = _grads(g, *arr, pi, pj, v)
+    ref = O.screened_coulomb_exact_and_grad(arr, pi, pj, v, block=block)
+    E, gr = _grads(g, *arr, pi, pj, v, block=block)
     np.testing.assert_allclose(E, ref["E"], rtol=1e-10)
     for k, t in gr.items():
-        _close(t, ref[k], 1e-10, f"{case} {k}")
+        _close(t, ref[k], 1e-10, f"{case} {block} {k}")
+    if case == "ref_rand24.npz" and block == "fused":
+        np.testing.assert_allclose(E, float(load_golden("ref_exact_grad.npz")["rand24_fused_E"]),
+                                   rtol=1e-10)
 
 
 def test_exact_term_is_differentiable_and_forward_token(g):

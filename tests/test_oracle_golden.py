@@ -223,14 +223,28 @@ def test_exact_coulomb_energy_matches_reference(case):
         np.testing.assert_allclose(Eu, float(r["rand48_E_unique"]), rtol=1e-12)
 
 
-def test_exact_coulomb_gradient_matches_reference():
+@pytest.mark.parametrize("block", ["schur", "fused"])
+def test_exact_coulomb_gradient_matches_reference(block):
     """The oracle's closed-form gradient of the screened exact E_J against Richardson central
-    differences of the executed reference's ``screened_coulomb_energy`` (10 splats, padded ordered
-    list, pair list frozen)."""
+    differences of the executed reference (10 splats, padded ordered list, pair list frozen): its
+    ``screened_coulomb_energy`` (Schur block) and the same sum over ``full_eri_block_fused``."""
     r = load_golden("ref_exact_grad.npz")
+    pre = "" if block == "schur" else "fused_"
     arr = (r["quat"], r["log_scale"], r["centers"], r["C_occ"], r["occ"])
-    res = O.screened_coulomb_exact_and_grad(arr, r["pi"], r["pj"], r["valid"])
-    np.testing.assert_allclose(res["E"], float(r["E"]), rtol=1e-12)
+    res = O.screened_coulomb_exact_and_grad(arr, r["pi"], r["pj"], r["valid"], block=block)
+    np.testing.assert_allclose(res["E"], float(r[pre + "E"]), rtol=1e-12)
     for k in ("g_quat", "g_log_scale", "g_centers", "g_C"):
-        ref = r[k]
+        ref = r[pre + k]
         np.testing.assert_allclose(res[k], ref, rtol=0, atol=5e-9 * np.abs(ref).max())
+
+
+def test_exact_coulomb_fused_block_energy_matches_reference():
+    """The fused 32-node block's sum on rand24's padded ordered list against the executed
+    reference's ``full_eri_block_fused``; the fused and Schur rules agree to quadrature accuracy."""
+    g = load_golden("ref_rand24.npz")
+    r = load_golden("ref_exact_grad.npz")
+    arr = (g["quat"], g["log_scale"], g["centers"], g["C_occ"], g["occ"])
+    E, _ = O.screened_coulomb_energy_exact(arr, g["pad_pi"], g["pad_pj"], g["pad_v"], block="fused")
+    np.testing.assert_allclose(E, float(r["rand24_fused_E"]), rtol=1e-12)
+    Es = float(load_golden("ref_exact.npz")["rand24_E"])
+    np.testing.assert_allclose(E, Es, rtol=1e-6)

@@ -84,18 +84,21 @@ def test_boys_small_argument_branch_joins_closed_form():
     np.testing.assert_allclose(F, closed, rtol=1e-14)
 
 
-def test_exact_coulomb_gradient_is_the_derivative_of_the_schur_energy():
+@pytest.mark.parametrize("block", ["schur", "fused"])
+def test_exact_coulomb_gradient_is_the_derivative_of_the_block_energy(block):
     """The closed-form exact-E_J gradient (direct 3x3 inverses per node) against Richardson
-    central differences of the oracle's Schur-complement energy on a seeded 8-splat system: the
-    two formulations of (a|b) are independent, so this pins the derivative and the algebra that
-    turns the 6x6 Schur determinant into det(I + t^2 H)."""
+    central differences of the oracle's block energy on a seeded 8-splat system: the Schur-
+    complement block, and the fused block in the reference's invariant form (C = A_a S^-1 A_b,
+    I1, I2, I3, q0, q1, q2, rho). The formulations of (a|b) are independent, so this pins the
+    derivative (with the fused rule's per-(a, b) scale) and the algebra that turns either form
+    into det(I + t^2 H)."""
     from gs_dft_b200.systems import small_random_system
     s = small_random_system(8, 2, seed=5, spread=1.0)
     x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy(), s.occ.copy()]
     q = O.full_quantities(*x0[:3])
     pi, pj, v = O.neighbor_pairs(q, eps=1e-7)[:3]
-    res = O.screened_coulomb_exact_and_grad(tuple(x0), pi, pj, v)
-    E0, J0 = O.screened_coulomb_energy_exact(tuple(x0), pi, pj, v)
+    res = O.screened_coulomb_exact_and_grad(tuple(x0), pi, pj, v, block=block)
+    E0, J0 = O.screened_coulomb_energy_exact(tuple(x0), pi, pj, v, block=block)
     np.testing.assert_allclose(res["E"], E0, rtol=1e-13)
     np.testing.assert_allclose(res["J"], J0, rtol=1e-12, atol=1e-14 * np.abs(J0).max())
 
@@ -106,8 +109,8 @@ def test_exact_coulomb_gradient_is_the_derivative_of_the_schur_energy():
             xm = [a.copy() for a in x0]
             xp[k][idx] += h
             xm[k][idx] -= h
-            g[idx] = (O.screened_coulomb_energy_exact(tuple(xp), pi, pj, v)[0]
-                      - O.screened_coulomb_energy_exact(tuple(xm), pi, pj, v)[0]) / (2 * h)
+            g[idx] = (O.screened_coulomb_energy_exact(tuple(xp), pi, pj, v, block=block)[0]
+                      - O.screened_coulomb_energy_exact(tuple(xm), pi, pj, v, block=block)[0]) / (2 * h)
         return g
 
     for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
