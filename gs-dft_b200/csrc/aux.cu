@@ -59,8 +59,11 @@ __device__ __forceinline__ double boys0(double T) {
 }
 
 // One metric entry in the canonical orientation (lo, hi) so V is exactly symmetric.
+// omega > 0: the long-range erf(omega r)/r kernel, F0(T) -> sqrt(z) F0(z T), z = omega^2 /
+// (omega^2 + rho) (gs_dft/coulomb/ri.py:63-76).
 __global__ void aux_metric_kernel(const double* __restrict__ beta, const double* __restrict__ R,
-                                  const double* __restrict__ KN, int64_t n, double* __restrict__ V) {
+                                  const double* __restrict__ KN, int64_t n, double omega,
+                                  double* __restrict__ V) {
   int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   if (q >= n) return;
   for (int64_t p = blockIdx.y; p < n; p += gridDim.y) {
@@ -73,7 +76,14 @@ __global__ void aux_metric_kernel(const double* __restrict__ beta, const double*
     double PQ2 = dx * dx + dy * dy + dz * dz;
     double rho = gab / gsum;
     double T = rho * PQ2;
-    double coul = 34.986836655249725 / (gab * sqrt(gsum)) * boys0(T);   // 2 pi^2.5
+    double F0;
+    if (omega > 0.0) {
+      const double z = (omega * omega) / (omega * omega + rho);
+      F0 = sqrt(z) * boys0(z * T);
+    } else {
+      F0 = boys0(T);
+    }
+    double coul = 34.986836655249725 / (gab * sqrt(gsum)) * F0;   // 2 pi^2.5
     V[p * n + q] = (KN[lo] * KN[hi]) * coul;
   }
 }
@@ -254,8 +264,74 @@ extern "C" int gsdft_aux_metric(const double* beta, const double* R, const doubl
   GSDFT_REQUIRE(n_aux > 0 && n_aux < (int64_t(1) << 31), "n_aux out of range");
   GSDFT_REQUIRE(beta && R && KN && V, "null pointer");
   dim3 grid(grid_1d(n_aux, 128), (unsigned)imin64(n_aux, 65535));
-  aux_metric_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(beta, R, KN, n_aux, V);
+  aux_metric_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(beta, R, KN, n_aux, 0.0, V);
   GSDFT_LAUNCHED("aux_metric");
+  return GSDFT_OK;
+}
+
+extern "C" int gsdft_aux_metric_lr(const double* beta, const double* R, const double* KN,
+                                   int64_t n_aux, double omega, double* V, gsdft_stream_t stream) {
+  GSDFT_REQUIRE(n_aux > 0 && n_aux < (int64_t(1) << 31), "n_aux out of range");
+  GSDFT_REQUIRE(omega > 0.0, "omega must be positive");
+  GSDFT_REQUIRE(beta && R && KN && V, "null pointer");
+  dim3 grid(grid_1d(n_aux, 128), (unsigned)imin64(n_aux, 65535));
+  aux_metric_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(beta, R, KN, n_aux, omega, V);
+  GSDFT_LAUNCHED("aux_metric");
+  return GSDFT_OK;
+}
+
+namespace gsdft {
+// Gauss-Legendre on [0, upper] (nq <= GSDFT_NQUAD nodes, ascending) as a runtime node table:
+// table[n] = t_n^2, table[GSDFT_NQUAD + n] = t_n^4, and from 2 GSDFT_NQUAD on, node n's row of 64
+// weighted exp2 entries w_n 2^(j/64). The roots of P_nq by Newton's method from the standard
+// cosine guesses (each thread one root, in FP64; the iteration stops at a relative step of 1e-16 or
+// after 100 steps), the weights 2 / ((1 - x^2) P'_nq(x)^2), mapped t = upper (x + 1)/2,
+// w = upper w_GL / 2 (gs_dft/integrals/dense.py:56-76).
+__device__ void legendre_eval(int nq, double x, double* p, double* dp) {
+  double p0 = 1.0, p1 = x;
+  for (int k = 1; k < nq; ++k) {
+    const double p2 = ((2.0 * k + 1.0) * x * p1 - k * p0) / (k + 1.0);
+    p0 = p1;
+    p1 = p2;
+  }
+  *p = p1;
+  *dp = nq * (x * p1 - p0) / (x * x - 1.0);
+}
+
+__global__ void lr_node_table_kernel(double upper, int nq, double* __restrict__ table) {
+  __shared__ double w[GSDFT_NQUAD];
+  const int n = threadIdx.x;
+  if (n < nq) {
+    const int i = nq - 1 - n;  // the guesses descend in x
+    double x = cos(3.14159265358979323846 * (i + 0.75) / (nq + 0.5));
+    double p, dp;
+    for (int it = 0; it < 100; ++it) {
+      legendre_eval(nq, x, &p, &dp);
+      const double dx = p / dp;
+      x -= dx;
+      if (fabs(dx) <= 1e-16 * fmax(fabs(x), 1e-3)) break;
+    }
+    legendre_eval(nq, x, &p, &dp);
+    const double t = 0.5 * upper * (x + 1.0);
+    table[n] = t * t;
+    table[GSDFT_NQUAD + n] = (t * t) * (t * t);
+    w[n] = 0.5 * upper * (2.0 / ((1.0 - x * x) * dp * dp));
+  } else if (n < GSDFT_NQUAD) {
+    table[n] = 0.0;
+    table[GSDFT_NQUAD + n] = 0.0;
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < nq * 64; k += blockDim.x)
+    table[2 * GSDFT_NQUAD + k] = w[k / 64] * exp2((k % 64) / 64.0);
+}
+}  // namespace gsdft
+
+extern "C" int gsdft_lr_node_table(double upper, int n_nodes, double* table,
+                                   gsdft_stream_t stream) {
+  GSDFT_REQUIRE(upper > 0.0 && n_nodes >= 1 && n_nodes <= GSDFT_NQUAD, "bad node rule");
+  GSDFT_REQUIRE(table, "null pointer");
+  lr_node_table_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(upper, n_nodes, table);
+  GSDFT_LAUNCHED("lr_node_table");
   return GSDFT_OK;
 }
 

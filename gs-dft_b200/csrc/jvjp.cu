@@ -56,15 +56,26 @@ __global__ void aux_vjp_pack_kernel(const double* __restrict__ beta, const doubl
 // each evaluated). Read by gsdft_node_evals.
 static __device__ unsigned long long g_vjp_node_evals;
 
-template <bool kW>
+// kLR: the node rule is a runtime table (gsdft_lr_node_table: t^2, t^4 and the weighted exp2 rows
+// of nq <= GSDFT_NQUAD nodes, e.g. the long-range kernel's segment rule) instead of the half-line
+// one; node screening is off for it (its weights are not monotone along the nodes).
+template <bool kW, bool kLR = false>
 __global__ void GSDFT_VJP_BOUNDS
     j_vjp_kernel(const double* __restrict__ rec, int64_t n_live, const double* __restrict__ auxr,
                  int64_t n_aux, int64_t per_split, double skip2, double* __restrict__ out,
-                 const double* __restrict__ Wt, int64_t ldw) {
+                 const double* __restrict__ Wt, int64_t ldw, const double* __restrict__ nodes,
+                 int nq) {
   __shared__ __align__(128) double tile[2][kVjpTile * kAuxRec];
   __shared__ __align__(8) uint64_t bar[2];
+  __shared__ double lrt[kLR ? 2 * GSDFT_NQUAD : 1];  // runtime rule: t^2, then t^4
   extern __shared__ __align__(16) double etab[];  // GSDFT_NQUAD x 2^kVjpBits weighted table
-  load_wexp2_tables<kVjpBits>(etab);
+  if (kLR) {
+    static_assert(!kLR || kVjpBits == 6, "runtime node tables have 64-entry rows");
+    for (int k = threadIdx.x; k < nq * 64; k += blockDim.x) etab[k] = nodes[2 * GSDFT_NQUAD + k];
+    for (int k = threadIdx.x; k < 2 * GSDFT_NQUAD; k += blockDim.x) lrt[k] = nodes[k];
+  } else {
+    load_wexp2_tables<kVjpBits>(etab);
+  }
   const int64_t a = blockIdx.x * (int64_t)kVjpThreads + threadIdx.x;
   const bool live = a < n_live;
   const int64_t aa = live ? a : 0;
@@ -124,10 +135,11 @@ __global__ void GSDFT_VJP_BOUNDS
       }
       double cf = 0.0, B[3] = {0, 0, 0}, C[3] = {0, 0, 0}, Z[6] = {0, 0, 0, 0, 0, 0};
       double e0 = 0.0;
-      int nodes = GSDFT_NQUAD;
+      int nodes_done = kLR ? nq : GSDFT_NQUAD;
 #pragma unroll
       for (int n = 0; n < GSDFT_NQUAD; ++n) {
-        const double t2 = kQuadT2[n], t4 = kQuadT4[n];
+        if (kLR && n >= nq) break;
+        const double t2 = kLR ? lrt[n] : kQuadT2[n], t4 = kLR ? lrt[GSDFT_NQUAD + n] : kQuadT4[n];
         // Gamma_k = lam_k (beta + t^2) + t^2 beta, rebuilt from two per-node scalars
         const double sn = b + t2, un = t2 * b;
         const double G0 = fma(L[0], sn, un);
@@ -158,12 +170,12 @@ __global__ void GSDFT_VJP_BOUNDS
         Z[4] = fma(h0, iG2, Z[4]);
         Z[5] = fma(h1, iG2, Z[5]);
         // node screening (warp-uniform): every later node is below the last bit of every lane's sums
-        if (node_check(n) && __all_sync(0xffffffffu, fma(x, t2, -e0) < -skip2)) {
-          nodes = n + 1;
+        if (!kLR && node_check(n) && __all_sync(0xffffffffu, fma(x, t2, -e0) < -skip2)) {
+          nodes_done = n + 1;
           break;
         }
       }
-      evals += (unsigned long long)nodes;
+      evals += (unsigned long long)nodes_done;
       SJ = fma(dk, cf, SJ);
       const double dkb = dk * b, dkb2 = dk * b2;
 #pragma unroll
@@ -480,13 +492,13 @@ __global__ void __launch_bounds__(kDgWarps * 32)
 // Aux splits: pair tiles x S CTAs filling whole waves of resident CTAs (S <= 8, since the partial
 // sums take S x n_live x 13 doubles). The occupancy query runs once per template (a thread-safe
 // static).
-template <bool kW>
+template <bool kW, bool kLR = false>
 static int vjp_splits(int64_t n_live, int64_t n_aux) {
   static const int per_sm = [] {
     int v = 0;
-    cudaFuncSetAttribute(j_vjp_kernel<kW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaFuncSetAttribute(j_vjp_kernel<kW, kLR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)kVjpDynSmem);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, j_vjp_kernel<kW>, kVjpThreads,
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, j_vjp_kernel<kW, kLR>, kVjpThreads,
                                                   kVjpDynSmem);
     return v > 0 ? v : 1;
   }();
@@ -522,18 +534,19 @@ namespace gsdft {
 template <bool kW>
 static size_t vjp_workspace_size(int64_t n_live, int64_t n_aux) {
   int S = vjp_splits<kW>(n_live, n_aux);
+  if constexpr (kW) S = (int)imax64(S, vjp_splits<kW, true>(n_live, n_aux));  // either rule
   Sizer z;
   z.take<double>((size_t)n_aux * kAuxRec);
   if (S > 1) z.take<double>((size_t)S * n_live * GSDFT_VJP_FIELDS);
   return z.off + 256;
 }
 
-template <bool kW>
+template <bool kW, bool kLR = false>
 static int vjp_run(const double* rec, int64_t n_live, const double* beta, const double* R,
                    const double* KN, const double* d, const double* g_E, const double* Wt,
                    int64_t ldw, int64_t n_aux, double* sums, void* ws, size_t ws_bytes,
-                   cudaStream_t st) {
-  int S = vjp_splits<kW>(n_live, n_aux);
+                   cudaStream_t st, const double* nodes = nullptr, int nq = 0) {
+  int S = vjp_splits<kW, kLR>(n_live, n_aux);
   Carver c(ws, ws_bytes);
   double* auxr = c.take<double>((size_t)n_aux * kAuxRec);
   double* part = S > 1 ? c.take<double>((size_t)S * n_live * GSDFT_VJP_FIELDS) : sums;
@@ -542,8 +555,8 @@ static int vjp_run(const double* rec, int64_t n_live, const double* beta, const 
   GSDFT_LAUNCHED("aux_vjp_pack");
   int64_t per_split = (n_aux + S - 1) / S;
   dim3 grid((unsigned)((n_live + kVjpThreads - 1) / kVjpThreads), (unsigned)S);
-  j_vjp_kernel<kW><<<grid, kVjpThreads, kVjpDynSmem, st>>>(rec, n_live, auxr, n_aux, per_split,
-                                                            node_skip_threshold(), part, Wt, ldw);
+  j_vjp_kernel<kW, kLR><<<grid, kVjpThreads, kVjpDynSmem, st>>>(
+      rec, n_live, auxr, n_aux, per_split, node_skip_threshold(), part, Wt, ldw, nodes, nq);
   GSDFT_LAUNCHED("j_vjp");
   if (S > 1) {
     sum_vjp_splits_kernel<<<grid_1d(n_live * GSDFT_VJP_FIELDS, 256), 256, 0, st>>>(part, S, n_live,
@@ -574,12 +587,17 @@ extern "C" size_t gsdft_j_vjp_weighted_workspace_size(int64_t n_live, int64_t n_
 
 extern "C" int gsdft_j_vjp_weighted(const double* rec, int64_t n_live, const double* beta,
                                     const double* R, const double* KN, const double* Wt,
-                                    int64_t ldw, int64_t n_aux, double* sums, void* ws,
-                                    size_t ws_bytes, gsdft_stream_t stream) {
+                                    int64_t ldw, int64_t n_aux, const double* nodes, int n_nodes,
+                                    double* sums, void* ws, size_t ws_bytes,
+                                    gsdft_stream_t stream) {
   GSDFT_REQUIRE(n_live >= 0 && n_aux > 0 && n_aux < (int64_t(1) << 31) && ldw >= n_live,
                 "bad sizes");
+  GSDFT_REQUIRE(!nodes || (n_nodes >= 1 && n_nodes <= GSDFT_NQUAD), "bad node count");
   if (n_live == 0) return GSDFT_OK;
   GSDFT_REQUIRE(rec && beta && R && KN && Wt && sums, "null pointer");
+  if (nodes)
+    return vjp_run<true, true>(rec, n_live, beta, R, KN, nullptr, nullptr, Wt, ldw, n_aux, sums,
+                               ws, ws_bytes, (cudaStream_t)stream, nodes, n_nodes);
   return vjp_run<true>(rec, n_live, beta, R, KN, nullptr, nullptr, Wt, ldw, n_aux, sums, ws,
                        ws_bytes, (cudaStream_t)stream);
 }

@@ -17,8 +17,9 @@ REC_FIELDS = 18
 VJP_FIELDS = 13
 SIDE_FIELDS = 20
 XC_FIELDS = 11
+NODE_TABLE_DOUBLES = 1320
 SOLVE_INV_MAX = 65536   # GSDFT_SOLVE_INV_MAX
-ABI_VERSION = 3         # GSDFT_ABI_VERSION
+ABI_VERSION = 4         # GSDFT_ABI_VERSION
 
 _c_p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -87,14 +88,16 @@ SIGNATURES = {
                          _c_p, _sz, _c_p]),
     "gsdft_density_pairs": (_i32, [_c_p, _c_p, _i64, _c_p, _c_p, _i64, _c_p, _c_p]),
     "gsdft_j_vjp_weighted_workspace_size": (_sz, [_i64, _i64]),
-    "gsdft_j_vjp_weighted": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _c_p, _sz,
-                                    _c_p]),
-    "gsdft_k_workspace_size": (_sz, [_i64, _i64, _i64]),
-    "gsdft_k_forward": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _c_p,
-                               _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
-    "gsdft_k_backward": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p,
-                                _c_p, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _i64,
-                                _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_j_vjp_weighted": (_i32, [_c_p, _i64, _c_p, _c_p, _c_p, _c_p, _i64, _i64, _c_p, _i32, _c_p,
+                                    _c_p, _sz, _c_p]),
+    "gsdft_lr_node_table": (_i32, [_f64, _i32, _c_p, _c_p]),
+    "gsdft_aux_metric_lr": (_i32, [_c_p, _c_p, _c_p, _i64, _f64, _c_p, _c_p]),
+    "gsdft_k_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "gsdft_k_forward": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _i32,
+                               _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
+    "gsdft_k_backward": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p, _i64, _c_p, _c_p, _c_p, _i64, _c_p, _i32,
+                                _c_p, _c_p, _i64, _i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                _c_p, _i64, _c_p, _c_p, _c_p, _sz, _c_p]),
     "gsdft_k_unit_q": (_i32, [_c_p, _i64, _c_p, _c_p]),
     "gsdft_exact_j_workspace_size": (_sz, [_i64]),
     "gsdft_exact_j": (_i32, [_c_p, _i64, _i32, _c_p, _c_p, _c_p, _sz, _c_p]),

@@ -8,23 +8,35 @@ every reduction, the reverse pass and the contractions (the library's DMMA GEMMs
 inverse factor for L^-1 and L^-T) are the library's kernels (``gsdft_k_forward`` /
 ``gsdft_k_backward``), then the same pair chain, per-splat reductions and chart reverse as RI-J.
 
-Differences from the reference, by design: the whole pair list is processed in one pass, holding
-the integral block and the orbital products (8 n_rep (n_aux + 2 n_occ^2) bytes, 1.8 GB at
-ethanol) instead of streaming over orbital chunks in O(n_aux^2) memory, so ``occ_chunk`` and
-``chunk`` are accepted and unused and lists beyond ``max_bytes`` raise; the solve uses the
-Cholesky factor's inverse, formed once per engine (the reference LU-solves V + lam I). ``omega``
-(range-separated exchange) is not supported.
+The orbital products are streamed over chunks of ``occ_chunk`` orbitals, as the reference streams
+its M-build: only n_rep x occ_chunk x n_occ products are held at a time. Differences from the
+reference, by design: the integral block over the whole list is kept resident for the step
+(8 n_rep n_aux bytes) instead of being recomputed per orbital chunk, and D's n_aux x n_occ^2 entries
+are held (the reference keeps only M); lists whose workspace exceeds ``max_bytes`` raise; the solve
+uses the Cholesky factor's inverse, formed once per engine (the reference LU-solves V + lam I).
+``chunk`` (the reference's pair-chunk knob) is accepted and unused. ``omega`` gives the long-range
+exchange E_K[erf(omega r)/r]: the 12-node segment rule on [0, omega] for the 3-centre integrals and
+the attenuated metric's factor (gs_dft/coulomb/ri.py:149,232-235,267-275).
 """
 from __future__ import annotations
 
 import torch
 
-from .._lib import REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, lib, ptr, stream_handle
+from .._lib import (NODE_TABLE_DOUBLES, REC_FIELDS, SIDE_FIELDS, SOLVE_INV_MAX, VJP_FIELDS, lib,
+                    ptr, stream_handle)
 from .. import _check
 from .engine import check_step_inputs, make_plan
 
 F64 = torch.float64
 MAX_WORKSPACE_BYTES = 64 << 30
+CHUNK_BYTES = 2 << 30        # the orbital-product chunk chosen when occ_chunk is None
+LR_NODES = 12                # nodes of the long-range segment rule (gs_dft/coulomb/ri.py:232)
+
+
+def auto_occ_chunk(n_rep: int, n_occ: int, budget: int = CHUNK_BYTES) -> int:
+    """Orbitals per chunk so that the n_rep x chunk x n_occ products fit ``budget`` bytes."""
+    per = 8 * max(n_rep, 1) * n_occ
+    return int(max(1, min(n_occ, budget // per)))
 
 
 class RIKEngine:
@@ -33,12 +45,15 @@ class RIKEngine:
     Args:
         pi, pj: int32 pair indices (device); valid: bool mask or 0/1 weights (0 = padding).
         M: number of splats; n_occ: orbitals (columns of C).
-        beta, R, KN: aux quantities; L: lower Cholesky factor of V + lam I (row-major).
+        beta, R, KN: aux quantities; L: lower Cholesky factor of V + lam I (row-major); with
+            ``omega`` the factor of the long-range metric (``aux_cholesky(aux, lam, omega)``).
         merge_twins: evaluate each live (i,j)/(j,i) twin once (same integral).
+        omega: range separation: the long-range exchange E_K[erf(omega r)/r].
+        occ_chunk: orbitals per product chunk (None: as many as fit ``CHUNK_BYTES``).
     """
 
     def __init__(self, pi, pj, valid, M, n_occ, beta, R, KN, L, merge_twins=True,
-                 max_bytes=MAX_WORKSPACE_BYTES):
+                 max_bytes=MAX_WORKSPACE_BYTES, omega=None, occ_chunk=None):
         w = valid.to(F64).contiguous()
         if bool(((w != 0) & (w != 1)).any()):
             raise ValueError("screened RI-K takes an ordered pair list with a 0/1 mask, as the "
@@ -62,10 +77,22 @@ class RIKEngine:
         lib.call("gsdft_j_solve_inverse", ptr(self.L), self.n_aux, ptr(self.Linv),
                  stream_handle(pi.device))
         dev, nl, n = self.device, self.plan.n_rep, self.plan.n
-        self.ws_bytes = int(lib.gsdft_k_workspace_size(nl, self.n_aux, self.n_occ))
+        self.omega = None if not omega else float(omega)
+        self.nodes, self.n_nodes = None, 0
+        if self.omega is not None:
+            if self.omega <= 0.0:
+                raise ValueError("omega must be positive")
+            self.nodes = torch.empty(NODE_TABLE_DOUBLES, dtype=F64, device=dev)
+            self.n_nodes = LR_NODES
+            lib.call("gsdft_lr_node_table", self.omega, LR_NODES, ptr(self.nodes),
+                     stream_handle(dev))
+        self.occ_chunk = (auto_occ_chunk(nl, self.n_occ) if occ_chunk is None
+                          else int(max(1, min(int(occ_chunk), self.n_occ))))
+        self.ws_bytes = int(lib.gsdft_k_workspace_size(nl, self.n_aux, self.n_occ, self.occ_chunk))
         if self.ws_bytes > max_bytes:
             raise ValueError(f"screened RI-K needs {self.ws_bytes / 2**30:.1f} GiB of workspace for "
-                             f"{nl} pairs x {self.n_aux} aux x {self.n_occ}^2 orbital products "
+                             f"{nl} pairs x {self.n_aux} aux (integral block) with {self.occ_chunk}"
+                             f"-orbital chunks of {self.n_occ} orbitals "
                              f"(limit {max_bytes / 2**30:.0f} GiB)")
         e = lambda *s: torch.empty(s, dtype=F64, device=dev)
         self.A9, self.N = e(self.M, 9), e(self.M)
@@ -91,8 +118,9 @@ class RIKEngine:
                  ptr(self.rec), s)
         lib.call("gsdft_k_forward", ptr(self.rec), ptr(self.pi), ptr(self.pj),
                  ptr(self.plan.rep_pos), ptr(self.plan.rep_twin), nl, ptr(self.beta), ptr(self.R),
-                 ptr(self.KN), self.n_aux, ptr(self.Linv), ptr(C), self.n_occ, ptr(self.Z),
-                 ptr(self.E), ptr(self.ws), self.ws_bytes, s)
+                 ptr(self.KN), self.n_aux, ptr(self.nodes), self.n_nodes, ptr(self.Linv), ptr(C),
+                 self.n_occ, self.occ_chunk, ptr(self.Z), ptr(self.E), ptr(self.ws), self.ws_bytes,
+                 s)
         self.last_forward = object()
         return self.E
 
@@ -103,7 +131,8 @@ class RIKEngine:
         nl, p = self.plan.n_rep, self.plan
         lib.call("gsdft_k_backward", ptr(self.rec), ptr(self.pi), ptr(self.pj), ptr(p.rep_pos),
                  ptr(p.rep_twin), nl, ptr(self.beta), ptr(self.R), ptr(self.KN), self.n_aux,
-                 ptr(self.Linv), ptr(C), self.n_occ, ptr(self.Z), ptr(g_E), ptr(p.order_i),
+                 ptr(self.nodes), self.n_nodes, ptr(self.Linv), ptr(C), self.n_occ,
+                 self.occ_chunk, ptr(self.Z), ptr(g_E), ptr(p.order_i),
                  ptr(p.seg_i), ptr(p.partner_i), ptr(p.order_j), ptr(p.seg_j), ptr(p.partner_j),
                  self.M, ptr(self.sums), ptr(self.g_C), ptr(self.ws), self.ws_bytes, s)
         lib.call("gsdft_k_unit_q", ptr(self.rec), nl, ptr(self.rec_K), s)
@@ -155,13 +184,14 @@ class _ScreenedDFExchange(torch.autograd.Function):
 def df_exchange_energy_screened(splats, C_occ, aux, pi, pj, lam=1e-8, chunk=2048, valid=None,
                                 occ_chunk=16, omega=None):
     """RI-K E_K over the significant bra-pairs (ordered list, 0/1 ``valid``); differentiable in the
-    splat parameters and ``C_occ`` through torch autograd."""
-    if omega is not None:
-        raise NotImplementedError("range-separated (omega) RI-K is not on the B200 path")
+    splat parameters and ``C_occ`` through torch autograd. ``omega``: the long-range exchange
+    E_K[erf(omega r)/r] (attenuated metric and 3-centre integrals). ``occ_chunk``: orbitals per
+    streamed product chunk."""
     from .ri import aux_cholesky
-    L = aux_cholesky(aux, lam)
+    L = aux_cholesky(aux, lam, omega=omega)
     beta, R, KN = aux.quantities()
     n = int(pi.shape[0])
     v = (torch.ones(n, dtype=torch.bool, device=pi.device) if valid is None else valid)
-    eng = RIKEngine(pi, pj, v, splats.n_basis, int(C_occ.shape[1]), beta, R, KN, L)
+    eng = RIKEngine(pi, pj, v, splats.n_basis, int(C_occ.shape[1]), beta, R, KN, L, omega=omega,
+                    occ_chunk=occ_chunk)
     return _ScreenedDFExchange.apply(splats.quat, splats.log_scale, splats.centers, C_occ, eng)

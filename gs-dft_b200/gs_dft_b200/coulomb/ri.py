@@ -29,13 +29,18 @@ def aux_quantities(aux):
     return aux.quantities()
 
 
-def aux_metric(aux) -> torch.Tensor:
-    """V_PQ = (P|Q), exact s-s Coulomb with F0 from erf, (N_aux, N_aux) row-major."""
+def aux_metric(aux, omega=None) -> torch.Tensor:
+    """V_PQ = (P|Q), exact s-s Coulomb with F0 from erf, (N_aux, N_aux) row-major; with ``omega``
+    the long-range (P|erf(omega r)/r|Q) (gs_dft/coulomb/ri.py:267-275)."""
     beta, R, KN = aux.quantities()
     n = int(beta.shape[0])
     V = torch.empty((n, n), dtype=F64, device=beta.device)
-    lib.call("gsdft_aux_metric", ptr(beta), ptr(R.contiguous()), ptr(KN), n, ptr(V),
-             stream_handle(beta.device))
+    if omega:
+        lib.call("gsdft_aux_metric_lr", ptr(beta), ptr(R.contiguous()), ptr(KN), n, float(omega),
+                 ptr(V), stream_handle(beta.device))
+    else:
+        lib.call("gsdft_aux_metric", ptr(beta), ptr(R.contiguous()), ptr(KN), n, ptr(V),
+                 stream_handle(beta.device))
     return V
 
 
@@ -64,9 +69,10 @@ def cholesky_inplace(V: torch.Tensor, lam: float) -> torch.Tensor:
     return V
 
 
-def aux_cholesky(aux, lam: float) -> torch.Tensor:
-    """Lower Cholesky factor of (V + lam I); V is factored in its own buffer."""
-    return cholesky_inplace(aux_metric(aux), lam)
+def aux_cholesky(aux, lam: float, omega=None) -> torch.Tensor:
+    """Lower Cholesky factor of (V + lam I) (the long-range metric with ``omega``); V is factored
+    in its own buffer (gs_dft/coulomb/ri.py:259-264)."""
+    return cholesky_inplace(aux_metric(aux, omega), lam)
 
 
 def _pairs_w(pi, pj, valid):

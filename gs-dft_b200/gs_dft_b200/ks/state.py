@@ -47,6 +47,7 @@ class SplatState:
     _engine: RIJEngine | None = field(default=None, repr=False)
     _ext_engine: RIJEngine | None = field(default=None, repr=False)
     _k_engine: object | None = field(default=None, repr=False)
+    _k_engines_lr: dict = field(default_factory=dict, repr=False)
 
     def engine_for(self, basis, C_occ) -> RIJEngine:
         """The device engine for this state's pairs/aux/factor (built once, reused per step)."""
@@ -58,12 +59,23 @@ class SplatState:
                                      int(C_occ.shape[1]), beta, R.contiguous(), KN, self.cholV)
         return self._engine
 
-    def k_engine_for(self, basis, C_occ):
-        """The device engine of the screened RI-K term on this state's pairs/aux/factor."""
+    def k_engine_for(self, basis, C_occ, omega=None, lam=None):
+        """The device engine of the screened RI-K term on this state's pairs/aux/factor; with
+        ``omega`` the long-range one, whose attenuated metric is factored here (with ``lam``)
+        once per state."""
+        from ..coulomb.exchange import RIKEngine
+        pi, pj, valid = self.pairs
+        beta, R, KN = self.aux.quantities()
+        if omega:
+            eng = self._k_engines_lr.get(float(omega))
+            if eng is None:
+                from ..coulomb.ri import aux_cholesky
+                L = aux_cholesky(self.aux, 1e-8 if lam is None else lam, omega=omega)
+                eng = RIKEngine(pi, pj, valid, basis.n_basis, int(C_occ.shape[1]), beta, R, KN,
+                                L, omega=omega)
+                self._k_engines_lr[float(omega)] = eng
+            return eng
         if self._k_engine is None:
-            from ..coulomb.exchange import RIKEngine
-            pi, pj, valid = self.pairs
-            beta, R, KN = self.aux.quantities()
             self._k_engine = RIKEngine(pi, pj, valid, basis.n_basis, int(C_occ.shape[1]), beta,
                                        R, KN, self.cholV)
         return self._k_engine
@@ -104,7 +116,8 @@ class CoulombKS:
     ``ks(model, state) -> E_J`` (differentiable in the model's splats and C)."""
 
     def __init__(self, *, coulomb: DFSpec | None = None, screen: Pairlist | None = None,
-                 n_devices: int = 1, hf_coeff: float = 0.0):
+                 n_devices: int = 1, hf_coeff: float = 0.0, hf_coeff_lr: float = 0.0,
+                 omega: float = 0.0):
         coulomb = coulomb or DFSpec()
         if not isinstance(coulomb, DFSpec):
             raise TypeError(f"coulomb must come from df(), got {coulomb!r}")
@@ -112,7 +125,8 @@ class CoulombKS:
             raise ValueError("the B200 RI-J path is the screened path: pass screen=pairlist(...)")
         self.screen = screen
         self.coulomb = ScreenedProductDFCoulomb.from_spec(coulomb, skip_pad=screen.skip_pad,
-                                                          hf_coeff=hf_coeff)
+                                                          hf_coeff=hf_coeff,
+                                                          hf_coeff_lr=hf_coeff_lr, omega=omega)
         self.n_devices = int(n_devices)
 
     def initial_pad(self, basis: Splat) -> int:
@@ -131,6 +145,13 @@ class CoulombKS:
         if state is None or state.pairs is None or state.aux is None:
             raise ValueError("coulomb=df() needs the refresh state: see refresh(ks, basis).")
         return self.coulomb.energy(model.basis, model.C, None, model.occupations, state)
+
+    def energy_lr(self, model: SplatModel, state: SplatState):
+        """The unscaled long-range exchange E_K[erf(omega r)/r] (0 unless the builder was given
+        ``hf_coeff_lr != 0``); the total exchange is hf_coeff E_K + hf_coeff_lr E_K^lr."""
+        if state is None or state.pairs is None or state.aux is None:
+            raise ValueError("coulomb=df() needs the refresh state: see refresh(ks, basis).")
+        return self.coulomb.energy_lr(model.basis, model.C, None, model.occupations, state)
 
 
 class ExternalKS:

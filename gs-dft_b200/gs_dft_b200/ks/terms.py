@@ -53,20 +53,37 @@ class ScreenedProductDFCoulomb:
     ``energy(basis, C_orth, P, occ, state) -> (E_J, E_K)`` like the reference
     (gs_dft/ks/terms.py:236-256): E_K from ``df_exchange_energy_screened`` on the same pairs and
     aux (the reference's aux_K is the same product basis, gs_dft/ks/energy.py:468) when
-    ``hf_coeff != 0``, else 0. Range-separated exchange (``energy_lr``) is not on the B200 path.
+    ``hf_coeff != 0``, else 0. ``energy_lr`` is the unscaled long-range exchange
+    E_K[erf(omega r)/r] when ``hf_coeff_lr != 0`` (gs_dft/ks/terms.py:258-265), else 0: the builder
+    adds hf_coeff E_K + hf_coeff_lr E_K^lr.
     """
 
     def __init__(self, hf_coeff: float = 0.0, lam: float = 1e-8, chunk: int = 2048,
-                 scales: tuple = (1.0,), diagonal: bool = True, skip_pad: bool = False):
+                 scales: tuple = (1.0,), diagonal: bool = True, skip_pad: bool = False,
+                 hf_coeff_lr: float = 0.0, omega: float = 0.0):
+        if hf_coeff_lr != 0.0 and not omega > 0.0:
+            raise ValueError("range-separated exchange (hf_coeff_lr != 0) needs omega > 0")
         self.hf_coeff = float(hf_coeff)
+        self.hf_coeff_lr, self.omega = float(hf_coeff_lr), float(omega)
         self.lam, self.chunk = float(lam), int(chunk)
         self.scales, self.diagonal = tuple(scales), bool(diagonal)
         self.skip_pad = bool(skip_pad)
 
     @classmethod
-    def from_spec(cls, spec: DFSpec, skip_pad: bool = False, hf_coeff: float = 0.0):
+    def from_spec(cls, spec: DFSpec, skip_pad: bool = False, hf_coeff: float = 0.0,
+                  hf_coeff_lr: float = 0.0, omega: float = 0.0):
         return cls(hf_coeff=hf_coeff, lam=spec.lam, chunk=spec.chunk, scales=spec.scales,
-                   diagonal=spec.diagonal, skip_pad=skip_pad)
+                   diagonal=spec.diagonal, skip_pad=skip_pad, hf_coeff_lr=hf_coeff_lr,
+                   omega=omega)
+
+    def energy_lr(self, basis, C_orth, P, occ, state):
+        """Unscaled long-range exchange E_K[erf(omega r)/r] on the same pairs and aux, with the
+        attenuated metric's factor (built once per state); 0 without range separation."""
+        if self.hf_coeff_lr == 0.0:
+            return torch.zeros((), dtype=torch.float64, device=basis.centers.device)
+        from ..coulomb.exchange import _ScreenedDFExchange
+        keng = state.k_engine_for(basis, C_orth, omega=self.omega, lam=self.lam)
+        return _ScreenedDFExchange.apply(basis.quat, basis.log_scale, basis.centers, C_orth, keng)
 
     def energy(self, basis, C_orth, P, occ, state):
         from ..coulomb.ri import _ScreenedDFEnergy

@@ -87,7 +87,7 @@ enum {
 
 /* Version of this ABI (entry points, argument meaning, record layouts); gsdft_version() returns it.
  * A host binding checks it at load time so that a library built from older sources is refused. */
-#define GSDFT_ABI_VERSION 3
+#define GSDFT_ABI_VERSION 4
 
 const char* gsdft_last_error_string(void);
 int gsdft_version(void);
@@ -380,23 +380,42 @@ int gsdft_density_pairs(const int32_t* pi, const int32_t* pj, int64_t n, const d
 size_t gsdft_j_vjp_weighted_workspace_size(int64_t n_rep, int64_t n_aux);
 int gsdft_j_vjp_weighted(const double* rec, int64_t n_rep, const double* beta, const double* R,
                          const double* KN, const double* Wt, int64_t ldw, int64_t n_aux,
-                         double* sums, void* ws, size_t ws_bytes, gsdft_stream_t stream);
+                         const double* nodes, int n_nodes, double* sums, void* ws, size_t ws_bytes,
+                         gsdft_stream_t stream);
+
+/* A runtime node rule of the 3-centre kernels (for the weighted reverse pass and RI-K): Gauss-Legendre
+ * on [0, upper] with n_nodes <= 20 nodes (ascending), the rule of the long-range kernel
+ * erf(omega r)/r with upper = omega (_gauss_legendre_segment / _lr_nodes,
+ * gs_dft/integrals/dense.py:56-76, gs_dft/coulomb/ri.py:232-235; the reference uses 12 nodes).
+ * table (GSDFT_NODE_TABLE_DOUBLES doubles, device): t^2 of each node (20 slots), t^4 (20 slots),
+ * then per node 64 entries w_n 2^(j/64). Nodes by Newton's method on P_n in FP64. Node screening
+ * does not apply to a runtime rule (its weights are not monotone). */
+#define GSDFT_NODE_TABLE_DOUBLES 1320
+int gsdft_lr_node_table(double upper, int n_nodes, double* table, gsdft_stream_t stream);
+
+/* The long-range aux metric (P|erf(omega r)/r|Q): F0(T) -> sqrt(z) F0(z T), z = omega^2 /
+ * (omega^2 + rho) (coulomb_block with omega, gs_dft/coulomb/ri.py:63-101,267-275). omega > 0. */
+int gsdft_aux_metric_lr(const double* beta, const double* R, const double* KN, int64_t n_aux,
+                        double omega, double* V, gsdft_stream_t stream);
 
 /* Screened RI-K over the pair representatives: D[P,o,o'] = sum_{live (i,k)} (P|ik) C_io C_ko',
  * E_K = -tr((V + lam I)^-1 D D^T) = -|L^-1 D|^2 (replaces _exchange_M_streamed_screened and
- * df_exchange_energy_screened, gs_dft/coulomb/ri.py:497-544, for omega = None). The pair list must
- * be an ordered 0/1 list (the reference masks with valid & occupied); a merged transposed twin adds
- * C_ko C_io'. Linv is the packed inverse factor of gsdft_j_solve_inverse (its lower triangle L^-1 is
- * read). Writes Z = L^-1 D (n_aux x n_occ^2, row-major; kept for the backward) and E (device
- * scalar). The contractions are the library's DMMA GEMMs. The workspace (gsdft_k_workspace_size:
- * 8 n_rep (n_aux + 2 n_occ^2) bytes and more) holds the integral block and the products between
- * forward and backward: pass the same, untouched workspace to gsdft_k_backward. */
-size_t gsdft_k_workspace_size(int64_t n_rep, int64_t n_aux, int64_t n_occ);
+ * df_exchange_energy_screened, gs_dft/coulomb/ri.py:497-544). The pair list must be an ordered 0/1
+ * list (the reference masks with valid & occupied); a merged transposed twin adds C_ko C_io'. Linv is
+ * the packed inverse factor of gsdft_j_solve_inverse (its lower triangle L^-1 is read). nodes NULL:
+ * the 1/r kernel; a gsdft_lr_node_table rule (with the factor of gsdft_aux_metric_lr's metric): the
+ * long-range exchange E_K[erf(omega r)/r]. The orbital products are streamed in chunks of occ_chunk
+ * orbitals (0 = all at once; the reference's occ_chunk): the workspace (gsdft_k_workspace_size)
+ * holds the integral block (8 n_rep n_aux bytes), one chunk of products (8 n_rep occ_chunk n_occ
+ * bytes), n_aux x n_occ^2 doubles and a chunk of D with its split partials. Writes Z = L^-1 D
+ * (n_aux x n_occ^2, row-major; kept for the backward) and E (device scalar). The contractions are
+ * the library's DMMA GEMMs. Pass the same, untouched workspace to gsdft_k_backward. */
+size_t gsdft_k_workspace_size(int64_t n_rep, int64_t n_aux, int64_t n_occ, int64_t occ_chunk);
 int gsdft_k_forward(const double* rec, const int32_t* pi, const int32_t* pj, const int32_t* rep_pos,
                     const int32_t* rep_twin, int64_t n_rep, const double* beta, const double* R,
-                    const double* KN, int64_t n_aux, const double* Linv, const double* C_occ,
-                    int64_t n_occ, double* Z, double* E, void* ws, size_t ws_bytes,
-                    gsdft_stream_t stream);
+                    const double* KN, int64_t n_aux, const double* nodes, int n_nodes,
+                    const double* Linv, const double* C_occ, int64_t n_occ, int64_t occ_chunk,
+                    double* Z, double* E, void* ws, size_t ws_bytes, gsdft_stream_t stream);
 /* Gradient of g_E * E_K (g_E a device scalar, NULL = 1): the reverse-pass sums (for gsdft_pair_chain
  * with gsdft_k_unit_q records) and g_C (M x n_occ, written). Groupings and partners from
  * gsdft_pair_groups. Overwrites the workspace's integral block: a second backward needs the forward
@@ -404,7 +423,8 @@ int gsdft_k_forward(const double* rec, const int32_t* pi, const int32_t* pj, con
 int gsdft_k_backward(const double* rec, const int32_t* pi, const int32_t* pj,
                      const int32_t* rep_pos, const int32_t* rep_twin, int64_t n_rep,
                      const double* beta, const double* R, const double* KN, int64_t n_aux,
-                     const double* Linv, const double* C_occ, int64_t n_occ, const double* Z,
+                     const double* nodes, int n_nodes, const double* Linv, const double* C_occ,
+                     int64_t n_occ, int64_t occ_chunk, const double* Z,
                      const double* g_E, const int32_t* order_i, const int64_t* seg_i,
                      const int32_t* partner_i, const int32_t* order_j, const int64_t* seg_j,
                      const int32_t* partner_j, int64_t M, double* sums, double* g_C, void* ws,

@@ -49,6 +49,19 @@ def gauss_legendre_halfline(n_quad: int = 20):
 
 QUAD_T, QUAD_W = gauss_legendre_halfline(20)
 
+
+def gauss_legendre_segment(upper: float, n_quad: int = 12):
+    """Gauss-Legendre on [0, upper]: the node table of the erf(omega r)/r kernel, the same node
+    integral taken to omega instead of infinity (gs_dft/integrals/dense.py:56-76)."""
+    x, w = np.polynomial.legendre.leggauss(n_quad)
+    return 0.5 * float(upper) * (x + 1.0), 0.5 * float(upper) * w
+
+
+def _node_table(omega):
+    """(t, w) of the 3-centre kernel: the half-line rule, or the 12-node segment rule on
+    [0, omega] for the long-range kernel (gs_dft/coulomb/ri.py:149,232-235)."""
+    return (QUAD_T, QUAD_W) if not omega else gauss_legendre_segment(omega, 12)
+
 # ----------------------------------------------------------------------------------------------
 #  Splat chart  (gs_dft/basis/spectral.py:33-40, 71-82)
 # ----------------------------------------------------------------------------------------------
@@ -289,8 +302,9 @@ def boys0(T):
     return np.where(small, ser, big)
 
 
-def coulomb_block(g1, P1, KN1, g2, P2, KN2):
-    """(1|2) = KN1 KN2 2 pi^2.5/(g1 g2 sqrt(g1+g2)) F0(g1g2/(g1+g2) |P1-P2|^2)
+def coulomb_block(g1, P1, KN1, g2, P2, KN2, omega=None):
+    """(1|2) = KN1 KN2 2 pi^2.5/(g1 g2 sqrt(g1+g2)) F0(g1g2/(g1+g2) |P1-P2|^2); with ``omega`` the
+    long-range erf(omega r)/r kernel, F0(T) -> sqrt(z) F0(z T), z = omega^2/(omega^2 + rho)
     (gs_dft/coulomb/ri.py:63-76)."""
     gab = g1[:, None] * g2[None, :]
     gsum = g1[:, None] + g2[None, :]
@@ -298,13 +312,18 @@ def coulomb_block(g1, P1, KN1, g2, P2, KN2):
     PQ2 = dx[..., 0] ** 2 + dx[..., 1] ** 2 + dx[..., 2] ** 2
     rho = gab / gsum
     T = rho * PQ2
-    coul = 2.0 * PI ** 2.5 / (gab * np.sqrt(gsum)) * boys0(T)
+    if omega:
+        z = omega ** 2 / (omega ** 2 + rho)
+        F0 = np.sqrt(z) * boys0(z * T)
+    else:
+        F0 = boys0(T)
+    coul = 2.0 * PI ** 2.5 / (gab * np.sqrt(gsum)) * F0
     return (KN1[:, None] * KN2[None, :]) * coul
 
 
-def aux_metric(beta, R, KN):
-    """V_PQ = (P|Q) (gs_dft/coulomb/ri.py:267-275)."""
-    return coulomb_block(beta, R, KN, beta, R, KN)
+def aux_metric(beta, R, KN, omega=None):
+    """V_PQ = (P|Q), or the long-range (P|erf(omega r)/r|Q) (gs_dft/coulomb/ri.py:267-275)."""
+    return coulomb_block(beta, R, KN, beta, R, KN, omega)
 
 
 def aux_cholesky(V, lam):
@@ -327,13 +346,14 @@ def df_coulomb_solve(gamma, L):
 PREF = 2.0 * PI ** 3 / math.sqrt(PI)
 
 
-def isobra_nodes(beta, dp2, Lam):
+def isobra_nodes(beta, dp2, Lam, nodes=None):
     """sum_t w_t (G0G1G2)^-1/2 exp(-t^2 sum_k W_k/G_k) in the division-lean form
-    (gs_dft/coulomb/ri.py:167-185). beta (A,), dp2 (A,B,3), Lam (B,3) -> (A,B)."""
+    (gs_dft/coulomb/ri.py:167-185). beta (A,), dp2 (A,B,3), Lam (B,3) -> (A,B). ``nodes`` = (t, w)
+    (default the half-line rule)."""
     b = beta[:, None]
     L0, L1, L2 = Lam[None, :, 0], Lam[None, :, 1], Lam[None, :, 2]
     coul = np.zeros((beta.shape[0], Lam.shape[0]))
-    for t, w in zip(QUAD_T, QUAD_W):
+    for t, w in zip(*(nodes or (QUAD_T, QUAD_W))):
         t2 = t * t
         G0 = b * L0 + t2 * (b + L0)
         G1 = b * L1 + t2 * (b + L1)
@@ -373,13 +393,14 @@ def isobra_nodes_bwd(beta, dp2, Lam, gI):
     return d_beta[:, 0], np.stack(d_dp2, -1), np.stack([dL[0] for dL in d_Lam], -1)
 
 
-def full_isobra_block(beta, R, KN_aux, A_pair, P_pair, KN_pair):
+def full_isobra_block(beta, R, KN_aux, A_pair, P_pair, KN_pair, omega=None):
     """(P|a): eigh of A_hat, dp2 = (U^T (R - P))^2, node sum, prefactor
-    (gs_dft/coulomb/ri.py:126-151). Returns (N_aux, n_pair)."""
+    (gs_dft/coulomb/ri.py:126-151); ``omega``: the long-range kernel's segment rule. Returns
+    (N_aux, n_pair)."""
     Lam, U = np.linalg.eigh(A_pair)
     d = R[:, None, :] - P_pair[None, :, :]
     dp2 = np.einsum("bki,abk->abi", U, d) ** 2
-    coul = isobra_nodes(beta, dp2, Lam)
+    coul = isobra_nodes(beta, dp2, Lam, _node_table(omega))
     return (KN_aux[:, None] * KN_pair[None, :]) * PREF * coul
 
 # ----------------------------------------------------------------------------------------------
@@ -419,7 +440,7 @@ def energy(sys_arrays, aux_q, L, pi, pj, valid, chunk=2048):
 # ----------------------------------------------------------------------------------------------
 
 
-def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa, W=None):
+def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa, W=None, omega=None):
     """For each pair: J_a = sum_P (P|a) d_P and the cotangents of (A_hat, P_a, KN_a) of
     E = sum_P d_P sum_a (P|a) q_a, without the 1/(lambda_i - lambda_j) terms of an eigh VJP.
     With ``W`` (N_aux, B) the cotangents are those of E = sum_{P,a} W[P,a] (P|a) instead
@@ -437,7 +458,7 @@ def _pair_vjp_integral(beta, R, KN_aux, dvec, A_pair, P_pair, KN_pair, qa, W=Non
     Dk = np.zeros(y.shape)                                    # sum_t f s / G_k
     Zkl = np.zeros(y.shape + (3,))                            # sum_t f t^4 beta^2 z_k z_l
     Vk = np.zeros(y.shape)                                    # sum_t f t^2 beta lam_k z_k
-    for t, w in zip(QUAD_T, QUAD_W):
+    for t, w in zip(*_node_table(omega)):
         t2 = t * t
         s = b + t2
         G = b[..., None] * Lam[None] + t2 * (b[..., None] + Lam[None])   # (A,B,3)
@@ -762,9 +783,10 @@ def screened_coulomb_exact_and_grad(sys_arrays, pi, pj, valid, bra_chunk=64, blo
 # ----------------------------------------------------------------------------------------------
 
 
-def _exchange_D(q_splat, C, aux_q, pi, pj, valid, chunk=1024):
+def _exchange_D(q_splat, C, aux_q, pi, pj, valid, chunk=1024, omega=None):
     """D[P,o,o'] = sum_{live (i,k)} (P|ik) C_io C_ko' over the listed pairs (``valid`` a 0/1 mask,
-    as the reference's ``cv & ov`` requires) (gs_dft/coulomb/ri.py:496-526)."""
+    as the reference's ``cv & ov`` requires) (gs_dft/coulomb/ri.py:496-526); ``omega``: the
+    long-range integrals."""
     beta, R, KN = aux_q
     n = pi.shape[0]
     live_all = np.ones(n, bool) if valid is None else (np.asarray(valid) != 0)
@@ -775,33 +797,34 @@ def _exchange_D(q_splat, C, aux_q, pi, pj, valid, chunk=1024):
         if not np.any(live):
             continue
         ci, cj = pi[sl][live], pj[sl][live]
-        blk = full_isobra_block(beta, R, KN, *full_pair_quantities(q_splat, ci, cj))
+        blk = full_isobra_block(beta, R, KN, *full_pair_quantities(q_splat, ci, cj), omega=omega)
         D += np.einsum("Ap,po,pq->Aoq", blk, C[ci], C[cj])
     return D
 
 
-def exchange_energy_screened(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024):
+def exchange_energy_screened(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024, omega=None):
     """E_K = -tr((V + lam I)^-1 M), M_PQ = sum_{o,o'} D[P,o,o'] D[Q,o,o']
     (gs_dft/coulomb/ri.py:529-544; ``sys_arrays`` = (quat, log_scale, centers, C_occ, occ), occ
-    unused as in the reference). Returns (E_K, D)."""
+    unused as in the reference); ``omega``: the long-range exchange E_K[erf(omega r)/r] (metric
+    and 3-centre integrals both attenuated). Returns (E_K, D)."""
     quat, log_scale, centers, C = sys_arrays[:4]
     q = full_quantities(quat, log_scale, centers)
-    D = _exchange_D(q, C, aux_q, pi, pj, valid, chunk)
-    Vs = aux_metric(*aux_q)
+    D = _exchange_D(q, C, aux_q, pi, pj, valid, chunk, omega)
+    Vs = aux_metric(*aux_q, omega=omega)
     Vs[np.diag_indices_from(Vs)] += lam
     Mm = np.einsum("Aoq,Boq->AB", D, D)
     return -float(np.trace(np.linalg.solve(Vs, Mm))), D
 
 
-def exchange_energy_and_grad(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024):
+def exchange_energy_and_grad(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024, omega=None):
     """E_K and its gradient with respect to (quat, log_scale, centers, C_occ), aux and pairs frozen.
     With Y = (V + lam I)^-1 D: dE/dD = -2 Y, dE/d(P|a) = -2 C_i^T Y_P C_k, and dE/dC from D's
     bilinear dependence on C_i, C_k."""
     quat, log_scale, centers, C = sys_arrays[:4]
     qs = full_quantities(quat, log_scale, centers)
-    E, D = exchange_energy_screened(sys_arrays, aux_q, lam, pi, pj, valid, chunk)
+    E, D = exchange_energy_screened(sys_arrays, aux_q, lam, pi, pj, valid, chunk, omega)
     beta, R, KN_aux = aux_q
-    Vs = aux_metric(*aux_q)
+    Vs = aux_metric(*aux_q, omega=omega)
     Vs[np.diag_indices_from(Vs)] += lam
     nA, no = D.shape[0], D.shape[1]
     Ybar = -2.0 * np.linalg.solve(Vs, D.reshape(nA, no * no)).reshape(nA, no, no)
@@ -817,9 +840,10 @@ def exchange_energy_and_grad(sys_arrays, aux_q, lam, pi, pj, valid, chunk=1024):
             continue
         ci, cj = pi[sl][live], pj[sl][live]
         Ah, Pa, KNa = full_pair_quantities(qs, ci, cj)
-        blk = full_isobra_block(beta, R, KN_aux, Ah, Pa, KNa)               # (N_aux, c)
+        blk = full_isobra_block(beta, R, KN_aux, Ah, Pa, KNa, omega=omega)  # (N_aux, c)
         W = np.einsum("po,Aoq,pq->Ap", C[ci], Ybar, C[cj])                  # dE/d(P|a)
-        _, Abar, Pbar, KNbar = _pair_vjp_integral(beta, R, KN_aux, None, Ah, Pa, KNa, None, W=W)
+        _, Abar, Pbar, KNbar = _pair_vjp_integral(beta, R, KN_aux, None, Ah, Pa, KNa, None, W=W,
+                                                  omega=omega)
         _scatter_pair_grads(qs, ci, cj, np.ones(ci.shape[0]), np.zeros(ci.shape[0]), Abar, Pbar,
                             KNbar, C, np.zeros(C.shape[1]), gA, gmu, gN, gC)
         T = np.einsum("Ap,Aoq->poq", blk, Ybar)                             # dE/dX[a,o,o']

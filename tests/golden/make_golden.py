@@ -36,8 +36,11 @@ Outputs (compressed .npz, a few hundred KB in all):
     over the fused 32-node block (``full_eri_block_fused``), and that sum's value on rand24's
     padded ordered list.
 
-``python tests/golden/make_golden.py vne`` (or ``k``, ``exact``, ``exact_grad``) regenerates only
-that file.
+  * ``ref_k_lr.npz``    — the long-range (range-separated) RI-K E_K[erf(omega r)/r], omega = 0.3,
+    on the same lists, and its gradient by Richardson central differences on the 10-splat system.
+
+``python tests/golden/make_golden.py vne`` (or ``k``, ``k_lr``, ``exact``, ``exact_grad``)
+regenerates only that file.
 """
 from __future__ import annotations
 
@@ -255,6 +258,53 @@ def make_k(eps=1e-7, lam=1e-8):
     print("k grad: M=10 E_K=", out["grad_E_K"])
 
 
+def make_k_lr(eps=1e-7, lam=1e-8, omega=0.3):
+    """The long-range exchange E_K[erf(omega r)/r] (``df_exchange_energy_screened(..., omega)``) on
+    the padded ordered list of the three systems, and its gradient by Richardson central
+    differences of the executed reference on the 10-splat system."""
+    spec, iso, pairs, ri = _modules()
+    out = {"omega": omega, "lam": lam, "eps": eps}
+    for name, s in _cases().items():
+        sp = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+        pi, pj, _ = pairs.neighbor_pairs(sp, eps=eps)
+        n = int(pi.shape[0])
+        pi2, pj2, v2 = pairs.neighbor_pairs(sp, eps=eps, pad_to=n + 37)
+        aux = iso.init_product_aux(sp)
+        out[f"{name}_E_K_lr"] = float(ri.df_exchange_energy_screened(
+            sp, J(s.C_occ), aux, pi2, pj2, lam=lam, chunk=512, valid=v2, omega=omega))
+        print(f"k lr {name}: E_K={out[f'{name}_E_K_lr']:.15g}", flush=True)
+
+    s = small_random_system(10, 3, seed=3, spread=1.0, n_atoms=3)
+    sp0 = spec.Splat(quat=J(s.quat), log_scale=J(s.log_scale), centers=J(s.centers))
+    pi, pj, v = pairs.neighbor_pairs(sp0, eps=eps)
+    aux = iso.init_product_aux(sp0)
+
+    def energy(quat, ls, cen, C):
+        sp = spec.Splat(quat=J(quat), log_scale=J(ls), centers=J(cen))
+        return float(ri.df_exchange_energy_screened(sp, J(C), aux, pi, pj, lam=lam, chunk=64,
+                                                    valid=v, omega=omega))
+
+    x0 = [s.quat.copy(), s.log_scale.copy(), s.centers.copy(), s.C_occ.copy()]
+
+    def fd(k, h):
+        g = np.zeros_like(x0[k])
+        for idx in np.ndindex(x0[k].shape):
+            xp = [a.copy() for a in x0]
+            xm = [a.copy() for a in x0]
+            xp[k][idx] += h
+            xm[k][idx] -= h
+            g[idx] = (energy(*xp) - energy(*xm)) / (2 * h)
+        return g
+
+    out.update(grad_quat=s.quat, grad_log_scale=s.log_scale, grad_centers=s.centers,
+               grad_C_occ=s.C_occ, grad_E_K=energy(*x0))
+    for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
+        h = 1e-3
+        out["grad_" + name] = (4 * fd(k, h / 2) - fd(k, h)) / 3      # Richardson, O(h^4)
+    np.savez_compressed(os.path.join(HERE, "ref_k_lr.npz"), **out)
+    print("k lr grad: M=10 E_K=", out["grad_E_K"])
+
+
 def make_exact(eps=1e-7):
     spec, _, pairs, _ = _modules()
     cs = jaxshim.load("gs_dft.coulomb.stream")
@@ -347,11 +397,15 @@ if __name__ == "__main__":
     if sys.argv[1:] == ["exact_grad"]:
         make_exact_grad()
         sys.exit(0)
+    if sys.argv[1:] == ["k_lr"]:
+        make_k_lr()
+        sys.exit(0)
     for name, s in _cases().items():
         make_case(name, s)
     make_grad()
     make_nodes_bwd()
     make_vne()
     make_k()
+    make_k_lr()
     make_exact()
     make_exact_grad()
