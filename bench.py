@@ -370,10 +370,11 @@ def main():
         # rows beyond the metric, measured after it; a failure here is recorded, never fatal
         next_rows = {}
         for name, fn in (("vne", measure_vne), ("k", measure_k), ("exact_j", measure_exact)):
-            if name != "vne" and args.config > 1:
+            if name != "vne" and args.config > 2:
                 next_rows[name] = {"skipped": (
-                    "RI-K keeps the whole list's integral block (rejected above 64 GiB)" if name == "k"
-                    else "O(n_rep^2): ~25 min at this size") + "; measured at configuration 1"}
+                    "RI-K keeps the whole list's integral block, 8 n_rep n_aux bytes (1.0 TB here)"
+                    if name == "k" else "O(n_rep^2): ~25 min at this size")
+                    + "; measured at configurations 1 and 2"}
                 continue
             try:
                 next_rows[name] = fn(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C,
@@ -513,10 +514,11 @@ def measure_k(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flu
     gradient per step (RIKEngine.step), device-timed with CUDA events, L2 flushed between steps."""
     beta, R, KN = aux.quantities()
     eng = g.RIKEngine(pi, pj, valid, sy.M, sy.n_occ, beta, R, KN, L)
-    for _ in range(2):
+    big = args.config >= 2            # seconds per step: one warm-up, one timed step
+    for _ in range(1 if big else 2):
         eng.step(quat, log_scale, centers, C)
     torch.cuda.synchronize()
-    K = max(3, min(args.steps, 10))
+    K = 1 if big else max(3, min(args.steps, 10))
     total = 0.0
     for k in range(K):
         flush.fill_(float(k))
@@ -536,7 +538,7 @@ def measure_k(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ, flu
                     "block, orbital products and their inverse-factor products as DMMA GEMMs, "
                     "weighted reverse pass, chain), not part of the metric",
             "ms_per_step": ms, "steps_timed": K, "evaluated_pairs": n_rep, "n_aux": n_aux,
-            "n_occ": sy.n_occ, "integrals_per_s": integrals / (ms * 1e-3),
+            "n_occ": sy.n_occ, "occ_chunk": eng.occ_chunk, "integrals_per_s": integrals / (ms * 1e-3),
             "flop_per_step": flop, "achieved_tflops": flop / (ms * 1e-3) / 1e12,
             "frac_of_measured_fp64_peak": flop / (ms * 1e-3) / peak,
             "E_K": float(eng.E[0]), "workspace_bytes": eng.ws_bytes}
@@ -560,7 +562,7 @@ def measure_exact(torch, g, sy, pi, pj, valid, quat, log_scale, centers, C, occ,
     def timed(grad):
         run(grad)
         torch.cuda.synchronize()
-        total, K = 0.0, 2
+        total, K = 0.0, (1 if args.config >= 2 else 2)
         for k in range(K):
             flush.fill_(float(k))
             a = torch.cuda.Event(enable_timing=True)

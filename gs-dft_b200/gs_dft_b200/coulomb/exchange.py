@@ -29,7 +29,7 @@ from .engine import check_step_inputs, make_plan
 
 F64 = torch.float64
 MAX_WORKSPACE_BYTES = 64 << 30
-CHUNK_BYTES = 2 << 30        # the orbital-product chunk chosen when occ_chunk is None
+CHUNK_BYTES = 8 << 30        # the orbital-product chunk chosen when occ_chunk is None
 LR_NODES = 12                # nodes of the long-range segment rule (gs_dft/coulomb/ri.py:232)
 
 
