@@ -35,45 +35,68 @@ __device__ __forceinline__ double abs_overlap(const double* __restrict__ A9,
   return fabs(__ddiv_rn(DM(KN, kPi15), __dsqrt_rn(det)));
 }
 
-// Per-row count of significant columns (j >= i when unique).
+constexpr int kRowWarps = kRowThreads / 32;
+
+// Per-row count of significant columns (j >= i when unique): per warp the population count of
+// its significance ballots, then the warps' counts added in warp order.
 __global__ void pairs_count_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
                                    const double* __restrict__ N, int M, double eps, int unique,
                                    int64_t* __restrict__ row_count) {
-  int i = blockIdx.x;
-  int j0 = unique ? i : 0;
-  int cnt = 0;
-  for (int j = j0 + threadIdx.x; j < M; j += blockDim.x)
-    cnt += abs_overlap(A9, mu, N, i, j) > eps ? 1 : 0;
-  typedef cub::BlockReduce<int, kRowThreads> BR;
-  __shared__ typename BR::TempStorage tmp;
-  int tot = BR(tmp).Sum(cnt);
-  if (threadIdx.x == 0) row_count[i] = tot;
+  __shared__ int s_warp[kRowWarps];
+  const int i = blockIdx.x;
+  const int j0 = unique ? i : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int cnt = 0;  // warp-uniform
+  for (int jb = j0; jb < M; jb += kRowThreads) {
+    const int j = jb + threadIdx.x;
+    const bool sig = j < M && abs_overlap(A9, mu, N, i, j) > eps;
+    cnt += __popc(__ballot_sync(0xffffffffu, sig));
+  }
+  if (lane == 0) s_warp[warp] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t tot = 0;
+    for (int w = 0; w < kRowWarps; ++w) tot += s_warp[w];
+    row_count[i] = tot;
+  }
 }
 
-// Ordered write of row i's significant columns at row_off[i]. Direct mode writes (pi,pj,w);
-// ranking mode writes (flat index, |S|) for the overflow selection.
+// Ordered write of row i's significant columns at row_off[i]: a warp-ballot + prefix-scan
+// compaction. Per chunk of kRowThreads columns, each warp's ballot of the significance flags gives
+// a lane its rank inside the warp (popc of the lower lanes' bits) and the warp its count; an
+// exclusive scan of the kRowWarps counts in shared memory gives each warp's offset, so the columns
+// land in ascending j. Direct mode writes (pi,pj,w); ranking mode writes (flat index, |S|) for the
+// overflow selection.
 __global__ void pairs_build_kernel(const double* __restrict__ A9, const double* __restrict__ mu,
                                    const double* __restrict__ N, int M, double eps, int unique,
                                    const int64_t* __restrict__ row_off, int ranking,
                                    int32_t* __restrict__ pi, int32_t* __restrict__ pj,
                                    double* __restrict__ w, int64_t* __restrict__ flat,
                                    double* __restrict__ val) {
-  int i = blockIdx.x;
-  int j0 = unique ? i : 0;
-  typedef cub::BlockScan<int, kRowThreads> BS;
-  __shared__ typename BS::TempStorage tmp;
-  __shared__ int s_total;
+  __shared__ int s_warp[kRowWarps];
+  const int i = blockIdx.x;
+  const int j0 = unique ? i : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned lower = (1u << lane) - 1u;
   int64_t base = row_off[i];
   for (int jb = j0; jb < M; jb += kRowThreads) {
-    int j = jb + threadIdx.x;
+    const int j = jb + threadIdx.x;
     double s = 0.0;
     int sig = 0;
     if (j < M) {
       s = abs_overlap(A9, mu, N, i, j);
       sig = s > eps ? 1 : 0;
     }
-    int rank, total;
-    BS(tmp).ExclusiveSum(sig, rank, total);
+    const unsigned ballot = __ballot_sync(0xffffffffu, sig);
+    if (lane == 0) s_warp[warp] = __popc(ballot);
+    __syncthreads();
+    int offset = 0, total = 0;
+    for (int w2 = 0; w2 < kRowWarps; ++w2) {
+      const int c = s_warp[w2];
+      offset += w2 < warp ? c : 0;
+      total += c;
+    }
+    const int rank = offset + __popc(ballot & lower);
     if (sig) {
       int64_t pos = base + rank;
       if (ranking) {
@@ -85,10 +108,8 @@ __global__ void pairs_build_kernel(const double* __restrict__ A9, const double* 
         w[pos] = unique ? (i == j ? 1.0 : 2.0) : 1.0;
       }
     }
-    if (threadIdx.x == 0) s_total = total;
-    __syncthreads();
-    base += s_total;
-    __syncthreads();
+    base += total;
+    __syncthreads();  // every warp has read s_warp before the next chunk overwrites it
   }
 }
 

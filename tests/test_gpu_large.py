@@ -244,3 +244,34 @@ def test_cost_balanced_rank_slices(g):
         assert prev == one.plan.n_rep_total
         assert max(rank_cost) / min(rank_cost) < 1.02
         close(total, gam, rtol=1e-12, atol_rel=1e-14)
+
+
+def test_sharded_step_sums_to_one_device_with_row_blocks(g):
+    """Configuration 2 (n_occ = 320: q and g_C on the row-block tiles) split over 2 ranks by
+    estimated cost, emulated in one process: the partial gammas summed, each rank's solve and
+    reverse pass on its slice, and the partial splat cotangents and g_C summed equal the one-device
+    step (each rank builds its row blocks over its own representatives only)."""
+    sy, s, pi, pj, v, aux, L = system(g, 2)
+    beta, R, KN = aux.quantities()
+    w = torch.ones(int(pi.shape[0]), dtype=torch.float64, device="cuda")
+    C, occ = dev(sy.C_occ), dev(sy.occ)
+    one = g.RIJEngine(pi, pj, w, sy.M, sy.n_occ, beta, R.contiguous(), KN, L)
+    assert one.blocks is not None
+    ref = {k: host(t).copy() for k, t in one.step(s.quat, s.log_scale, s.centers, C, occ).items()}
+    del one
+    ranks = [g.RIJEngine(pi, pj, w, sy.M, sy.n_occ, beta, R.contiguous(), KN, L, rank=r, world=2,
+                         balance=(s.quat, s.log_scale, s.centers)) for r in range(2)]
+    gam = sum(e.forward_local(s.quat, s.log_scale, s.centers, C, occ).clone() for e in ranks)
+    parts = {"gA6": 0.0, "gmu": 0.0, "gN": 0.0, "g_C": 0.0}
+    for e in ranks:
+        assert e.blocks is not None
+        e.gamma.copy_(gam)
+        e.solve()
+        gA6, gmu, gN, gC = e.backward_local(s.centers, C, occ)
+        for k, t in (("gA6", gA6), ("gmu", gmu), ("gN", gN), ("g_C", gC[:, :sy.n_occ])):
+            parts[k] = parts[k] + host(t)
+    close(float(ranks[0].E[0]), ref["E"][0], rtol=1e-12)
+    close(parts["g_C"], ref["g_C"], rtol=1e-10, atol_rel=1e-12)
+    close(parts["gmu"], ref["g_centers"], rtol=1e-10, atol_rel=1e-12)
+    close(parts["gA6"], ref["gA6"], rtol=1e-10, atol_rel=1e-12)
+    close(parts["gN"], ref["gN"], rtol=1e-10, atol_rel=1e-12)
