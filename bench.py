@@ -441,6 +441,13 @@ def main():
                    "execution": ("step replayed from CUDA graphs: one graph on 1 GPU; on N GPUs the "
                                  "compute segments between the two NCCL allreduces, which run eagerly")},
         "refresh_s": refresh_s,
+        # the refresh (pair list, aux, metric, factor, plan, inverse) amortised over the trainer's
+        # default refresh interval of 10 steps (conf/config.yaml:22 of the reference)
+        "refresh_amortized": {
+            "refresh_every_steps": 10,
+            "s_per_step": ms_per_step * 1e-3 + refresh_s / 10,
+            "value": n_aux * n_live / (ms_per_step * 1e-3 + refresh_s / 10) / 1e9,
+            "unit": UNIT},
         "kernel_ms": {"j_forward": t_fwd, "j_vjp": t_vjp},
         "roofline": {"bound": "fp64", "kernel": dom, "achieved": achieved / 1e12,
                      "peak": peak / 1e12, "unit": "TFLOP/s", "frac": achieved / peak,
