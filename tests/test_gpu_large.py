@@ -95,6 +95,25 @@ def test_pair_list_bit_exact_large(g, cfg):
         assert not host(ppi[n_sig:]).any() and not host(pv[n_sig:]).any()
 
 
+def test_pair_list_bit_exact_north_star(g):
+    """Configuration 4 ((H2O)914, M = 53,000: 2.8e9 candidates, the north-star system): the whole
+    significant list of the GPU bit-exact against the oracle's C sweep, and its count equal to
+    BASELINE.md's 36,896,926. Pairs only (no aux or factor: the metric alone is 22.5 GB)."""
+    from gs_dft_b200.systems import make_config
+    _SYSTEMS.clear()
+    torch.cuda.empty_cache()
+    sy = make_config(4)
+    s = g.Splat(dev(sy.quat), dev(sy.log_scale), dev(sy.centers))
+    pi, pj, v = g.neighbor_pairs(s, eps=sy.eps)
+    q = O.full_quantities(sy.quat, sy.log_scale, sy.centers)
+    opi, opj, ov, n_sig, n_guard = O.neighbor_pairs_c(q, sy.eps)
+    assert n_guard == 0, f"{n_guard} candidates within 1e-12 of eps"
+    assert n_sig == 36_896_926 and int(pi.shape[0]) == n_sig
+    np.testing.assert_array_equal(host(pi), opi)
+    np.testing.assert_array_equal(host(pj), opj)
+    np.testing.assert_array_equal(host(v), ov)
+
+
 def _subset(n, k, seed):
     rng = np.random.default_rng(seed)
     return np.sort(rng.choice(n, size=min(k, n), replace=False))
