@@ -148,10 +148,186 @@ __global__ void __launch_bounds__(128) dmma_gemm_kernel(GemmArgs g) {
       }
 }
 
-// Host launcher: picks the instantiation; grid (N tiles, M tiles, batch).
+// ------------------------------------------------------------------------------------------------
+// The same GEMM for large, 16-byte-aligned operands: a 128 x 64 tile of C per block of 256 threads
+// (eight warps of 32 x 32, 2 x 4 DMMA tiles each), the operand tiles of three K stages of 16 in
+// flight at once through cp.async (16-byte copies straight into shared memory, no register
+// staging), one barrier per stage. A copy's source size zero-fills what lies beyond the matrix edge
+// or above a triangular operand's diagonal, so edges and triangles need no second path.
+// ------------------------------------------------------------------------------------------------
+#ifndef GSDFT_GEMM_V2
+#define GSDFT_GEMM_V2 1
+#endif
+constexpr int kBM = 128, kBN = 64, kBK = 16, kStages = 3, kV2Threads = 256;
+
+template <bool kTA>
+__host__ __device__ constexpr int v2_a_cols() { return (kTA ? kBM : kBK) + 4; }
+template <bool kTA>
+__host__ __device__ constexpr int v2_a_size() { return (kTA ? kBK : kBM) * v2_a_cols<kTA>(); }
+template <bool kTB>
+__host__ __device__ constexpr int v2_b_cols() { return (kTB ? kBK : kBN) + 4; }
+template <bool kTB>
+__host__ __device__ constexpr int v2_b_size() { return (kTB ? kBN : kBK) * v2_b_cols<kTB>(); }
+template <bool kTA, bool kTB>
+__host__ __device__ constexpr size_t v2_smem() {
+  return sizeof(double) * kStages * (v2_a_size<kTA>() + v2_b_size<kTB>());
+}
+
+__device__ __forceinline__ void cp_async16(double* dst, const double* src, int bytes) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// One 16-byte chunk (two doubles from (gr, gc) on) of a stored operand with rows x cols elements:
+// how many of its doubles exist (0, 1, 2), after the edge and, for a lower-triangular operand, the
+// diagonal (entries with column > row read as zero).
+template <bool kTri>
+__device__ __forceinline__ int chunk_doubles(int64_t gr, int64_t gc, int64_t rows, int64_t cols) {
+  if (gr >= rows) return 0;
+  int64_t v = imin64(2, imax64(0, cols - gc));
+  if (kTri) v = imin64(v, imax64(0, gr - gc + 1));
+  return (int)v;
+}
+
+template <bool kTA, bool kTB, bool kTriA, bool kTriB, bool kLower>
+__global__ void __launch_bounds__(kV2Threads) dmma_gemm_v2_kernel(GemmArgs g) {
+  const int64_t z = blockIdx.z;
+  const int64_t M = imin64(g.M, g.Mclip - z * g.Mstep);
+  const int64_t N = imin64(g.N, g.Nclip - z * g.Nstep);
+  const int64_t K = imin64(g.K, g.Kclip - z * g.Kstep);
+  const int64_t m0 = (int64_t)blockIdx.y * kBM, n0 = (int64_t)blockIdx.x * kBN;
+  if (m0 >= M || n0 >= N) return;
+  if (kLower && n0 > m0 + kGT) return;  // both 64-row halves lie above the block diagonal
+  const double* __restrict__ A = g.A + z * g.sa;
+  const double* __restrict__ B = g.B + z * g.sb;
+  double* __restrict__ C = g.C + z * g.sc;
+
+  extern __shared__ __align__(16) double sm2[];
+  constexpr int AC = v2_a_cols<kTA>(), AS = v2_a_size<kTA>();
+  constexpr int BC = v2_b_cols<kTB>(), BS = v2_b_size<kTB>();
+  double* As = sm2;
+  double* Bs = sm2 + kStages * AS;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+  const int64_t arows = kTA ? K : M, acols = kTA ? M : K;
+  const int64_t brows = kTB ? N : K, bcols = kTB ? K : N;
+
+  auto issue = [&](int stage, int64_t k0) {
+    double* as = As + stage * AS;
+    double* bs = Bs + stage * BS;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // A: 1024 chunks of the 128 x 16 (or 16 x 128) tile
+      const int id = tid + q * kV2Threads;
+      const int r = kTA ? id >> 6 : id >> 3, c = kTA ? (id & 63) * 2 : (id & 7) * 2;
+      const int64_t gr = kTA ? k0 + r : m0 + r, gc = kTA ? m0 + c : k0 + c;
+      const int nd = chunk_doubles<kTriA>(gr, gc, arows, acols);
+      cp_async16(as + r * AC + c, nd ? A + gr * g.lda + gc : A, nd * 8);
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {  // B: 512 chunks of the 16 x 64 (or 64 x 16) tile
+      const int id = tid + q * kV2Threads;
+      const int r = kTB ? id >> 3 : id >> 5, c = kTB ? (id & 7) * 2 : (id & 31) * 2;
+      const int64_t gr = kTB ? n0 + r : k0 + r, gc = kTB ? k0 + c : n0 + c;
+      const int nd = chunk_doubles<kTriB>(gr, gc, brows, bcols);
+      cp_async16(bs + r * BC + c, nd ? B + gr * g.ldb + gc : B, nd * 8);
+    }
+  };
+
+  double acc[2][4][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[i][j][r] = 0.0;
+
+  const int64_t KT = (K + kBK - 1) / kBK;
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < KT) issue(s, (int64_t)s * kBK);
+    cp_async_commit();
+  }
+  for (int64_t kt = 0; kt < KT; ++kt) {
+    cp_async_wait<kStages - 2>();  // this thread's copies of stage kt have landed
+    __syncthreads();               // everyone's have; stage kt - 1 is no longer read
+    const int64_t nk = kt + kStages - 1;
+    if (nk < KT) issue((int)(nk % kStages), nk * kBK);
+    cp_async_commit();
+    const double* as = As + (kt % kStages) * AS;
+    const double* bs = Bs + (kt % kStages) * BS;
+#pragma unroll
+    for (int kk = 0; kk < kBK; kk += 4) {
+      double a0[2], a1[2], b[4];
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi) {
+        const int m = wm + mi * 16 + gq;
+        a0[mi] = kTA ? as[(kk + tq) * AC + m] : as[m * AC + kk + tq];
+        a1[mi] = kTA ? as[(kk + tq) * AC + m + 8] : as[(m + 8) * AC + kk + tq];
+      }
+#pragma unroll
+      for (int ni = 0; ni < 4; ++ni) {
+        const int n = wn + ni * 8 + gq;
+        b[ni] = kTB ? bs[n * BC + kk + tq] : bs[(kk + tq) * BC + n];
+      }
+#pragma unroll
+      for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+        for (int ni = 0; ni < 4; ++ni) dmma_m16n8k4(acc[mi][ni], a0[mi], a1[mi], b[ni]);
+    }
+  }
+  cp_async_wait<0>();
+
+#pragma unroll
+  for (int mi = 0; mi < 2; ++mi)
+#pragma unroll
+    for (int ni = 0; ni < 4; ++ni)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int64_t row = m0 + wm + mi * 16 + gq + (r >> 1) * 8;
+        const int64_t col = n0 + wn + ni * 8 + 2 * tq + (r & 1);
+        // kLower: the 64 x 64 blocks on or below the block diagonal, as the 64-tile kernel writes
+        if (row < M && col < N && !(kLower && n0 > (row / kGT) * kGT)) {
+          double* p = C + row * g.ldc + col;
+          const double v = g.alpha * acc[mi][ni][r];
+          *p = g.beta == 0.0 ? v : fma(g.beta, *p, v);
+        }
+      }
+}
+
+// Host launcher: picks the instantiation; grid (N tiles, M tiles, batch). Large products whose
+// operands are 16-byte aligned (bases, leading dimensions and batch strides even) take the
+// pipelined kernel.
 template <bool kTA, bool kTB, bool kTriA, bool kTriB, bool kLower>
 static int gemm_launch(const GemmArgs& g, int64_t batch, cudaStream_t st) {
   if (g.M <= 0 || g.N <= 0 || batch <= 0) return GSDFT_OK;
+  const bool aligned = (reinterpret_cast<uintptr_t>(g.A) & 15) == 0 &&
+                       (reinterpret_cast<uintptr_t>(g.B) & 15) == 0 && g.lda % 2 == 0 &&
+                       g.ldb % 2 == 0 && g.sa % 2 == 0 && g.sb % 2 == 0;
+  if (GSDFT_GEMM_V2 && aligned && g.M >= kBM && g.N >= kBN && g.K >= kBK) {
+    constexpr size_t smem = v2_smem<kTA, kTB>();
+    static const bool attr = [] {
+      return cudaFuncSetAttribute(dmma_gemm_v2_kernel<kTA, kTB, kTriA, kTriB, kLower>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)smem) == cudaSuccess;
+    }();
+    GSDFT_REQUIRE(attr, "gemm: shared-memory attribute refused");
+    dim3 grid((unsigned)((g.N + kBN - 1) / kBN), (unsigned)((g.M + kBM - 1) / kBM),
+              (unsigned)batch);
+    GSDFT_REQUIRE(grid.y <= 65535 && grid.z <= 65535, "gemm grid too large");
+    dmma_gemm_v2_kernel<kTA, kTB, kTriA, kTriB, kLower><<<grid, kV2Threads, smem, st>>>(g);
+    GSDFT_LAUNCHED("dmma_gemm");
+    return GSDFT_OK;
+  }
   dim3 grid((unsigned)((g.N + kGT - 1) / kGT), (unsigned)((g.M + kGT - 1) / kGT),
             (unsigned)batch);
   GSDFT_REQUIRE(grid.y <= 65535 && grid.z <= 65535, "gemm grid too large");

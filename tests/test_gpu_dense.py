@@ -49,6 +49,37 @@ def test_gemm_matches_host(g, ta, tb, M, N, K):
     assert got.shape == (M, N)
 
 
+@pytest.mark.parametrize("ta", [0, 1])
+@pytest.mark.parametrize("tb", [0, 1])
+@pytest.mark.parametrize("M,N,K,pad", [(258, 130, 38, 0), (300, 200, 150, 0), (512, 64, 1000, 0),
+                                       (384, 192, 77, 1)])
+def test_pipelined_gemm_matches_host(g, ta, tb, M, N, K, pad):
+    """Sizes that take the pipelined kernel (M >= 128, N >= 64, even leading dimensions): ragged
+    last tiles in M, N and K, and an odd K stored with a padded (even) leading dimension, whose
+    last 16-byte chunk per row holds one element of the operand."""
+    from gs_dft_b200._lib import lib, ptr, stream_handle
+    rng = np.random.default_rng(M + 3 * N + 7 * K + 11 * ta + 13 * tb)
+    A = rng.standard_normal((K, M) if ta else (M, K))
+    B = rng.standard_normal((N, K) if tb else (K, N))
+    C0 = rng.standard_normal((M, N))
+    want = 0.75 * (A.T if ta else A) @ (B.T if tb else B) - 0.5 * C0
+
+    def padded(X):
+        # pad columns with NaN (never read) up to an even leading dimension, at least one column
+        extra = (1 if X.shape[1] % 2 else 2) if pad else 0
+        P = np.full((X.shape[0], X.shape[1] + extra), np.nan)
+        P[:, :X.shape[1]] = X
+        return P
+    Ap, Bp = padded(A), padded(B)
+    assert Ap.shape[1] % 2 == 0 and Bp.shape[1] % 2 == 0
+    dA, dB, dC = dev(Ap), dev(Bp), dev(C0)
+    lib.call("gsdft_dense_gemm", ta, tb, M, N, K, 0.75, ptr(dA), Ap.shape[1], ptr(dB), Bp.shape[1],
+             -0.5, ptr(dC), N, stream_handle(dC.device))
+    got = host(dC)
+    tol = 1e-15 * K * np.abs(A).max() * np.abs(B).max() + 1e-14
+    np.testing.assert_allclose(got, want, rtol=0, atol=tol)
+
+
 def _spd(n, seed, cond=1e4):
     rng = np.random.default_rng(seed)
     Q, _ = np.linalg.qr(rng.standard_normal((n, n)))
