@@ -70,3 +70,37 @@ def test_partition_bounds_balance_cost():
         assert b[0] == 0 and b[-1] == 1000 and all(x <= y for x, y in zip(b, b[1:]))
         sums = [int(cost[b[k]:b[k + 1]].sum()) for k in range(world)]
         assert max(sums) - min(sums) <= 2 * int(cost.max())
+
+
+def test_row_blocks_structure():
+    """The row-block structure of the many-orbital q / g_C tiles (host logic, on CPU tensors):
+    every representative gets its own cell inside its row block's tile, at its row (the splat's
+    place in its block of 64) and its partner's column; each block's partner list is sorted and
+    holds exactly the partners of its rows; tile offsets are the exclusive sums of rows x partners;
+    blocks without representatives are empty."""
+    import numpy as np
+    from gs_dft_b200.coulomb.engine import row_blocks
+    rng = np.random.default_rng(4)
+    M = 200                                   # blocks of 64, 64, 64, 8 rows; block 1 left empty
+    live = np.r_[np.arange(0, 64), np.arange(128, M)]
+    pairs = sorted({(int(rng.choice(live)), int(rng.choice(M))) for _ in range(1500)})
+    rows = torch.tensor([p[0] for p in pairs], dtype=torch.int32)
+    partners = torch.tensor([p[1] for p in pairs], dtype=torch.int32)
+    bl = row_blocks(rows, partners, M)
+    assert bl.n_blocks == 4
+    nj, joff, boff = bl.nj.numpy(), bl.joff.numpy(), bl.boff.numpy()
+    jidx, cell = bl.jidx.numpy(), bl.cell.numpy()
+    rows_b = np.minimum(64, M - 64 * np.arange(4))
+    np.testing.assert_array_equal(boff, np.r_[0, np.cumsum(rows_b * nj)[:-1]])
+    assert bl.buf_len == int((rows_b * nj).sum()) and bl.max_nj == int(nj.max()) and nj[1] == 0
+    r, p = rows.numpy().astype(np.int64), partners.numpy().astype(np.int64)
+    for b in range(4):
+        J = jidx[joff[b]:joff[b] + nj[b]]
+        assert np.all(np.diff(J) > 0)
+        np.testing.assert_array_equal(J, np.unique(p[r // 64 == b]))
+    b = r // 64
+    col = np.array([np.searchsorted(jidx[joff[k]:joff[k] + nj[k]], q) for k, q in zip(b, p)])
+    np.testing.assert_array_equal(cell, boff[b] + (r - 64 * b) * nj[b] + col)
+    assert len(np.unique(cell)) == len(cell) and cell.max() < bl.buf_len
+    empty = row_blocks(rows[:0], partners[:0], M)
+    assert empty.buf_len == 0 and empty.max_nj == 0
