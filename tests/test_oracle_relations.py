@@ -116,3 +116,95 @@ def test_exact_coulomb_gradient_is_the_derivative_of_the_block_energy(block):
     for k, name in enumerate(["g_quat", "g_log_scale", "g_centers", "g_C"]):
         ref = (4 * fd(k, 5e-4) - fd(k, 1e-3)) / 3
         np.testing.assert_allclose(res[name], ref, rtol=0, atol=1e-9 * np.abs(ref).max())
+
+
+def _df_problem(seed=11, M=14, n_occ=3):
+    from gs_dft_b200.systems import small_random_system
+    s = small_random_system(M, n_occ, seed=seed, spread=1.2)
+    arr = (s.quat, s.log_scale, s.centers, s.C_occ, s.occ)
+    return s, arr
+
+
+def _df_energy_and_grad(arr, pi, pj, w, lam):
+    q = O.full_quantities(*arr[:3])
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    L = O.aux_cholesky(O.aux_metric(*aq), lam)
+    return O.energy_and_grad(arr, aq, L, pi, pj, w)
+
+
+def test_unique_weighted_list_equals_ordered_list():
+    """The unique list (j >= i, weights 2 - delta_ij) gives the ordered list's E_J and gradients:
+    the reference's unique-mode identity (tests/unit/test_pair_tricks.py:81-100, rtol 1e-10)."""
+    s, arr = _df_problem()
+    q = O.full_quantities(*arr[:3])
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=1e-7)
+    ui, uj, uw, _ = O.neighbor_pairs(q, eps=1e-7, unique=True)
+    a = _df_energy_and_grad(arr, pi, pj, np.asarray(v, np.float64), s.lam)
+    b = _df_energy_and_grad(arr, ui, uj, np.asarray(uw, np.float64), s.lam)
+    np.testing.assert_allclose(b["E"], a["E"], rtol=1e-10)
+    for k in ("gamma", "g_quat", "g_log_scale", "g_centers", "g_C"):
+        np.testing.assert_allclose(b[k], a[k], rtol=1e-10, atol=1e-12 * np.abs(a[k]).max())
+
+
+def test_full_ordered_list_equals_dense_density_fit():
+    """With eps < 0 (every ordered pair) the screened gamma and E_J equal the dense density fit
+    gamma_P = sum_ij P_ij (P|ij) with the dense density P = C diag(occ) C^T (the reference's
+    tests/unit/test_coulomb_df.py:107-126, rtol 1e-9)."""
+    s, arr = _df_problem(seed=12, M=10)
+    quat, log_scale, centers, C, occ = arr
+    q = O.full_quantities(quat, log_scale, centers)
+    pi, pj, v, _ = O.neighbor_pairs(q, eps=-1.0)
+    assert pi.size == s.M * s.M
+    la, R = O.init_product_aux(q)
+    aq = O.aux_quantities(la, R)
+    L = O.aux_cholesky(O.aux_metric(*aq), s.lam)
+    E, gamma, _ = O.energy(arr, aq, L, pi, pj, np.ones(pi.size))
+    P = (C * occ[None, :]) @ C.T
+    ii, jj = np.meshgrid(np.arange(s.M), np.arange(s.M), indexing="ij")
+    blk = O.full_isobra_block(*aq, *O.full_pair_quantities(q, ii.ravel(), jj.ravel()))
+    gamma_dense = blk @ P.ravel()
+    np.testing.assert_allclose(gamma, gamma_dense, rtol=1e-12, atol=1e-14 * np.abs(gamma).max())
+    E_dense, _ = O.df_coulomb_solve(gamma_dense, L)
+    np.testing.assert_allclose(E, E_dense, rtol=1e-9)
+
+
+def _quat_mul(a, b):
+    w1, x1, y1, z1 = a[..., 0], a[..., 1], a[..., 2], a[..., 3]
+    w2, x2, y2, z2 = b[..., 0], b[..., 1], b[..., 2], b[..., 3]
+    return np.stack([w1 * w2 - x1 * x2 - y1 * y2 - z1 * z2,
+                     w1 * x2 + x1 * w2 + y1 * z2 - z1 * y2,
+                     w1 * y2 - x1 * z2 + y1 * w2 + z1 * x2,
+                     w1 * z2 + x1 * y2 - y1 * x2 + z1 * w2], -1)
+
+
+def test_rotation_invariance_and_gradient_equivariance():
+    """A global rotation Q of every splat (centres Q mu, orientations Q R(q)) leaves E_J unchanged
+    and rotates the centre gradient (g -> Q g), the log-scale gradient staying put: the chart's
+    equivariance that the reference checks (tests/unit/test_splat_chart.py:19-52), through the whole
+    DF energy and its analytic gradient."""
+    s, arr = _df_problem(seed=13)
+    quat, log_scale, centers, C, occ = arr
+    qQ = np.array([0.8, -0.3, 0.4, 0.2])
+    qQ = qQ / np.linalg.norm(qQ)
+    Q = O.quat_to_rotation(qQ[None])[0]
+    quat_n = quat / np.linalg.norm(quat, axis=-1, keepdims=True)
+    rot = (_quat_mul(np.broadcast_to(qQ, quat_n.shape), quat_n), log_scale, centers @ Q.T, C, occ)
+    np.testing.assert_allclose(O.quat_to_rotation(rot[0]), Q @ O.quat_to_rotation(quat_n),
+                               atol=1e-14)
+
+    def run(a):
+        qq = O.full_quantities(*a[:3])
+        pi, pj, v, _ = O.neighbor_pairs(qq, eps=1e-7)
+        return pi, pj, _df_energy_and_grad(a, pi, pj, np.asarray(v, np.float64), s.lam)
+
+    pi0, pj0, r0 = run(arr)
+    pi1, pj1, r1 = run(rot)
+    np.testing.assert_array_equal(pi0, pi1)
+    np.testing.assert_array_equal(pj0, pj1)
+    np.testing.assert_allclose(r1["E"], r0["E"], rtol=1e-11)
+    np.testing.assert_allclose(r1["g_centers"], r0["g_centers"] @ Q.T, rtol=1e-9,
+                               atol=1e-11 * np.abs(r0["g_centers"]).max())
+    np.testing.assert_allclose(r1["g_log_scale"], r0["g_log_scale"], rtol=1e-9,
+                               atol=1e-11 * np.abs(r0["g_log_scale"]).max())
+    np.testing.assert_allclose(r1["g_C"], r0["g_C"], rtol=1e-9, atol=1e-11 * np.abs(r0["g_C"]).max())
